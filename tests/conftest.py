@@ -1,0 +1,21 @@
+import os
+import sys
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a CUDA device (B200, sm_100a)")
+
+
+@pytest.fixture(scope="session")
+def tiny_runtime(tmp_path_factory):
+    """The small seeded model in the reference's runtime layout."""
+    from kernel_optimization_webgpu_b200 import synth
+    d = str(tmp_path_factory.mktemp("tiny_runtime"))
+    synth.write_runtime(d, synth.TINY, seed=2)
+    return d
