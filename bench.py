@@ -1,0 +1,401 @@
+"""Benchmark: batch-1 greedy decode of the Qwen3-0.6B-shaped q4 stack on B200.
+
+One step = one generated token: all 28 layers at the current position plus the
+f16 LM head and argmax (one CUDA-graph launch), positions cycling over the
+8-token-prompt + 24-token decode of the batch-1 workload (positions 7..30, the
+same token flow every cycle). Weights are seeded synthetic (seed 2) in the
+reference's runtime layout.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N > 1 (torchrun): N independent replicas, one per GPU (batch-1 decode does not
+shard); value = total tokens over all ranks / max over ranks of the device time.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+import numpy as np  # noqa: E402
+
+from kernel_optimization_webgpu_b200 import synth  # noqa: E402
+
+PROMPT_LEN, NEW_TOKENS = 8, 24
+WORKLOAD = ("batch-1 greedy decode, Qwen3-0.6B shape (28 layers, hidden 1024, 16q/8kv heads x 128, "
+            "SwiGLU 3072, q4 MatMulNBits block 32 with f16 scales, tied f16 LM head 151936x1024, f16 KV), "
+            "8-token prompt + 24 generated, seed 2")
+METRIC, UNIT = "decode tok/s", "tok/s"
+
+
+def prompt_ids():
+    rng = np.random.Generator(np.random.PCG64(2))
+    return rng.integers(0, synth.QWEN3_0_6B.vocab, size=PROMPT_LEN).tolist()
+
+
+def runtime_dir() -> str:
+    return os.environ.get("QDECODE_BENCH_RUNTIME", "/tmp/qdecode_runtime_qwen3_seed2")
+
+
+def token_bytes(shape: synth.Shape, position: int, kv_bytes: int = 2) -> int:
+    """Algorithmic HBM bytes of one batch-1 token at `position` (weights read once,
+    KV rows 0..position read, one KV row written, logits written, id read back)."""
+    H, I = shape.hidden, shape.intermediate
+    QS, KV = shape.heads * shape.head_dim, shape.kv_heads * shape.head_dim
+    params = H * (QS + 2 * KV) + QS * H + 2 * H * I + I * H           # q4 weights per layer
+    per_layer = params // 2 + (params // 32) * 2 + (2 * H + 2 * shape.head_dim) * 2
+    kv_row = 2 * KV * kv_bytes                                          # K and V, one position
+    return (shape.layers * per_layer + H * 2 + shape.vocab * H * 2 + H * 2
+            + shape.layers * kv_row * (position + 1) + shape.layers * kv_row + shape.vocab * 4)
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index, self.rows, self.proc = index, [], None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                self.rows.append(parts)
+
+    def __exit__(self, *exc):
+        if self.proc:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        dist.init_process_group("nccl" if _cuda() else "gloo", timeout=datetime.timedelta(seconds=120),
+                                device_id=None)
+    return world, rank, local
+
+
+def _cuda():
+    import torch
+    return torch.cuda.is_available()
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda" if _cuda() else "cpu")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def prepare_runtime(world: int, rank: int) -> str:
+    d = runtime_dir()
+    if rank == 0:
+        synth.ensure_runtime(d, synth.QWEN3_0_6B, seed=2)
+    barrier(world)
+    return d
+
+
+# ---- CPU oracle timing (reference arm and the cpu_baseline object) -----------------
+
+def time_cpu_decode(rt: str, steps: int, warmup: int):
+    """Oracle decode tokens per second on the host cores: prefill once, then
+    `warmup` + `steps` decode steps cycling over positions 7..30."""
+    from oracle import oracle as O
+    model = O.Model(rt)
+    sess = model.session(max_seq=64, kv_f16=True)
+    ids = prompt_ids()
+    for i, t in enumerate(ids[:-1]):
+        sess.forward(t, i)
+    tok, pos, done, t_total = ids[-1], PROMPT_LEN - 1, 0, 0.0
+    for i in range(warmup + steps):
+        t0 = time.perf_counter()
+        sess.forward(tok, pos)
+        tok, _, _ = sess.next_token()
+        dt = time.perf_counter() - t0
+        if i >= warmup:
+            t_total += dt
+            done += 1
+        pos += 1
+        if pos == PROMPT_LEN - 1 + NEW_TOKENS:
+            pos, tok = PROMPT_LEN - 1, ids[-1]
+    return done / t_total, O.lib().qo_num_threads(), done
+
+
+def run_reference(args, world, rank):
+    """The reference's CPU path: its WGSL math restated in C (oracle), all host threads."""
+    if rank != 0:
+        return 0
+    rt = runtime_dir()
+    synth.ensure_runtime(rt, synth.QWEN3_0_6B, seed=2)
+    steps = max(1, min(args.steps, 48))
+    tps, cores, n = time_cpu_decode(rt, steps, max(1, min(args.warmup, 4)))
+    sample = f"{n} decode tokens of the batch-1 workload (positions 7..30, after an 8-token prefill)"
+    line = {"metric": METRIC, "value": round(tps, 4), "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
+            "steps": n, "warmup": max(1, min(args.warmup, 4)), "ms_per_step": round(1000.0 / tps, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded random-init weights, reference runtime layout)",
+            "config": {"workload": WORKLOAD, "parallelism": "host cores (OpenMP)"},
+            "cpu_baseline": {"value": round(tps, 4), "unit": UNIT, "cores": cores, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": round(tps, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "note": "the reference runs only through WebGPU (no graphics stack here: unavailable on this box); "
+                    "this arm times its WGSL math restated in C on the host cores"}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---- GPU arm --------------------------------------------------------------------------
+
+def kernel_rooflines(torch, R, peak):
+    """q4 matvec (gate 1024->3072, 128 distinct weight copies, 228 MB > L2) and the LM head
+    (311 MB table per launch), each launched back to back inside one CUDA graph."""
+    out = {}
+    stream = torch.cuda.Stream()
+    # q4 matvec, gate shape
+    x, w, s = synth.matvec_case(3072, 1024, seed=0)
+    copies = 128
+    xs = torch.from_numpy(x).cuda()
+    wd = torch.from_numpy(w.view(np.int32)).cuda()
+    sd = torch.from_numpy(s.astype(np.float16)).cuda()
+    wcs = [wd.clone() for _ in range(copies)]
+    scs = [sd.clone() for _ in range(copies)]
+    ys = torch.empty(copies, 3072, device="cuda")
+    per = 4 * 1024 + 3072 * 1024 // 2 + 3072 * 32 * 2 + 3072 * 4
+    with torch.cuda.stream(stream):
+        for i in range(copies):
+            R.q4_matvec(xs, wcs[i], scs[i], ys[i], stream=stream)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        for i in range(copies):
+            R.q4_matvec(xs, wcs[i], scs[i], ys[i], stream=stream)
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 20
+    e0.record(stream)
+    for _ in range(reps):
+        g.replay()
+    e1.record(stream)
+    e1.synchronize()
+    t = e0.elapsed_time(e1) / 1000.0 / (reps * copies)
+    out["q4_matvec_gate_1024x3072"] = {"us_per_launch": round(t * 1e6, 3), "bytes": per,
+                                       "achieved_gbs": round(per / t / 1e9, 1),
+                                       "frac": round(per / t / 1e9 / peak, 4)}
+    del g, wcs, scs
+    # LM head + argmax
+    table, xh, eps = synth.lm_head_case()
+    tb = torch.from_numpy(table.view(np.uint16)).cuda().view(torch.float16)
+    xd = torch.from_numpy(xh).cuda()
+    nw = torch.ones(1024, device="cuda")
+    logits = torch.empty(151936, device="cuda")
+    ws = R.LmHeadWorkspace(151936, "cuda")
+    res = torch.zeros(2, dtype=torch.int32, device="cuda")
+    per = 151936 * 1024 * 2 + 1024 * 4 * 2 + 151936 * 4 + 8
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            R.lm_head_argmax(xd, tb, nw, eps, logits, ws, res, stream=stream)
+        e0.record(stream)
+        n = 30
+        for _ in range(n):
+            R.lm_head_argmax(xd, tb, nw, eps, logits, ws, res, stream=stream)
+        e1.record(stream)
+    e1.synchronize()
+    t = e0.elapsed_time(e1) / 1000.0 / n
+    out["lm_head_argmax_151936x1024"] = {"us_per_launch": round(t * 1e6, 3), "bytes": per,
+                                         "achieved_gbs": round(per / t / 1e9, 1),
+                                         "frac": round(per / t / 1e9 / peak, 4)}
+    return out
+
+
+def run_ours(args, world, rank, local):
+    import torch
+
+    from kernel_optimization_webgpu_b200 import runtime as R
+    torch.cuda.set_device(local)
+    rt = prepare_runtime(world, rank)
+    peak, peak_kind = peaks()
+    ids = prompt_ids()
+    eng = R.Engine(rt, device=local, max_seq=64)
+    step_kernels = eng.step_kernels
+    stream = torch.cuda.Stream()
+    eng.set_stream(stream)
+    shape = synth.QWEN3_0_6B
+    cycle = NEW_TOKENS  # positions 7..30
+
+    # warm-up (untimed): a full prompt + decode cycle at least
+    eng.decode_begin(ids, NEW_TOKENS)
+    pos_in_cycle, seeks = 0, 0
+    for _ in range(max(args.warmup, 3)):
+        if pos_in_cycle == cycle:
+            eng.decode_seek(PROMPT_LEN - 1)
+            pos_in_cycle = 0
+        eng.decode_step()
+        pos_in_cycle += 1
+    eng.decode_sync(0)
+
+    # timed: exactly K steps
+    positions = []
+    barrier(world)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        e0.record(stream)
+        for _ in range(args.steps):
+            if pos_in_cycle == cycle:
+                eng.decode_seek(PROMPT_LEN - 1)
+                pos_in_cycle = 0
+                seeks += 1
+            positions.append(PROMPT_LEN - 1 + pos_in_cycle)
+            eng.decode_step()
+            pos_in_cycle += 1
+        e1.record(stream)
+        e1.synchronize()
+    torch.cuda.synchronize()
+    barrier(world)
+    eng.decode_sync(0)
+    t_local = e0.elapsed_time(e1) / 1000.0
+    t_max = max_over_ranks(t_local, world)
+    value = world * args.steps / t_max
+    ms_per_step = t_max * 1000.0 / args.steps
+    bytes_avg = sum(token_bytes(shape, p) for p in positions) / len(positions)
+    achieved = bytes_avg / (t_local / args.steps) / 1e9
+
+    # e2e: the public C-ABI call with host buffers (prompt in, generated ids out)
+    n_e2e = max(1, args.steps // NEW_TOKENS)
+    eng.generate_greedy(ids, NEW_TOKENS)
+    barrier(world)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    for _ in range(n_e2e):
+        gen, _ = eng.generate_greedy(ids, NEW_TOKENS)
+    f1.record(stream)
+    f1.synchronize()
+    t_e2e = max(f0.elapsed_time(f1) / 1000.0, time.perf_counter() - t0)
+    t_e2e = max_over_ranks(t_e2e, world)
+    e2e = world * n_e2e * NEW_TOKENS / t_e2e
+
+    extra = {}
+    cpu = None
+    if rank == 0 and world == 1:
+        extra = kernel_rooflines(torch, R, peak)
+        if not args.no_cpu:
+            tps, cores, n = time_cpu_decode(rt, args.cpu_steps, 1)
+            cpu = {"value": round(tps, 4), "unit": UNIT, "cores": cores, "kind": "port",
+                   "sample": f"{n} decode tokens of the batch-1 workload (positions 7..30) on the host "
+                             f"cores, WGSL math restated in C (OpenMP)"}
+    eng.close()
+    if rank == 0:
+        clocks = clk.summary()
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": max(args.warmup, 3), "ms_per_step": round(ms_per_step, 5), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded random-init weights, reference runtime layout)",
+            "config": {"workload": WORKLOAD, "global_batch": world, "seq_len": PROMPT_LEN + NEW_TOKENS,
+                       "parallelism": f"replicas x{world} (batch-1 decode does not shard)",
+                       "l2": "inputs larger than L2 (559 MB of weights streamed per token, L2 126 MB)"},
+            "roofline": {"bound": "hbm", "kernel": "decode token (one CUDA graph: 28 layers x 5 kernels + "
+                                                   "LM head/argmax)",
+                         "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "traffic": None,
+                         "bytes_per_step": int(bytes_avg), "peak_source": peak_kind},
+            "e2e": {"value": round(e2e, 2), "unit": UNIT, "h2d_bytes_per_step": PROMPT_LEN * 4,
+                    "d2h_bytes_per_step": NEW_TOKENS * 4,
+                    "step": "one qd_generate_greedy call: 8 prompt ids in, 24 generated ids out (prefill included)"},
+            "gpu_launches": args.steps * step_kernels + seeks,
+            "clocks": clocks,
+            "kernels": extra,
+            "generated_ids_sample": gen[:8],
+        }
+        if cpu:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=480)
+    ap.add_argument("--warmup", type=int, default=24)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--cpu-steps", type=int, default=24)
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    world, rank, local = dist_setup()
+    try:
+        rc = run_reference(args, world, rank) if args.impl == "reference" else run_ours(args, world, rank, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+    return rc
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,137 @@
+/*
+ * qdecode: B200 (sm_100a) decode engine for the Qwen3-0.6B q4 stack of
+ * kernel_optimization_webgpu, behind a plain C ABI.
+ *
+ * Conventions: every call returns 0 (QD_OK) or a negative QD_E_* code and never
+ * throws. qd_last_error() gives the message. An engine is driven by one host
+ * thread at a time; different engines (one per GPU) may run concurrently.
+ * Kernel-level entry points take DEVICE pointers and a cudaStream_t (as void*,
+ * NULL = the legacy default stream) and return after enqueueing.
+ *
+ * Reference interfaces replaced (paths within the reference project):
+ *   qd_engine_create    createWebGpuContext + createAutoregressiveQwenRuntime
+ *                       (src/bench/webgpu-runtime.js:43-60, :223-314), reading the
+ *                       runtime directory written by scripts/extract-qwen-runtime-assets.mjs
+ *   qd_generate_greedy  runCustomQwenGreedyPrompt (src/bench/webgpu-runtime.js:165-214)
+ *   qd_q4_matvec        matmul_nbits_q4.wgsl (src/kernels/matmul_nbits_q4.wgsl:43-92),
+ *                       bound by createQ4RuntimeProjection (webgpu-runtime.js:1191-1207)
+ *   qd_lm_head_argmax   lm_head_f16.wgsl + argmax_stage1/2.wgsl, dispatched by
+ *                       greedyNextTokenResident (webgpu-runtime.js:580-604)
+ *   qd_gqa_decode       gqa_decode.wgsl (src/kernels/gqa_decode.wgsl:17-90) without its
+ *                       256-position cap
+ */
+#ifndef QDECODE_H
+#define QDECODE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define QD_OK 0
+#define QD_E_INVALID (-1)     /* bad argument or shape the kernels do not support */
+#define QD_E_IO (-2)          /* runtime directory: missing, short or malformed file */
+#define QD_E_CUDA (-3)        /* CUDA runtime error (message has the CUDA error string) */
+#define QD_E_NOMEM (-4)       /* device or pinned allocation failed */
+#define QD_E_RANGE (-5)       /* prompt + generation beyond max_seq, token id beyond vocab */
+#define QD_E_DEVICE (-6)      /* a kernel flagged a bad token or position (status word) */
+
+#define QD_KV_F16 0           /* f16 KV cache (default) */
+#define QD_KV_F32 1           /* f32 KV cache, as the reference (cache_write.wgsl) */
+
+typedef struct qd_engine qd_engine;
+
+typedef struct qd_options {
+  int device;            /* CUDA device ordinal */
+  int max_seq;           /* KV capacity in positions (the reference sizes it prompt + new) */
+  int kv_dtype;          /* QD_KV_F16 or QD_KV_F32 */
+  int rope_row_stride;   /* cos/sin offset = position * stride + pair; 0 = head_dim (reference) */
+  const char* variant;   /* "optimized" | "mixed" | "original": accepted, one B200 path */
+  int use_graph;         /* 1 (default): each token is one CUDA graph launch */
+} qd_options;
+
+typedef struct qd_profile {
+  int layers, hidden, intermediate, heads, kv_heads, head_dim, vocab, rope_rows;
+  float eps;
+} qd_profile;
+
+typedef struct qd_stats {
+  double generate_ms;          /* prefill + every decode step (generateMs) */
+  double first_token_ms;       /* firstTokenMs */
+  double steady_ms_per_token;  /* (generate_ms - first_token_ms) / (generated - 1) */
+  int generated_tokens;
+  int prompt_tokens;
+} qd_stats;
+
+/* Called on the calling thread once per generated token, in order
+ * (onToken in runCustomQwenGreedyPrompt). Return non-zero to stop early. */
+typedef int (*qd_token_cb)(int32_t token, void* user);
+
+void qd_options_default(qd_options* opt);
+int qd_engine_create(const char* runtime_dir, const qd_options* opt, qd_engine** out);
+void qd_engine_destroy(qd_engine* e);
+/* Message of the last failed call on this engine; with e == NULL, of the last
+ * failed qd_engine_create or kernel-level call on this thread. */
+const char* qd_last_error(const qd_engine* e);
+int qd_engine_profile(const qd_engine* e, qd_profile* out);
+
+/* Greedy generation: prompt ids at positions 0..n_prompt-1, then max_new_tokens
+ * tokens, each fed back at the next position. out_ids (host) receives the
+ * generated ids. Requires n_prompt >= 1 and n_prompt + max_new_tokens - 1 <= max_seq. */
+int qd_generate_greedy(qd_engine* e, const int32_t* input_ids, int n_prompt, int max_new_tokens,
+                       int32_t* out_ids, qd_token_cb on_token, void* user, qd_stats* stats);
+
+/* Parity and inspection helpers. */
+int qd_engine_logits(qd_engine* e, float* host_logits);       /* logits of the last generated step */
+int qd_engine_hidden(qd_engine* e, float* host_hidden);       /* residual stream after the last layer */
+/* One token through the layers at `position` (no LM head), with the residual
+ * stream after every layer copied to host_trace[layers][hidden]. */
+int qd_engine_forward_trace(qd_engine* e, int32_t token, int position, float* host_trace);
+
+/* Stepping interface (enqueue only; used to time steady-state decode on a
+ * caller's stream). qd_decode_begin copies the prompt, resets the position and
+ * enqueues the prefill of ids[0 .. n_prompt-2]; each qd_decode_step enqueues one
+ * token (layers at the current position + LM head + argmax, token fed back);
+ * qd_decode_seek enqueues a position change (KV rows below it are kept);
+ * qd_decode_sync waits, checks the device status word and copies up to n
+ * generated ids. These replace the per-token loop of runCustomQwenGreedyPrompt
+ * (webgpu-runtime.js:195-205) for callers that drive the loop themselves. */
+int qd_engine_set_stream(qd_engine* e, void* stream);   /* NULL: the engine's own stream */
+int qd_decode_begin(qd_engine* e, const int32_t* input_ids, int n_prompt, int max_new_tokens);
+int qd_decode_step(qd_engine* e);
+int qd_decode_seek(qd_engine* e, int position);
+int qd_decode_sync(qd_engine* e, int32_t* out_ids, int n);
+/* Kernels one qd_decode_step launches (for launch accounting). */
+int qd_decode_step_kernels(const qd_engine* e);
+
+/* ---- kernel level (device pointers) ---------------------------------------- */
+
+/* y[out_size] = dequant(weights) . x. weights: u32 words [out_size][blocks_per_row*block_size/8]
+ * (ONNX MatMulNBits bits=4), scales_f16: [out_size][blocks_per_row], implicit zero point 8.
+ * Only block_size 32 is supported; in_size <= blocks_per_row * 32. */
+int qd_q4_matvec(const float* x, const uint32_t* weights, const uint16_t* scales_f16, float* y,
+                 uint32_t in_size, uint32_t out_size, uint32_t blocks_per_row,
+                 uint32_t block_size, void* stream);
+
+/* Workspace (device, zeroed once by the caller; left zeroed by each call). */
+size_t qd_lm_head_argmax_workspace_bytes(uint32_t vocab);
+/* logits[vocab] = embed_f16 . h where h = rms_norm(hidden) * norm_weight when norm_weight
+ * is non-NULL (eps), else hidden. result[2] = {argmax index (ties: lowest), f32 bits of the
+ * max}. logits may be NULL. hidden_size must be a multiple of 256, at most 1024. */
+int qd_lm_head_argmax(const float* hidden, const float* norm_weight, float eps,
+                      const uint16_t* embed_f16, float* logits, uint32_t* result,
+                      uint32_t hidden_size, uint32_t vocab, void* workspace, void* stream);
+
+/* Decode attention over positions [0, seq_len): q [q_heads][128] f32 (final, after RoPE),
+ * caches [seq][kv_heads][128] of kv_dtype, y [q_heads][128]. head_dim must be 128. */
+size_t qd_gqa_decode_workspace_bytes(uint32_t seq_len, uint32_t q_heads);
+int qd_gqa_decode(const float* q, const void* k_cache, const void* v_cache, int kv_dtype, float* y,
+                  uint32_t seq_len, uint32_t q_heads, uint32_t kv_heads, uint32_t head_dim,
+                  void* workspace, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,911 @@
+// qdecode engine: loads the reference's runtime directory, keeps every weight
+// resident in HBM, captures one token (all layers, plus LM head + argmax) as a
+// CUDA graph and runs the reference's greedy flow (webgpu-runtime.js:165-214).
+#include <chrono>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <fstream>
+#include <sstream>
+#include <string>
+#include <vector>
+
+#include "../../include/qdecode.h"
+#include "json.hpp"
+#include "kernels.cuh"
+
+using namespace qd;
+
+namespace {
+
+thread_local std::string t_last_error;
+
+struct QdError {
+  int code;
+  std::string msg;
+};
+
+#define QD_CK(call)                                                                              \
+  do {                                                                                          \
+    cudaError_t e_ = (call);                                                                    \
+    if (e_ != cudaSuccess) throw QdError{QD_E_CUDA, std::string(#call) + ": " + cudaGetErrorString(e_)}; \
+  } while (0)
+
+template <typename... KArgs, typename... Args>
+void launch(void (*kernel)(KArgs...), dim3 grid, cudaStream_t stream, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  QD_CK(cudaLaunchKernelEx(&cfg, kernel, args...));
+}
+
+int sm_count(int dev) {
+  int n = 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+  return n;
+}
+
+int current_sms() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  return sm_count(dev);
+}
+
+// ---- matvec stage planning and dispatch -------------------------------------
+struct StagePlan {
+  int kc, nr, grid;
+};
+
+// Register budget at 2 CTAs per SM (128 per thread): a lane holds KC * 32
+// activations and KC * NR * NW uint4 of weights plus their scales. Combos over
+// the budget are not instantiated (except the single-row one, which every
+// shape needs); rows beyond one wave of warps go to more CTAs instead.
+constexpr bool stage_ok(int kc, int nr, int nw) {
+  return kc * 32 + kc * nr * nw * 5 < 112 || (nr == 1 && nw == 1);
+}
+
+StagePlan plan_stage(int rows, int nb, int sms, int nw = 1) {
+  if (nb <= 0 || nb > 128) throw QdError{QD_E_INVALID, "q4 matvec: in_size must be 1..4096"};
+  StagePlan p;
+  p.kc = (nb + 31) / 32;
+  const int want = (rows + sms * kWarps - 1) / (sms * kWarps);
+  p.nr = 1;
+  for (int nr : {2, 4, 8})
+    if (p.nr < want && stage_ok(p.kc, nr, nw)) p.nr = nr;
+  p.grid = (rows + kWarps * p.nr - 1) / (kWarps * p.nr);
+  return p;
+}
+
+template <int PRO, int EPI>
+void launch_stage(const StageArgs& a, const StagePlan& p, cudaStream_t s) {
+  constexpr int NW = (EPI == kEpiSilu) ? 2 : 1;
+#define QD_STAGE_CASE(KC, NR)                                               \
+  if constexpr (stage_ok(KC, NR, NW)) {                                     \
+    if (p.kc == KC && p.nr == NR) {                                         \
+      launch(k_stage<KC, NR, PRO, EPI>, dim3(p.grid), s, a);                \
+      return;                                                               \
+    }                                                                       \
+  }
+#define QD_STAGE_KC(KC) QD_STAGE_CASE(KC, 1) QD_STAGE_CASE(KC, 2) QD_STAGE_CASE(KC, 4) QD_STAGE_CASE(KC, 8)
+  QD_STAGE_KC(1) QD_STAGE_KC(2) QD_STAGE_KC(3) QD_STAGE_KC(4)
+#undef QD_STAGE_KC
+#undef QD_STAGE_CASE
+  throw QdError{QD_E_INVALID, "q4 matvec: unsupported shape"};
+}
+
+void launch_lmhead(const LmArgs& a, int grid, cudaStream_t s) {
+  switch (a.H / 256) {
+    case 1: launch(k_lmhead<1>, dim3(grid), s, a); return;
+    case 2: launch(k_lmhead<2>, dim3(grid), s, a); return;
+    case 3: launch(k_lmhead<3>, dim3(grid), s, a); return;
+    case 4: launch(k_lmhead<4>, dim3(grid), s, a); return;
+  }
+  throw QdError{QD_E_INVALID, "LM head: hidden size must be 256, 512, 768 or 1024"};
+}
+
+template <typename KVT>
+void launch_attn_t(const AttnArgs& a, int group, int splits, cudaStream_t s) {
+  const dim3 grid(a.kv_heads, splits);
+  switch (group) {
+    case 1: launch(k_attn<1, KVT>, grid, s, a); return;
+    case 2: launch(k_attn<2, KVT>, grid, s, a); return;
+    case 4: launch(k_attn<4, KVT>, grid, s, a); return;
+    case 8: launch(k_attn<8, KVT>, grid, s, a); return;
+  }
+  throw QdError{QD_E_INVALID, "attention: q_heads / kv_heads must be 1, 2, 4 or 8"};
+}
+
+void launch_attn(const AttnArgs& a, int kv_dtype, int splits, cudaStream_t s) {
+  const int group = a.q_heads / a.kv_heads;
+  if (kv_dtype == QD_KV_F32) launch_attn_t<float>(a, group, splits, s);
+  else launch_attn_t<__half>(a, group, splits, s);
+}
+
+// ---- files ----------------------------------------------------------------
+std::vector<char> read_file(const std::string& path, size_t expect) {
+  std::ifstream f(path, std::ios::binary | std::ios::ate);
+  if (!f) throw QdError{QD_E_IO, "cannot open " + path};
+  const size_t n = (size_t)f.tellg();
+  if (expect && n != expect)
+    throw QdError{QD_E_IO, path + ": expected " + std::to_string(expect) + " bytes, found " + std::to_string(n)};
+  std::vector<char> buf(n);
+  f.seekg(0);
+  if (n && !f.read(buf.data(), (std::streamsize)n)) throw QdError{QD_E_IO, "cannot read " + path};
+  return buf;
+}
+
+float h2f(uint16_t h) {
+  __half_raw r;
+  r.x = h;
+  return __half2float(__half(r));
+}
+
+uint16_t f2h(float f) {
+  const __half h = __float2half_rn(f);
+  return __half_raw(h).x;
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+struct LayerDev {
+  const uint4 *w_qkv, *w_o, *w_gu, *w_d;
+  const __half *s_qkv, *s_o, *s_gu, *s_d;
+  const float *n_in, *n_q, *n_k, *n_post;
+  void *kc, *vc;
+};
+
+struct qd_engine {
+  std::string err;
+  int dev = 0, sms = 148;
+  cudaStream_t stream = nullptr;      // the stream work is enqueued on
+  cudaStream_t own_stream = nullptr;  // created with the engine
+  int stepping_max_new = 0;
+  qd_profile p{};
+  qd_options opt{};
+  std::string variant;
+  int splits = 1, rows_qkv = 0, lm_grid = 0;
+  void* blob = nullptr;
+  void* kv = nullptr;
+  void* scratch = nullptr;
+  __half* embed = nullptr;
+  float *cos_t = nullptr, *sin_t = nullptr, *final_norm = nullptr;
+  std::vector<LayerDev> layers;
+  float *h = nullptr, *h_attn = nullptr, *qkv = nullptr, *act = nullptr, *logits = nullptr, *part_o = nullptr;
+  float2* part_ml = nullptr;
+  DevState* st = nullptr;
+  int *tokens = nullptr, *out_dev = nullptr;
+  int* out_host = nullptr;  // mapped pinned: the kernel writes each token here
+  int* out_host_dev = nullptr;
+  uint32_t* result = nullptr;
+  float* lm_pv = nullptr;
+  uint32_t* lm_pi = nullptr;
+  unsigned* lm_counter = nullptr;
+  int32_t* pinned_ids = nullptr;
+  DevState* pinned_state = nullptr;
+  cudaGraphExec_t g_layers = nullptr, g_full = nullptr;
+  cudaEvent_t ev[2] = {nullptr, nullptr};
+};
+
+namespace {
+
+struct Arena {
+  size_t off = 0;
+  size_t take(size_t bytes) {
+    const size_t o = off;
+    off += (bytes + 255) & ~size_t(255);
+    return o;
+  }
+};
+
+void enqueue_layer(qd_engine* e, int l, cudaStream_t s) {
+  const qd_profile& p = e->p;
+  const LayerDev& L = e->layers[l];
+  const int qsize = p.heads * kHeadDim, kvsize = p.kv_heads * kHeadDim;
+  // 1. RMSNorm + fused QKV projection (layer 0 gathers the embedding row on device).
+  {
+    StageArgs a{};
+    a.w = L.w_qkv; a.s = L.s_qkv; a.rows = e->rows_qkv; a.nb = p.hidden / kBlockCols; a.k_valid = p.hidden;
+    a.src = e->h; a.norm_w = L.n_in; a.eps = p.eps; a.out = e->qkv;
+    const StagePlan sp = plan_stage(a.rows, a.nb, e->sms);
+    if (l == 0) {
+      a.embed = e->embed; a.tokens = e->tokens; a.st = e->st; a.vocab = p.vocab; a.h_out = e->h;
+      a.max_seq = e->opt.max_seq;
+      launch_stage<kProEmbed, kEpiStore>(a, sp, s);
+    } else {
+      launch_stage<kProRms, kEpiStore>(a, sp, s);
+    }
+  }
+  // 2. Head RMSNorm + RoPE + KV append + split-KV attention.
+  {
+    AttnArgs a{};
+    a.q_in = e->qkv; a.k_in = e->qkv + qsize; a.v_in = e->qkv + qsize + kvsize;
+    a.norm_q = L.n_q; a.norm_k = L.n_k; a.eps = p.eps;
+    a.cos_t = e->cos_t; a.sin_t = e->sin_t; a.row_stride = e->opt.rope_row_stride;
+    a.k_cache = L.kc; a.v_cache = L.vc; a.st = e->st; a.seq_len = 0; a.max_seq = e->opt.max_seq;
+    a.q_heads = p.heads; a.kv_heads = p.kv_heads; a.scale = 1.0f / std::sqrt((float)kHeadDim);
+    a.raw_q = 0; a.part_ml = e->part_ml; a.part_o = e->part_o;
+    launch_attn(a, e->opt.kv_dtype, e->splits, s);
+  }
+  // 3. Split combine + O projection + residual.
+  {
+    StageArgs a{};
+    a.w = L.w_o; a.s = L.s_o; a.rows = p.hidden; a.nb = qsize / kBlockCols; a.k_valid = qsize;
+    a.res = e->h; a.out = e->h_attn;
+    a.part_ml = e->part_ml; a.part_o = e->part_o; a.splits = e->splits; a.q_heads = p.heads;
+    launch_stage<kProCombine, kEpiResidual>(a, plan_stage(a.rows, a.nb, e->sms), s);
+  }
+  // 4. Post-attention RMSNorm + gate/up + silu_mul.
+  {
+    StageArgs a{};
+    a.w = L.w_gu; a.s = L.s_gu; a.rows = p.intermediate; a.nb = p.hidden / kBlockCols; a.k_valid = p.hidden;
+    a.src = e->h_attn; a.norm_w = L.n_post; a.eps = p.eps; a.out = e->act;
+    launch_stage<kProRms, kEpiSilu>(a, plan_stage(a.rows, a.nb, e->sms, 2), s);
+  }
+  // 5. Down projection + residual into the stream state.
+  {
+    StageArgs a{};
+    a.w = L.w_d; a.s = L.s_d; a.rows = p.hidden; a.nb = p.intermediate / kBlockCols; a.k_valid = p.intermediate;
+    a.src = e->act; a.res = e->h_attn; a.out = e->h;
+    launch_stage<kProPlain, kEpiResidual>(a, plan_stage(a.rows, a.nb, e->sms), s);
+  }
+}
+
+void enqueue_lmhead(qd_engine* e, cudaStream_t s) {
+  LmArgs a{};
+  a.h = e->h; a.norm_w = e->final_norm; a.eps = e->p.eps;
+  a.table = reinterpret_cast<const uint4*>(e->embed); a.vocab = e->p.vocab; a.H = e->p.hidden;
+  a.logits = e->logits; a.part_v = e->lm_pv; a.part_i = e->lm_pi; a.counter = e->lm_counter;
+  a.result = e->result; a.st = e->st; a.tokens = e->tokens; a.out_dev = e->out_dev;
+  a.out_host = e->out_host_dev; a.max_seq = e->opt.max_seq;
+  launch_lmhead(a, e->lm_grid, s);
+}
+
+void enqueue_token(qd_engine* e, bool with_head, cudaStream_t s) {
+  for (int l = 0; l < e->p.layers; ++l) enqueue_layer(e, l, s);
+  if (with_head) enqueue_lmhead(e, s);
+  else launch(k_advance, dim3(1), s, e->st);
+}
+
+cudaGraphExec_t capture(qd_engine* e, bool with_head) {
+  cudaGraph_t g = nullptr;
+  QD_CK(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal));
+  try {
+    enqueue_token(e, with_head, e->stream);
+  } catch (...) {
+    cudaStreamEndCapture(e->stream, &g);
+    if (g) cudaGraphDestroy(g);
+    throw;
+  }
+  QD_CK(cudaStreamEndCapture(e->stream, &g));
+  cudaGraphExec_t ex = nullptr;
+  const cudaError_t rc = cudaGraphInstantiate(&ex, g, 0);
+  cudaGraphDestroy(g);
+  QD_CK(rc);
+  return ex;
+}
+
+void run_token(qd_engine* e, bool with_head) {
+  if (e->opt.use_graph) QD_CK(cudaGraphLaunch(with_head ? e->g_full : e->g_layers, e->stream));
+  else enqueue_token(e, with_head, e->stream);
+}
+
+int dims_of(const Json& entry, size_t i) { return (int)entry.at("dims").at(i).as_int(); }
+
+// Host-only half of engine creation: parse and validate the manifest against
+// the shapes the kernels support (no CUDA call, so it is testable without a GPU).
+Json parse_manifest(qd_engine* e, const std::string& dir) {
+  std::string text;
+  {
+    auto buf = read_file(dir + "/manifest.json", 0);
+    text.assign(buf.begin(), buf.end());
+  }
+  Json m;
+  try {
+    m = parse_json(text);
+  } catch (const std::exception& ex) {
+    throw QdError{QD_E_IO, ex.what()};
+  }
+  qd_profile& p = e->p;
+  try {
+    p.hidden = (int)m.at("hiddenSize").as_int();
+    p.intermediate = (int)m.at("intermediateSize").as_int();
+    p.heads = (int)m.at("attentionHeads").as_int();
+    p.kv_heads = (int)m.at("kvHeads").as_int();
+    p.head_dim = (int)m.at("headDim").as_int();
+    p.layers = (int)m.at("layers").size();
+    const Json& emb = m.at("shared").at("embedTokens");
+    p.vocab = dims_of(emb, 0);
+    if (dims_of(emb, 1) != p.hidden) throw QdError{QD_E_IO, "embed_tokens dims do not match hiddenSize"};
+    const Json& cs = m.at("shared").at("cosCache");
+    p.rope_rows = dims_of(cs, 0);
+    if (dims_of(cs, 1) != p.head_dim / 2) throw QdError{QD_E_IO, "cos_cache width must be headDim/2"};
+    const Json* eps = m.find("normEpsilon");
+    p.eps = eps ? (float)eps->as_num() : 1e-6f;  // qwenProfile.normEpsilon (src/model/qwen3-0.6b.js:13)
+  } catch (const std::runtime_error& ex) {
+    throw QdError{QD_E_IO, ex.what()};
+  }
+  if (p.head_dim != kHeadDim) throw QdError{QD_E_INVALID, "head_dim must be 128"};
+  if (p.hidden % 256 || p.hidden > 1024) throw QdError{QD_E_INVALID, "hidden size must be a multiple of 256, at most 1024"};
+  if (p.intermediate % 32 || p.intermediate > 4096) throw QdError{QD_E_INVALID, "intermediate size must be a multiple of 32, at most 4096"};
+  if (p.kv_heads <= 0 || p.heads % p.kv_heads) throw QdError{QD_E_INVALID, "heads must be a multiple of kv_heads"};
+  const int group = p.heads / p.kv_heads;
+  if (group != 1 && group != 2 && group != 4 && group != 8) throw QdError{QD_E_INVALID, "heads / kv_heads must be 1, 2, 4 or 8"};
+  if (p.heads * kHeadDim > 4096) throw QdError{QD_E_INVALID, "heads * head_dim must be at most 4096"};
+  if (p.layers <= 0 || p.vocab <= 0) throw QdError{QD_E_IO, "manifest has no layers or no vocabulary"};
+
+  qd_options& o = e->opt;
+  if (o.rope_row_stride <= 0) o.rope_row_stride = p.head_dim;  // rope.wgsl:27 with headDim
+  if (o.rope_row_stride % 4) throw QdError{QD_E_INVALID, "rope_row_stride must be a multiple of 4"};
+  if (o.max_seq <= 0) throw QdError{QD_E_INVALID, "max_seq must be positive"};
+  const long long last = (long long)(o.max_seq - 1) * o.rope_row_stride + p.head_dim / 2;
+  if (last > (long long)p.rope_rows * (p.head_dim / 2))
+    throw QdError{QD_E_RANGE, "max_seq exceeds the RoPE table (positions * row_stride must stay inside cos_cache)"};
+
+  // Every projection must match the model shape (extract-qwen-runtime-assets.mjs:94-100).
+  static const char* kProjNames[7] = {"q", "k", "v", "o", "gate", "up", "down"};
+  const int QS0 = p.heads * kHeadDim, KV0 = p.kv_heads * kHeadDim;
+  const int out_sz[7] = {QS0, KV0, KV0, p.hidden, p.intermediate, p.intermediate, p.hidden};
+  const int in_sz[7] = {p.hidden, p.hidden, p.hidden, QS0, p.hidden, p.hidden, p.intermediate};
+  try {
+    for (int l = 0; l < p.layers; ++l)
+      for (int j = 0; j < 7; ++j) {
+        const Json& d = m.at("layers").at(l).at("projections").at(kProjNames[j]).at("matmulNBits");
+        const int outS = (int)d.at("outSize").as_int(), inS = (int)d.at("inSize").as_int();
+        const int bpr = (int)d.at("blocksPerRow").as_int(), bs = (int)d.at("blockSize").as_int();
+        if (outS != out_sz[j] || inS != in_sz[j] || bs != kBlockCols || bpr * bs != inS)
+          throw QdError{QD_E_IO, "layer " + std::to_string(l) + " " + kProjNames[j] +
+                                     ": matmulNBits dims do not match the model shape (block size must be 32)"};
+      }
+  } catch (const std::runtime_error& ex) {
+    throw QdError{QD_E_IO, ex.what()};
+  }
+  return m;
+}
+
+void load_engine(qd_engine* e, const std::string& dir, const Json& m) {
+  const qd_profile& p = e->p;
+  const qd_options& o = e->opt;
+  const int H = p.hidden, I = p.intermediate, QS = p.heads * kHeadDim, KV = p.kv_heads * kHeadDim;
+  e->rows_qkv = QS + 2 * KV;
+  const int nb_h = H / kBlockCols, nb_q = QS / kBlockCols, nb_i = I / kBlockCols;
+  const int half = p.head_dim / 2;
+
+  // Offsets in one weight arena.
+  Arena ar;
+  const size_t o_embed = ar.take((size_t)p.vocab * H * 2);
+  const size_t o_cos = ar.take((size_t)p.rope_rows * half * 4);
+  const size_t o_sin = ar.take((size_t)p.rope_rows * half * 4);
+  const size_t o_fn = ar.take((size_t)H * 4);
+  struct LOff { size_t w_qkv, s_qkv, w_o, s_o, w_gu, s_gu, w_d, s_d, n_in, n_q, n_k, n_post; };
+  std::vector<LOff> lo(p.layers);
+  for (int l = 0; l < p.layers; ++l) {
+    lo[l].w_qkv = ar.take((size_t)e->rows_qkv * nb_h * 16);
+    lo[l].s_qkv = ar.take((size_t)e->rows_qkv * nb_h * 2);
+    lo[l].w_o = ar.take((size_t)H * nb_q * 16);
+    lo[l].s_o = ar.take((size_t)H * nb_q * 2);
+    lo[l].w_gu = ar.take((size_t)2 * I * nb_h * 16);
+    lo[l].s_gu = ar.take((size_t)2 * I * nb_h * 2);
+    lo[l].w_d = ar.take((size_t)H * nb_i * 16);
+    lo[l].s_d = ar.take((size_t)H * nb_i * 2);
+    lo[l].n_in = ar.take((size_t)H * 4);
+    lo[l].n_q = ar.take(kHeadDim * 4);
+    lo[l].n_k = ar.take(kHeadDim * 4);
+    lo[l].n_post = ar.take((size_t)H * 4);
+  }
+  if (cudaMalloc(&e->blob, ar.off) != cudaSuccess)
+    throw QdError{QD_E_NOMEM, "cannot allocate " + std::to_string(ar.off) + " bytes of weights"};
+  char* base = static_cast<char*>(e->blob);
+  auto up = [&](size_t off, const void* src, size_t bytes) {
+    QD_CK(cudaMemcpy(base + off, src, bytes, cudaMemcpyHostToDevice));
+  };
+  auto f16_to_f32 = [&](const std::vector<char>& b) {
+    std::vector<float> out(b.size() / 2);
+    const uint16_t* s = reinterpret_cast<const uint16_t*>(b.data());
+    for (size_t i = 0; i < out.size(); ++i) out[i] = h2f(s[i]);
+    return out;
+  };
+  auto file = [&](const Json& entry) { return dir + "/" + entry.at("file").as_str(); };
+
+  try {
+    {
+      auto b = read_file(file(m.at("shared").at("embedTokens")), (size_t)p.vocab * H * 2);
+      up(o_embed, b.data(), b.size());
+    }
+    for (int which = 0; which < 2; ++which) {
+      const Json& entry = m.at("shared").at(which ? "sinCache" : "cosCache");
+      auto v = f16_to_f32(read_file(file(entry), (size_t)p.rope_rows * half * 2));
+      up(which ? o_sin : o_cos, v.data(), v.size() * 4);
+    }
+    {
+      auto v = f16_to_f32(read_file(file(m.at("finalNorm")), (size_t)H * 2));
+      up(o_fn, v.data(), v.size() * 4);
+    }
+    static const char* kProj[7] = {"q", "k", "v", "o", "gate", "up", "down"};
+    for (int l = 0; l < p.layers; ++l) {
+      const Json& le = m.at("layers").at(l);
+      const Json& norms = le.at("norms");
+      auto nv = [&](const char* k, size_t n, size_t off) {
+        auto v = f16_to_f32(read_file(file(norms.at(k)), n * 2));
+        up(off, v.data(), v.size() * 4);
+      };
+      nv("input", H, lo[l].n_in);
+      nv("q", kHeadDim, lo[l].n_q);
+      nv("k", kHeadDim, lo[l].n_k);
+      nv("postAttention", H, lo[l].n_post);
+      // Row offsets of each projection inside the fused device matrices.
+      const int out_sz[7] = {QS, KV, KV, H, I, I, H};
+      const int in_sz[7] = {H, H, H, QS, H, H, I};
+      const size_t w_base[7] = {lo[l].w_qkv, lo[l].w_qkv, lo[l].w_qkv, lo[l].w_o, lo[l].w_gu, lo[l].w_gu, lo[l].w_d};
+      const size_t s_base[7] = {lo[l].s_qkv, lo[l].s_qkv, lo[l].s_qkv, lo[l].s_o, lo[l].s_gu, lo[l].s_gu, lo[l].s_d};
+      const int row0[7] = {0, QS, QS + KV, 0, 0, I, 0};
+      for (int j = 0; j < 7; ++j) {
+        const Json& pj = le.at("projections").at(kProj[j]);
+        const int outS = out_sz[j], bpr = in_sz[j] / kBlockCols;  // validated by parse_manifest
+        auto wb = read_file(file(pj.at("weight")), (size_t)outS * bpr * 16);
+        up(w_base[j] + (size_t)row0[j] * bpr * 16, wb.data(), wb.size());
+        auto sb = read_file(file(pj.at("scales")), (size_t)outS * bpr * 4);
+        const float* sf = reinterpret_cast<const float*>(sb.data());
+        std::vector<uint16_t> sh(sb.size() / 4);
+        for (size_t i = 0; i < sh.size(); ++i) {
+          sh[i] = f2h(sf[i]);
+          const float back = h2f(sh[i]);
+          if (!(back == sf[i]) && !(std::isnan(back) && std::isnan(sf[i])))
+            throw QdError{QD_E_IO, std::string("layer ") + std::to_string(l) + " " + kProj[j] +
+                                       ": a block scale is not an f16 value (the q4f16 format stores f16 scales)"};
+        }
+        up(s_base[j] + (size_t)row0[j] * bpr * 2, sh.data(), sh.size() * 2);
+      }
+    }
+  } catch (const std::runtime_error& ex) {
+    throw QdError{QD_E_IO, ex.what()};
+  }
+
+  e->embed = reinterpret_cast<__half*>(base + o_embed);
+  e->cos_t = reinterpret_cast<float*>(base + o_cos);
+  e->sin_t = reinterpret_cast<float*>(base + o_sin);
+  e->final_norm = reinterpret_cast<float*>(base + o_fn);
+  e->layers.resize(p.layers);
+
+  // KV cache [layer][pos][kv_head][128] for K and V.
+  const size_t kv_elem = o.kv_dtype == QD_KV_F32 ? 4 : 2;
+  const size_t kv_layer = (size_t)o.max_seq * KV * kv_elem;
+  if (cudaMalloc(&e->kv, kv_layer * 2 * p.layers) != cudaSuccess)
+    throw QdError{QD_E_NOMEM, "cannot allocate the KV cache"};
+  QD_CK(cudaMemset(e->kv, 0, kv_layer * 2 * p.layers));
+  for (int l = 0; l < p.layers; ++l) {
+    LayerDev& L = e->layers[l];
+    L.w_qkv = reinterpret_cast<const uint4*>(base + lo[l].w_qkv);
+    L.s_qkv = reinterpret_cast<const __half*>(base + lo[l].s_qkv);
+    L.w_o = reinterpret_cast<const uint4*>(base + lo[l].w_o);
+    L.s_o = reinterpret_cast<const __half*>(base + lo[l].s_o);
+    L.w_gu = reinterpret_cast<const uint4*>(base + lo[l].w_gu);
+    L.s_gu = reinterpret_cast<const __half*>(base + lo[l].s_gu);
+    L.w_d = reinterpret_cast<const uint4*>(base + lo[l].w_d);
+    L.s_d = reinterpret_cast<const __half*>(base + lo[l].s_d);
+    L.n_in = reinterpret_cast<const float*>(base + lo[l].n_in);
+    L.n_q = reinterpret_cast<const float*>(base + lo[l].n_q);
+    L.n_k = reinterpret_cast<const float*>(base + lo[l].n_k);
+    L.n_post = reinterpret_cast<const float*>(base + lo[l].n_post);
+    L.kc = static_cast<char*>(e->kv) + (size_t)(2 * l) * kv_layer;
+    L.vc = static_cast<char*>(e->kv) + (size_t)(2 * l + 1) * kv_layer;
+  }
+
+  // Activations, partials and per-engine state.
+  e->splits = (o.max_seq + kAttnChunk - 1) / kAttnChunk;
+  e->lm_grid = e->sms;
+  Arena sa;
+  const size_t s_h = sa.take(H * 4), s_ha = sa.take(H * 4), s_qkv = sa.take((size_t)e->rows_qkv * 4);
+  const size_t s_act = sa.take((size_t)I * 4), s_log = sa.take((size_t)p.vocab * 4);
+  const size_t s_pml = sa.take((size_t)e->splits * p.heads * 8);
+  const size_t s_po = sa.take((size_t)e->splits * p.heads * kHeadDim * 4);
+  const size_t s_st = sa.take(sizeof(DevState));
+  const size_t s_tok = sa.take((size_t)(o.max_seq + 1) * 4), s_out = sa.take((size_t)(o.max_seq + 1) * 4);
+  const size_t s_res = sa.take(8), s_pv = sa.take((size_t)e->lm_grid * 4), s_pi = sa.take((size_t)e->lm_grid * 4);
+  const size_t s_ctr = sa.take(4);
+  if (cudaMalloc(&e->scratch, sa.off) != cudaSuccess) throw QdError{QD_E_NOMEM, "cannot allocate activations"};
+  QD_CK(cudaMemset(e->scratch, 0, sa.off));
+  char* sb = static_cast<char*>(e->scratch);
+  e->h = reinterpret_cast<float*>(sb + s_h);
+  e->h_attn = reinterpret_cast<float*>(sb + s_ha);
+  e->qkv = reinterpret_cast<float*>(sb + s_qkv);
+  e->act = reinterpret_cast<float*>(sb + s_act);
+  e->logits = reinterpret_cast<float*>(sb + s_log);
+  e->part_ml = reinterpret_cast<float2*>(sb + s_pml);
+  e->part_o = reinterpret_cast<float*>(sb + s_po);
+  e->st = reinterpret_cast<DevState*>(sb + s_st);
+  e->tokens = reinterpret_cast<int*>(sb + s_tok);
+  e->out_dev = reinterpret_cast<int*>(sb + s_out);
+  e->result = reinterpret_cast<uint32_t*>(sb + s_res);
+  e->lm_pv = reinterpret_cast<float*>(sb + s_pv);
+  e->lm_pi = reinterpret_cast<uint32_t*>(sb + s_pi);
+  e->lm_counter = reinterpret_cast<unsigned*>(sb + s_ctr);
+
+  if (cudaHostAlloc(reinterpret_cast<void**>(&e->out_host), (size_t)(o.max_seq + 1) * 4, cudaHostAllocMapped) != cudaSuccess)
+    throw QdError{QD_E_NOMEM, "cannot allocate mapped host memory"};
+  QD_CK(cudaHostGetDevicePointer(reinterpret_cast<void**>(&e->out_host_dev), e->out_host, 0));
+  if (cudaHostAlloc(reinterpret_cast<void**>(&e->pinned_ids), (size_t)(o.max_seq + 1) * 4, cudaHostAllocDefault) != cudaSuccess ||
+      cudaHostAlloc(reinterpret_cast<void**>(&e->pinned_state), sizeof(DevState), cudaHostAllocDefault) != cudaSuccess)
+    throw QdError{QD_E_NOMEM, "cannot allocate pinned host memory"};
+  QD_CK(cudaEventCreateWithFlags(&e->ev[0], cudaEventDisableTiming));
+  QD_CK(cudaEventCreateWithFlags(&e->ev[1], cudaEventDisableTiming));
+  if (o.use_graph) {
+    e->g_layers = capture(e, false);
+    e->g_full = capture(e, true);
+  }
+  QD_CK(cudaStreamSynchronize(e->stream));
+}
+
+void free_engine(qd_engine* e) {
+  if (!e) return;
+  if (!e->own_stream) {  // failed before any CUDA resource was created
+    delete e;
+    return;
+  }
+  cudaSetDevice(e->dev);
+  if (e->stream) cudaStreamSynchronize(e->stream);
+  if (e->g_layers) cudaGraphExecDestroy(e->g_layers);
+  if (e->g_full) cudaGraphExecDestroy(e->g_full);
+  for (auto& ev : e->ev)
+    if (ev) cudaEventDestroy(ev);
+  if (e->blob) cudaFree(e->blob);
+  if (e->kv) cudaFree(e->kv);
+  if (e->scratch) cudaFree(e->scratch);
+  if (e->out_host) cudaFreeHost(e->out_host);
+  if (e->pinned_ids) cudaFreeHost(e->pinned_ids);
+  if (e->pinned_state) cudaFreeHost(e->pinned_state);
+  if (e->stream != e->own_stream) cudaStreamSynchronize(e->stream);
+  cudaStreamDestroy(e->own_stream);
+  delete e;
+}
+
+int fail(qd_engine* e, const QdError& err) {
+  if (e) e->err = err.msg;
+  t_last_error = err.msg;
+  return err.code;
+}
+
+void set_state(qd_engine* e, int pos, int max_new) {
+  e->pinned_state->pos = pos;
+  e->pinned_state->step = 0;
+  e->pinned_state->max_new = max_new;
+  e->pinned_state->err = 0;
+  QD_CK(cudaMemcpyAsync(e->st, e->pinned_state, sizeof(DevState), cudaMemcpyHostToDevice, e->stream));
+}
+
+void check_state(qd_engine* e) {
+  QD_CK(cudaMemcpyAsync(e->pinned_state, e->st, sizeof(DevState), cudaMemcpyDeviceToHost, e->stream));
+  QD_CK(cudaStreamSynchronize(e->stream));
+  const int err = e->pinned_state->err;
+  if (err & kErrToken) throw QdError{QD_E_DEVICE, "device: token id outside the vocabulary"};
+  if (err & kErrPosition) throw QdError{QD_E_DEVICE, "device: position beyond max_seq"};
+}
+
+double ms_since(std::chrono::steady_clock::time_point t0) {
+  return std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+extern "C" {
+
+void qd_options_default(qd_options* opt) {
+  if (!opt) return;
+  opt->device = 0;
+  opt->max_seq = 256;
+  opt->kv_dtype = QD_KV_F16;
+  opt->rope_row_stride = 0;
+  opt->variant = "optimized";
+  opt->use_graph = 1;
+}
+
+int qd_engine_create(const char* runtime_dir, const qd_options* opt, qd_engine** out) {
+  if (!out) return fail(nullptr, QdError{QD_E_INVALID, "out is NULL"});
+  *out = nullptr;
+  if (!runtime_dir) return fail(nullptr, QdError{QD_E_INVALID, "runtime_dir is NULL"});
+  qd_engine* e = new qd_engine();
+  qd_options_default(&e->opt);
+  if (opt) e->opt = *opt;
+  e->variant = e->opt.variant ? e->opt.variant : "optimized";
+  e->opt.variant = nullptr;
+  if (e->opt.kv_dtype != QD_KV_F16 && e->opt.kv_dtype != QD_KV_F32) {
+    delete e;
+    return fail(nullptr, QdError{QD_E_INVALID, "kv_dtype must be QD_KV_F16 or QD_KV_F32"});
+  }
+  try {
+    e->dev = e->opt.device;
+    const Json m = parse_manifest(e, runtime_dir);
+    QD_CK(cudaSetDevice(e->dev));
+    e->sms = sm_count(e->dev);
+    QD_CK(cudaStreamCreateWithFlags(&e->own_stream, cudaStreamNonBlocking));
+    e->stream = e->own_stream;
+    load_engine(e, runtime_dir, m);
+  } catch (const QdError& err) {
+    const int code = fail(nullptr, err);
+    free_engine(e);
+    return code;
+  } catch (const std::exception& ex) {
+    const int code = fail(nullptr, QdError{QD_E_IO, ex.what()});
+    free_engine(e);
+    return code;
+  }
+  *out = e;
+  return QD_OK;
+}
+
+void qd_engine_destroy(qd_engine* e) { free_engine(e); }
+
+const char* qd_last_error(const qd_engine* e) { return e ? e->err.c_str() : t_last_error.c_str(); }
+
+int qd_engine_profile(const qd_engine* e, qd_profile* out) {
+  if (!e || !out) return QD_E_INVALID;
+  *out = e->p;
+  return QD_OK;
+}
+
+int qd_generate_greedy(qd_engine* e, const int32_t* input_ids, int n_prompt, int max_new_tokens,
+                       int32_t* out_ids, qd_token_cb on_token, void* user, qd_stats* stats) {
+  if (!e) return fail(nullptr, QdError{QD_E_INVALID, "engine is NULL"});
+  try {
+    if (!input_ids || n_prompt < 1) throw QdError{QD_E_INVALID, "the prompt needs at least one token"};
+    if (max_new_tokens < 0 || (max_new_tokens > 0 && !out_ids)) throw QdError{QD_E_INVALID, "bad max_new_tokens or out_ids"};
+    // Positions written: 0 .. n_prompt + max_new - 2 (the last token is never fed back).
+    if ((long long)n_prompt + max_new_tokens - 1 > e->opt.max_seq)
+      throw QdError{QD_E_RANGE, "prompt + generation length exceeds max_seq (" + std::to_string(e->opt.max_seq) + ")"};
+    for (int i = 0; i < n_prompt; ++i)
+      if (input_ids[i] < 0 || input_ids[i] >= e->p.vocab) throw QdError{QD_E_RANGE, "prompt token id outside the vocabulary"};
+    QD_CK(cudaSetDevice(e->dev));
+    const auto t0 = std::chrono::steady_clock::now();
+    std::memcpy(e->pinned_ids, input_ids, (size_t)n_prompt * 4);
+    QD_CK(cudaMemcpyAsync(e->tokens, e->pinned_ids, (size_t)n_prompt * 4, cudaMemcpyHostToDevice, e->stream));
+    set_state(e, 0, max_new_tokens);
+    const int n_layers_only = max_new_tokens > 0 ? n_prompt - 1 : n_prompt;
+    for (int i = 0; i < n_layers_only; ++i) run_token(e, false);
+    double first_ms = 0.0;
+    int produced = 0;
+    bool stop = false;
+    for (int step = 0; step < max_new_tokens && !stop; ++step) {
+      run_token(e, true);
+      QD_CK(cudaEventRecord(e->ev[step & 1], e->stream));
+      if (step > 0) {  // deliver the previous token while this one runs
+        QD_CK(cudaEventSynchronize(e->ev[(step - 1) & 1]));
+        const int tok = *reinterpret_cast<volatile int*>(e->out_host + step - 1);
+        out_ids[step - 1] = tok;
+        ++produced;
+        if (step == 1) first_ms = ms_since(t0);
+        if (on_token && on_token(tok, user)) stop = true;
+      }
+    }
+    QD_CK(cudaStreamSynchronize(e->stream));
+    if (max_new_tokens > 0 && !stop) {
+      const int last = max_new_tokens - 1;
+      const int tok = *reinterpret_cast<volatile int*>(e->out_host + last);
+      out_ids[last] = tok;
+      ++produced;
+      if (last == 0) first_ms = ms_since(t0);
+      if (on_token) on_token(tok, user);
+    }
+    const double gen_ms = ms_since(t0);
+    check_state(e);
+    if (stats) {
+      stats->generate_ms = gen_ms;
+      stats->first_token_ms = first_ms;
+      stats->generated_tokens = produced;
+      stats->prompt_tokens = n_prompt;
+      stats->steady_ms_per_token = produced > 1 ? (gen_ms - first_ms) / (produced - 1) : NAN;
+    }
+  } catch (const QdError& err) {
+    return fail(e, err);
+  }
+  return QD_OK;
+}
+
+int qd_engine_logits(qd_engine* e, float* host_logits) {
+  if (!e || !host_logits) return fail(e, QdError{QD_E_INVALID, "NULL argument"});
+  try {
+    QD_CK(cudaSetDevice(e->dev));
+    QD_CK(cudaMemcpyAsync(host_logits, e->logits, (size_t)e->p.vocab * 4, cudaMemcpyDeviceToHost, e->stream));
+    QD_CK(cudaStreamSynchronize(e->stream));
+  } catch (const QdError& err) {
+    return fail(e, err);
+  }
+  return QD_OK;
+}
+
+int qd_engine_hidden(qd_engine* e, float* host_hidden) {
+  if (!e || !host_hidden) return fail(e, QdError{QD_E_INVALID, "NULL argument"});
+  try {
+    QD_CK(cudaSetDevice(e->dev));
+    QD_CK(cudaMemcpyAsync(host_hidden, e->h, (size_t)e->p.hidden * 4, cudaMemcpyDeviceToHost, e->stream));
+    QD_CK(cudaStreamSynchronize(e->stream));
+  } catch (const QdError& err) {
+    return fail(e, err);
+  }
+  return QD_OK;
+}
+
+int qd_engine_forward_trace(qd_engine* e, int32_t token, int position, float* host_trace) {
+  if (!e || !host_trace) return fail(e, QdError{QD_E_INVALID, "NULL argument"});
+  try {
+    if (token < 0 || token >= e->p.vocab) throw QdError{QD_E_RANGE, "token id outside the vocabulary"};
+    if (position < 0 || position >= e->opt.max_seq) throw QdError{QD_E_RANGE, "position beyond max_seq"};
+    QD_CK(cudaSetDevice(e->dev));
+    e->pinned_ids[0] = token;
+    QD_CK(cudaMemcpyAsync(e->tokens + position, e->pinned_ids, 4, cudaMemcpyHostToDevice, e->stream));
+    set_state(e, position, 0);
+    for (int l = 0; l < e->p.layers; ++l) {
+      enqueue_layer(e, l, e->stream);
+      QD_CK(cudaMemcpyAsync(host_trace + (size_t)l * e->p.hidden, e->h, (size_t)e->p.hidden * 4,
+                            cudaMemcpyDeviceToHost, e->stream));
+    }
+    QD_CK(cudaStreamSynchronize(e->stream));
+    check_state(e);
+  } catch (const QdError& err) {
+    return fail(e, err);
+  }
+  return QD_OK;
+}
+
+int qd_engine_set_stream(qd_engine* e, void* stream) {
+  if (!e) return fail(nullptr, QdError{QD_E_INVALID, "engine is NULL"});
+  try {
+    QD_CK(cudaSetDevice(e->dev));
+    QD_CK(cudaStreamSynchronize(e->stream));
+    e->stream = stream ? static_cast<cudaStream_t>(stream) : e->own_stream;
+  } catch (const QdError& err) {
+    return fail(e, err);
+  }
+  return QD_OK;
+}
+
+int qd_decode_begin(qd_engine* e, const int32_t* input_ids, int n_prompt, int max_new_tokens) {
+  if (!e) return fail(nullptr, QdError{QD_E_INVALID, "engine is NULL"});
+  try {
+    if (!input_ids || n_prompt < 1 || n_prompt > e->opt.max_seq) throw QdError{QD_E_INVALID, "bad prompt length"};
+    if (max_new_tokens < 0 || max_new_tokens > e->opt.max_seq) throw QdError{QD_E_INVALID, "bad max_new_tokens"};
+    for (int i = 0; i < n_prompt; ++i)
+      if (input_ids[i] < 0 || input_ids[i] >= e->p.vocab) throw QdError{QD_E_RANGE, "prompt token id outside the vocabulary"};
+    QD_CK(cudaSetDevice(e->dev));
+    QD_CK(cudaStreamSynchronize(e->stream));  // pinned staging buffers are reused below
+    std::memcpy(e->pinned_ids, input_ids, (size_t)n_prompt * 4);
+    QD_CK(cudaMemcpyAsync(e->tokens, e->pinned_ids, (size_t)n_prompt * 4, cudaMemcpyHostToDevice, e->stream));
+    set_state(e, 0, max_new_tokens);
+    e->stepping_max_new = max_new_tokens;
+    for (int i = 0; i < n_prompt - 1; ++i) run_token(e, false);
+  } catch (const QdError& err) {
+    return fail(e, err);
+  }
+  return QD_OK;
+}
+
+int qd_decode_step(qd_engine* e) {
+  if (!e) return fail(nullptr, QdError{QD_E_INVALID, "engine is NULL"});
+  try {
+    run_token(e, true);
+  } catch (const QdError& err) {
+    return fail(e, err);
+  }
+  return QD_OK;
+}
+
+int qd_decode_seek(qd_engine* e, int position) {
+  if (!e) return fail(nullptr, QdError{QD_E_INVALID, "engine is NULL"});
+  try {
+    if (position < 0 || position >= e->opt.max_seq) throw QdError{QD_E_RANGE, "position beyond max_seq"};
+    launch(k_seek, dim3(1), e->stream, e->st, position);
+  } catch (const QdError& err) {
+    return fail(e, err);
+  }
+  return QD_OK;
+}
+
+int qd_decode_sync(qd_engine* e, int32_t* out_ids, int n) {
+  if (!e) return fail(nullptr, QdError{QD_E_INVALID, "engine is NULL"});
+  try {
+    QD_CK(cudaSetDevice(e->dev));
+    check_state(e);
+    const int k = std::min(n, e->stepping_max_new);
+    for (int i = 0; out_ids && i < k; ++i) out_ids[i] = *reinterpret_cast<volatile int*>(e->out_host + i);
+  } catch (const QdError& err) {
+    return fail(e, err);
+  }
+  return QD_OK;
+}
+
+int qd_decode_step_kernels(const qd_engine* e) { return e ? e->p.layers * 5 + 1 : 0; }
+
+// ---- kernel level -------------------------------------------------------------
+
+int qd_q4_matvec(const float* x, const uint32_t* weights, const uint16_t* scales_f16, float* y,
+                 uint32_t in_size, uint32_t out_size, uint32_t blocks_per_row, uint32_t block_size,
+                 void* stream) {
+  try {
+    if (!x || !weights || !scales_f16 || !y) throw QdError{QD_E_INVALID, "NULL pointer"};
+    if (block_size != (uint32_t)kBlockCols) throw QdError{QD_E_INVALID, "only block_size 32 is supported"};
+    if (out_size == 0 || blocks_per_row == 0 || blocks_per_row > 128 || in_size == 0 ||
+        in_size > blocks_per_row * block_size)
+      throw QdError{QD_E_INVALID, "bad matvec dimensions (in_size <= blocks_per_row * 32 <= 4096)"};
+    if ((reinterpret_cast<uintptr_t>(weights) & 15) != 0) throw QdError{QD_E_INVALID, "weights must be 16-byte aligned"};
+    StageArgs a{};
+    a.w = reinterpret_cast<const uint4*>(weights);
+    a.s = reinterpret_cast<const __half*>(scales_f16);
+    a.rows = (int)out_size; a.nb = (int)blocks_per_row; a.k_valid = (int)in_size; a.src = x; a.out = y;
+    launch_stage<kProPlain, kEpiStore>(a, plan_stage(a.rows, a.nb, current_sms()), static_cast<cudaStream_t>(stream));
+  } catch (const QdError& err) {
+    return fail(nullptr, err);
+  }
+  return QD_OK;
+}
+
+static constexpr int kLmMaxGrid = 1024;
+
+size_t qd_lm_head_argmax_workspace_bytes(uint32_t) { return 256 + (size_t)kLmMaxGrid * 8; }
+
+int qd_lm_head_argmax(const float* hidden, const float* norm_weight, float eps, const uint16_t* embed_f16,
+                      float* logits, uint32_t* result, uint32_t hidden_size, uint32_t vocab, void* workspace,
+                      void* stream) {
+  try {
+    if (!hidden || !embed_f16 || !result || !workspace) throw QdError{QD_E_INVALID, "NULL pointer"};
+    if (hidden_size % 256 || hidden_size == 0 || hidden_size > 1024)
+      throw QdError{QD_E_INVALID, "hidden_size must be 256, 512, 768 or 1024"};
+    if (vocab == 0) throw QdError{QD_E_INVALID, "vocab must be positive"};
+    if ((reinterpret_cast<uintptr_t>(embed_f16) & 15) || (reinterpret_cast<uintptr_t>(workspace) & 15))
+      throw QdError{QD_E_INVALID, "embed_f16 and workspace must be 16-byte aligned"};
+    char* ws = static_cast<char*>(workspace);
+    LmArgs a{};
+    a.h = hidden; a.norm_w = norm_weight; a.eps = eps; a.table = reinterpret_cast<const uint4*>(embed_f16);
+    a.vocab = (int)vocab; a.H = (int)hidden_size; a.logits = logits;
+    a.counter = reinterpret_cast<unsigned*>(ws);
+    a.part_v = reinterpret_cast<float*>(ws + 256);
+    a.part_i = reinterpret_cast<uint32_t*>(ws + 256 + kLmMaxGrid * 4);
+    a.result = result;
+    const int grid = std::min(current_sms(), kLmMaxGrid);
+    launch_lmhead(a, grid, static_cast<cudaStream_t>(stream));
+  } catch (const QdError& err) {
+    return fail(nullptr, err);
+  }
+  return QD_OK;
+}
+
+size_t qd_gqa_decode_workspace_bytes(uint32_t seq_len, uint32_t q_heads) {
+  const size_t splits = (seq_len + kAttnChunk - 1) / kAttnChunk;
+  return 256 + splits * q_heads * 8 + splits * q_heads * kHeadDim * 4;
+}
+
+int qd_gqa_decode(const float* q, const void* k_cache, const void* v_cache, int kv_dtype, float* y,
+                  uint32_t seq_len, uint32_t q_heads, uint32_t kv_heads, uint32_t head_dim, void* workspace,
+                  void* stream) {
+  try {
+    if (!q || !k_cache || !v_cache || !y || !workspace) throw QdError{QD_E_INVALID, "NULL pointer"};
+    if (head_dim != (uint32_t)kHeadDim) throw QdError{QD_E_INVALID, "head_dim must be 128"};
+    if (seq_len == 0 || kv_heads == 0 || q_heads % kv_heads) throw QdError{QD_E_INVALID, "bad attention dimensions"};
+    if (kv_dtype != QD_KV_F16 && kv_dtype != QD_KV_F32) throw QdError{QD_E_INVALID, "bad kv_dtype"};
+    const int splits = (int)((seq_len + kAttnChunk - 1) / kAttnChunk);
+    char* ws = static_cast<char*>(workspace);
+    AttnArgs a{};
+    a.q_in = q; a.k_cache = const_cast<void*>(k_cache); a.v_cache = const_cast<void*>(v_cache);
+    a.st = nullptr; a.seq_len = (int)seq_len; a.max_seq = (int)seq_len;
+    a.q_heads = (int)q_heads; a.kv_heads = (int)kv_heads; a.scale = 1.0f / std::sqrt((float)kHeadDim);
+    a.raw_q = 1;
+    a.part_ml = reinterpret_cast<float2*>(ws + 256);
+    a.part_o = reinterpret_cast<float*>(ws + 256 + (size_t)splits * q_heads * 8);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    launch_attn(a, kv_dtype, splits, s);
+    const int n = (int)q_heads * kHeadDim;
+    launch(k_attn_combine, dim3((n + kThreads - 1) / kThreads), s, (const float2*)a.part_ml, (const float*)a.part_o,
+           splits, (int)q_heads, y);
+  } catch (const QdError& err) {
+    return fail(nullptr, err);
+  }
+  return QD_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,292 @@
+"""Host-side API over libqdecode.so.
+
+Two layers:
+
+* `Engine` and the kernel-level functions (`q4_matvec`, `lm_head_argmax`,
+  `gqa_decode`) - thin, typed wrappers of the C ABI.
+* `createWebGpuContext` / `runCustomQwenGreedyPrompt` - the reference's own
+  JavaScript entry points (src/bench/webgpu-runtime.js:43-60 and :165-214),
+  same argument names, same result object and the same error on an over-long
+  request, so callers of the reference switch by changing the import.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from typing import Callable, Optional, Sequence
+
+import numpy as np
+
+from . import _lib
+from ._lib import QD_KV_F16, QD_KV_F32, QdError, QdOptions, QdProfile, QdStats, check
+
+# qwenProfile, src/model/qwen3-0.6b.js:1-15.
+qwen_profile = {
+    "modelId": "Qwen/Qwen3-0.6B",
+    "parameters": "0.6B",
+    "nonEmbeddingParameters": "0.44B",
+    "layers": 28,
+    "hiddenSize": 1024,
+    "intermediateSize": 3072,
+    "attentionHeads": 16,
+    "kvHeads": 8,
+    "headDim": 128,
+    "contextLength": 32768,
+    "vocabSize": 151936,
+    "normEpsilon": 1e-6,
+    "quantizationTarget": "weight-only Q4 MatMulNBits for projection and MLP matvecs",
+}
+qwenProfile = qwen_profile
+
+VARIANTS = ("original", "mixed", "optimized")
+
+
+class Engine:
+    """One model resident on one GPU (qd_engine_create / qd_generate_greedy)."""
+
+    def __init__(self, runtime_dir: str, device: int = 0, max_seq: int = 256, kv_dtype: str = "f16",
+                 rope_row_stride: int = 0, variant: str = "optimized", use_graph: bool = True):
+        L = _lib.load()
+        opt = QdOptions()
+        L.qd_options_default(C.byref(opt))
+        opt.device = device
+        opt.max_seq = max_seq
+        opt.kv_dtype = {"f16": QD_KV_F16, "f32": QD_KV_F32}[kv_dtype]
+        opt.rope_row_stride = rope_row_stride
+        self._variant = variant.encode()
+        opt.variant = self._variant
+        opt.use_graph = int(use_graph)
+        h = C.c_void_p()
+        check(L.qd_engine_create(os.fsencode(runtime_dir), C.byref(opt), C.byref(h)))
+        self._h = h
+        self.max_seq = max_seq
+        self.variant = variant
+        p = QdProfile()
+        check(L.qd_engine_profile(self._h, C.byref(p)), self._h)
+        self.profile = {f: getattr(p, f) for f, _ in QdProfile._fields_}
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            _lib.load().qd_engine_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        self.close()
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def generate_greedy(self, ids: Sequence[int], max_new: int,
+                        on_token: Optional[Callable[[int], object]] = None):
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        out = np.zeros(max(max_new, 1), np.int32)
+        st = QdStats()
+        err: list = []
+
+        def _cb(tok, _user):
+            try:
+                return 1 if (on_token and on_token(int(tok)) is False) else 0
+            except BaseException as ex:  # surface callback errors after the C call returns
+                err.append(ex)
+                return 1
+
+        cb = _lib.TOKEN_CB(_cb)
+        rc = _lib.load().qd_generate_greedy(self._h, ids.ctypes.data, int(ids.size), int(max_new),
+                                            out.ctypes.data, cb, None, C.byref(st))
+        check(rc, self._h)
+        if err:
+            raise err[0]
+        stats = {f: getattr(st, f) for f, _ in QdStats._fields_}
+        return out[:st.generated_tokens].tolist(), stats
+
+    # stepping interface (enqueue only)
+    def set_stream(self, stream=None) -> None:
+        """Enqueue on a torch.cuda.Stream (None: the engine's own stream)."""
+        ptr = C.c_void_p(stream.cuda_stream) if stream is not None else None
+        check(_lib.load().qd_engine_set_stream(self._h, ptr), self._h)
+
+    def decode_begin(self, ids: Sequence[int], max_new: int) -> None:
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        check(_lib.load().qd_decode_begin(self._h, ids.ctypes.data, int(ids.size), int(max_new)), self._h)
+
+    def decode_step(self) -> None:
+        check(_lib.load().qd_decode_step(self._h), self._h)
+
+    def decode_seek(self, position: int) -> None:
+        check(_lib.load().qd_decode_seek(self._h, int(position)), self._h)
+
+    def decode_sync(self, n: int = 0) -> list:
+        out = np.zeros(max(n, 1), np.int32)
+        check(_lib.load().qd_decode_sync(self._h, out.ctypes.data, int(n)), self._h)
+        return out[:n].tolist()
+
+    @property
+    def step_kernels(self) -> int:
+        return int(_lib.load().qd_decode_step_kernels(self._h))
+
+    def logits(self) -> np.ndarray:
+        out = np.zeros(self.profile["vocab"], np.float32)
+        check(_lib.load().qd_engine_logits(self._h, out.ctypes.data), self._h)
+        return out
+
+    def hidden(self) -> np.ndarray:
+        out = np.zeros(self.profile["hidden"], np.float32)
+        check(_lib.load().qd_engine_hidden(self._h, out.ctypes.data), self._h)
+        return out
+
+    def forward_trace(self, token: int, position: int) -> np.ndarray:
+        out = np.zeros((self.profile["layers"], self.profile["hidden"]), np.float32)
+        check(_lib.load().qd_engine_forward_trace(self._h, int(token), int(position), out.ctypes.data), self._h)
+        return out
+
+
+# ---- the reference's JavaScript API --------------------------------------------
+
+class CudaDevice:
+    """What createWebGpuContext().device stands for: a GPU plus the runtime files.
+
+    Engines are created on first use and kept (the reference builds a runtime on
+    every call and never frees it, docs/04-results.md:43-54)."""
+
+    def __init__(self, runtime_dir: str, ordinal: int = 0, kv_dtype: str = "f16"):
+        self.runtime_dir = runtime_dir
+        self.ordinal = ordinal
+        self.kv_dtype = kv_dtype
+        self._engines: dict = {}
+
+    def engine(self, needed_positions: int, variant: str) -> Engine:
+        cap = max(256, needed_positions)
+        for (c, v), eng in self._engines.items():
+            if c >= needed_positions and v == variant:
+                return eng
+        eng = Engine(self.runtime_dir, self.ordinal, max_seq=cap, kv_dtype=self.kv_dtype, variant=variant)
+        self._engines[(cap, variant)] = eng
+        return eng
+
+    def close(self) -> None:
+        for eng in self._engines.values():
+            eng.close()
+        self._engines.clear()
+
+
+def createWebGpuContext(runtime_dir: Optional[str] = None, device: int = 0, kv_dtype: str = "f16"):
+    """createWebGpuContext (webgpu-runtime.js:43-60): {adapter, device}.
+
+    runtime_dir defaults to $QDECODE_RUNTIME (the reference fetches /qwen/runtime)."""
+    runtime_dir = runtime_dir or os.environ.get("QDECODE_RUNTIME")
+    if not runtime_dir or not os.path.exists(os.path.join(runtime_dir, "manifest.json")):
+        raise RuntimeError("No qwen runtime directory was found (set QDECODE_RUNTIME).")
+    try:
+        import torch  # noqa: F401  (only for the adapter description)
+        name = torch.cuda.get_device_name(device) if torch.cuda.is_available() else "cuda"
+    except Exception:  # pragma: no cover
+        name = "cuda"
+    return {"adapter": {"info": {"vendor": "nvidia", "architecture": "sm_100a", "device": name}},
+            "device": CudaDevice(runtime_dir, device, kv_dtype)}
+
+
+create_web_gpu_context = createWebGpuContext
+
+
+def runCustomQwenGreedyPrompt(*, device: CudaDevice, profile: dict, inputIds: Sequence[int],
+                              maxNewTokens: int, onToken=None, decodeToken=None, onProgress=None,
+                              variant: str = "optimized", maxSeqLen: int = 256) -> dict:
+    """runCustomQwenGreedyPrompt (webgpu-runtime.js:165-214) on the B200 engine.
+
+    Raises like the reference when prompt + generation exceeds the capacity
+    (256 positions by default, the reference's cap; pass maxSeqLen for more)."""
+    if len(inputIds) + maxNewTokens > maxSeqLen:
+        raise ValueError(f"Custom CUDA path currently supports prompt + generation length up to "
+                         f"{maxSeqLen} tokens.")
+    eng = device.engine(len(inputIds) + maxNewTokens, variant)
+    p = eng.profile
+    for key, ours in (("hiddenSize", "hidden"), ("intermediateSize", "intermediate"),
+                      ("attentionHeads", "heads"), ("kvHeads", "kv_heads"), ("headDim", "head_dim")):
+        if key in profile and int(profile[key]) != p[ours]:
+            raise ValueError(f"profile.{key}={profile[key]} does not match the runtime ({p[ours]})")
+    if onProgress:
+        onProgress(f"Custom prefill {len(inputIds)}/{len(inputIds)}")
+    count = [0]
+
+    def _tok(t):
+        count[0] += 1
+        if onProgress:
+            onProgress(f"Custom decode {count[0]}/{maxNewTokens}")
+        if onToken:
+            onToken(decodeToken([t]) if decodeToken else str(t))
+
+    generated, st = eng.generate_greedy(list(inputIds), maxNewTokens, _tok)
+    return {
+        "generated": generated,
+        "generatedTokens": len(generated),
+        "generateMs": st["generate_ms"],
+        "firstTokenMs": st["first_token_ms"] if generated else None,
+        "outputText": decodeToken(generated) if decodeToken else " ".join(str(t) for t in generated),
+    }
+
+
+run_custom_qwen_greedy_prompt = runCustomQwenGreedyPrompt
+
+
+# ---- kernel level (torch CUDA tensors as device memory) -------------------------
+
+def _stream(stream):
+    import torch
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return C.c_void_p(s.cuda_stream)
+
+
+def q4_matvec(x, weights, scales_f16, y=None, in_size: Optional[int] = None, stream=None):
+    """y = dequant(weights) . x on the GPU (qd_q4_matvec). weights: uint32/int32 [N][K/8]."""
+    import torch
+    n = weights.shape[0]
+    bpr = scales_f16.numel() // n
+    in_size = in_size or bpr * 32
+    if y is None:
+        y = torch.empty(n, dtype=torch.float32, device=x.device)
+    check(_lib.load().qd_q4_matvec(x.data_ptr(), weights.data_ptr(), scales_f16.data_ptr(), y.data_ptr(),
+                                   in_size, n, bpr, 32, _stream(stream)))
+    return y
+
+
+class LmHeadWorkspace:
+    def __init__(self, vocab: int, device):
+        import torch
+        n = _lib.load().qd_lm_head_argmax_workspace_bytes(vocab)
+        self.buf = torch.zeros(n, dtype=torch.uint8, device=device)
+
+
+def lm_head_argmax(hidden, embed_f16, norm_weight=None, eps: float = 1e-6, logits=None,
+                   workspace: Optional[LmHeadWorkspace] = None, result=None, stream=None):
+    """logits = embed . rms_norm(hidden) and the (index, value) argmax (qd_lm_head_argmax)."""
+    import torch
+    vocab, hs = embed_f16.shape
+    ws = workspace or LmHeadWorkspace(vocab, hidden.device)
+    if result is None:
+        result = torch.zeros(2, dtype=torch.int32, device=hidden.device)
+    lp = logits.data_ptr() if logits is not None else None
+    nw = norm_weight.data_ptr() if norm_weight is not None else None
+    check(_lib.load().qd_lm_head_argmax(hidden.data_ptr(), nw, eps, embed_f16.data_ptr(), lp,
+                                        result.data_ptr(), hs, vocab, ws.buf.data_ptr(), _stream(stream)))
+    return result
+
+
+def gqa_decode(q, k_cache, v_cache, seq_len: int, q_heads: int, kv_heads: int, y=None, stream=None):
+    """Decode attention over [0, seq_len) (qd_gqa_decode); caches f16 or f32 [seq][kv][128]."""
+    import torch
+    kv_dtype = QD_KV_F16 if k_cache.dtype == torch.float16 else QD_KV_F32
+    if y is None:
+        y = torch.empty(q_heads * 128, dtype=torch.float32, device=q.device)
+    n = _lib.load().qd_gqa_decode_workspace_bytes(seq_len, q_heads)
+    ws = torch.empty(n, dtype=torch.uint8, device=q.device)
+    check(_lib.load().qd_gqa_decode(q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), kv_dtype,
+                                    y.data_ptr(), seq_len, q_heads, kv_heads, 128, ws.data_ptr(),
+                                    _stream(stream)))
+    return y
+
+
+__all__ = ["Engine", "QdError", "createWebGpuContext", "runCustomQwenGreedyPrompt", "qwen_profile",
+           "qwenProfile", "q4_matvec", "lm_head_argmax", "gqa_decode", "LmHeadWorkspace"]

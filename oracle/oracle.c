@@ -276,10 +276,25 @@ void qo_residual_add(const float* a, const float* b, float* y, uint32_t n) {
 
 /* ---- LM head + argmax ------------------------------------------------------ */
 
+/* Exact f16 -> f32 for all 65536 codes (the values qo_half_to_float gives). */
+static float g_h2f[65536];
+static int g_h2f_ready = 0;
+static const float* h2f_table(void) {
+  if (!g_h2f_ready) {
+#pragma omp critical(qo_h2f)
+    if (!g_h2f_ready) {
+      for (uint32_t h = 0; h < 65536u; ++h) g_h2f[h] = qo_half_to_float((uint16_t)h);
+      __atomic_store_n(&g_h2f_ready, 1, __ATOMIC_RELEASE);
+    }
+  }
+  return g_h2f;
+}
+
 /* lm_head_f16.wgsl:19-58: 64 lanes per vocab row, one f16 pair (u32 word) per lane. */
 void qo_lm_head_f16(const float* hidden, const uint16_t* embed, float* logits,
                     uint32_t hidden_size, uint32_t rows) {
   const uint32_t words_per_row = hidden_size / 2u;
+  const float* h2f = h2f_table();
 #pragma omp parallel for schedule(static)
   for (long row = 0; row < (long)rows; ++row) {
     const uint16_t* e = embed + (uint64_t)row * hidden_size;
@@ -288,8 +303,8 @@ void qo_lm_head_f16(const float* hidden, const uint16_t* embed, float* logits,
       float acc = 0.0f;
       for (uint32_t w = tid; w < words_per_row; w += 64) {
         const uint32_t col = w * 2u;
-        const float px = qo_half_to_float(e[col]);
-        const float py = qo_half_to_float(e[col + 1]);
+        const float px = h2f[e[col]];
+        const float py = h2f[e[col + 1]];
         acc = acc + px * hidden[col] + py * hidden[col + 1];
       }
       partial[tid] = acc;

@@ -1,0 +1,126 @@
+"""The C-ABI library: builds, loads, exports what include/qdecode.h declares, and
+rejects bad input on the host (no GPU needed for any of these)."""
+import ctypes as C
+import json
+import os
+import re
+
+import pytest
+
+from kernel_optimization_webgpu_b200 import _lib, runtime, synth
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def header_functions():
+    text = open(os.path.join(ROOT, "include", "qdecode.h")).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(qd_[a-z0-9_]+)\s*\(", text)) - {"qd_token_cb"})
+
+
+def test_library_exports_every_declared_function():
+    L = _lib.load()
+    declared = header_functions()
+    assert declared, "no declarations parsed"
+    missing = [f for f in declared if not hasattr(L, f)]
+    assert not missing, missing
+    assert sorted(_lib.EXPORTS) == declared
+
+
+def test_library_is_sm100a_only_and_links_no_torch():
+    data = open(_lib.lib_path(), "rb").read()
+    assert b"sm_100a" in data
+    assert b"libtorch" not in data and b"libc10" not in data
+
+
+def test_options_default():
+    opt = _lib.QdOptions()
+    _lib.load().qd_options_default(C.byref(opt))
+    assert opt.max_seq == 256 and opt.kv_dtype == _lib.QD_KV_F16 and opt.use_graph == 1
+    assert opt.rope_row_stride == 0 and opt.variant == b"optimized"
+
+
+def _create(runtime_dir, **kw):
+    return runtime.Engine(runtime_dir, **kw)
+
+
+def test_create_rejects_missing_runtime(tmp_path):
+    with pytest.raises(_lib.QdError) as ex:
+        _create(str(tmp_path / "nope"))
+    assert ex.value.code == _lib.QD_E_IO
+    assert "manifest.json" in str(ex.value)
+
+
+def test_create_rejects_malformed_manifest(tmp_path):
+    (tmp_path / "manifest.json").write_text("{\"hiddenSize\": 1024, ")
+    with pytest.raises(_lib.QdError) as ex:
+        _create(str(tmp_path))
+    assert ex.value.code == _lib.QD_E_IO
+
+
+def _manifest_copy(src_dir, dst_dir, edit):
+    m = json.load(open(os.path.join(src_dir, "manifest.json")))
+    edit(m)
+    os.makedirs(dst_dir, exist_ok=True)
+    json.dump(m, open(os.path.join(dst_dir, "manifest.json"), "w"))
+
+
+def test_create_rejects_unsupported_head_dim(tiny_runtime, tmp_path):
+    _manifest_copy(tiny_runtime, str(tmp_path), lambda m: m.update(headDim=64))
+    with pytest.raises(_lib.QdError) as ex:
+        _create(str(tmp_path))
+    assert ex.value.code in (_lib.QD_E_INVALID, _lib.QD_E_IO)
+
+
+def test_create_rejects_projection_shape_mismatch(tiny_runtime, tmp_path):
+    def edit(m):
+        m["layers"][1]["projections"]["down"]["matmulNBits"]["outSize"] = 7
+    _manifest_copy(tiny_runtime, str(tmp_path), edit)
+    with pytest.raises(_lib.QdError) as ex:
+        _create(str(tmp_path))
+    assert ex.value.code == _lib.QD_E_IO and "down" in str(ex.value)
+
+
+def test_create_rejects_block_size_other_than_32(tiny_runtime, tmp_path):
+    def edit(m):
+        d = m["layers"][0]["projections"]["q"]["matmulNBits"]
+        d["blockSize"], d["blocksPerRow"] = 64, d["blocksPerRow"] // 2
+    _manifest_copy(tiny_runtime, str(tmp_path), edit)
+    with pytest.raises(_lib.QdError):
+        _create(str(tmp_path))
+
+
+def test_create_rejects_max_seq_beyond_rope_table(tiny_runtime):
+    # TINY has 4096 table rows; position p reads row 2p, so 2049 positions do not fit.
+    with pytest.raises(_lib.QdError) as ex:
+        _create(tiny_runtime, max_seq=2049)
+    assert ex.value.code == _lib.QD_E_RANGE
+
+
+def test_kernel_entry_points_validate_before_touching_the_device():
+    L = _lib.load()
+    p = C.c_void_p(16)
+    assert L.qd_q4_matvec(p, p, p, p, 1024, 8, 32, 16, None) == _lib.QD_E_INVALID   # block 16
+    assert L.qd_q4_matvec(p, p, p, p, 2048, 8, 32, 32, None) == _lib.QD_E_INVALID   # in_size > 32*32
+    assert L.qd_q4_matvec(None, p, p, p, 1024, 8, 32, 32, None) == _lib.QD_E_INVALID
+    assert b"block_size" in L.qd_last_error(None) or L.qd_last_error(None)
+    assert L.qd_lm_head_argmax(p, None, 1e-6, p, None, p, 1000, 10, p, None) == _lib.QD_E_INVALID
+    assert L.qd_gqa_decode(p, p, p, 0, p, 10, 16, 8, 64, p, None) == _lib.QD_E_INVALID
+    assert L.qd_gqa_decode(p, p, p, 0, p, 10, 15, 8, 128, p, None) == _lib.QD_E_INVALID
+    assert L.qd_lm_head_argmax_workspace_bytes(151936) >= 256 + 8 * 148
+    assert L.qd_gqa_decode_workspace_bytes(2048, 16) >= 8 * 16 * (128 * 4 + 8)
+
+
+def test_greedy_api_rejects_over_long_requests_like_the_reference():
+    dev = runtime.CudaDevice("/nonexistent")
+    with pytest.raises(ValueError, match="up to 256 tokens"):
+        runtime.runCustomQwenGreedyPrompt(device=dev, profile=runtime.qwenProfile,
+                                          inputIds=list(range(200)), maxNewTokens=57)
+
+
+def test_qwen_profile_mirrors_the_reference_profile():
+    p = runtime.qwenProfile
+    s = synth.QWEN3_0_6B
+    assert (p["layers"], p["hiddenSize"], p["intermediateSize"], p["attentionHeads"], p["kvHeads"],
+            p["headDim"], p["vocabSize"], p["normEpsilon"]) == (s.layers, s.hidden, s.intermediate, s.heads,
+                                                               s.kv_heads, s.head_dim, s.vocab, s.eps)

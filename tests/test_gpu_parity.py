@@ -1,0 +1,266 @@
+"""CUDA path vs the CPU oracle through the C ABI (needs a B200).
+
+Tolerances: north_star allows 1e-2 relative for logits and matvec outputs; the
+kernels accumulate in f32 like the reference, so these tests hold them to a
+tighter 1e-4 (max |diff| / max |reference|) and greedy ids to bit-exact.
+"""
+import json
+import math
+import os
+
+import numpy as np
+import pytest
+
+from kernel_optimization_webgpu_b200 import runtime as R
+from kernel_optimization_webgpu_b200 import synth
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+torch = pytest.importorskip("torch")
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
+TOL = 1e-4
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _cuda():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+
+
+def rel(a, b):
+    a, b = np.asarray(a, np.float64), np.asarray(b, np.float64)
+    return float(np.max(np.abs(a - b)) / max(float(np.max(np.abs(b))), 1e-30))
+
+
+def dev(a, dtype=None):
+    t = torch.from_numpy(np.ascontiguousarray(a))
+    if dtype is not None:
+        t = t.view(dtype)
+    return t.cuda()
+
+
+def run_matvec(x, w, s, in_size=None):
+    y = R.q4_matvec(dev(x), dev(w.view(np.int32)), dev(s.astype(np.float16)), in_size=in_size)
+    torch.cuda.synchronize()
+    return y.cpu().numpy()
+
+
+@pytest.mark.parametrize("n,k", [(3072, 1024), (2048, 1024), (1024, 2048), (1024, 3072),
+                                 (4096, 1024), (6144, 1024)])
+def test_q4_matvec_config0_shapes(n, k):
+    x, w, s = synth.matvec_case(n, k, seed=0)
+    assert rel(run_matvec(x, w, s), O.q4_matvec(x, w, s)) < TOL
+
+
+def test_q4_matvec_matches_golden_js_port():
+    refs = np.load(os.path.join(GOLDEN, "js_cpu_refs.npz"))
+    for name, (n, k) in {"gate": (3072, 1024), "q": (2048, 1024), "o": (1024, 2048),
+                         "down": (1024, 3072)}.items():
+        x, w, s = synth.matvec_case(n, k, seed=0)
+        assert rel(run_matvec(x, w, s), refs[f"q4_{name}_y"]) < TOL, name
+
+
+@pytest.mark.parametrize("n,k,in_size", [(1, 1024, 1024), (7, 512, 512), (33, 256, 250),
+                                         (129, 4096, 4096), (5000, 96, 90)])
+def test_q4_matvec_ragged_shapes(n, k, in_size):
+    x, w, s = synth.matvec_case(n, k, seed=7)
+    assert rel(run_matvec(x, w, s, in_size), O.q4_matvec(x, w, s, in_size=in_size)) < TOL
+
+
+def lm_head(table, h, norm_weight=None, eps=1e-6):
+    logits = torch.empty(table.shape[0], dtype=torch.float32, device="cuda")
+    nw = dev(norm_weight) if norm_weight is not None else None
+    r = R.lm_head_argmax(dev(h), dev(table.view(np.uint16), torch.float16), nw, eps, logits=logits)
+    torch.cuda.synchronize()
+    r = r.cpu().numpy().view(np.uint32)
+    return int(r[0]), float(r[1:2].view(np.float32)[0]), logits.cpu().numpy()
+
+
+def test_lm_head_argmax_config1():
+    table, x, eps = synth.lm_head_case()
+    ones = np.ones(1024, np.float32)
+    idx, val, logits = lm_head(table, x, ones, eps)
+    h = O.rms_norm(x, ones, eps)
+    want = O.lm_head_f16(h, table)
+    assert rel(logits, want) < TOL
+    oi, ov = O.argmax(want)
+    assert idx == oi
+    assert val == logits[idx]
+    # the winner must be clear of the numerical noise for an exact index match to mean anything
+    srt = np.sort(want)
+    assert srt[-1] - srt[-2] > 1e-4
+
+
+@pytest.mark.parametrize("case", ["all_ties", "last_wins", "dup_far_apart", "nan_row", "all_neg_inf"])
+def test_lm_head_argmax_adversarial(case):
+    V, H = 151936, 1024
+    h = np.ones(H, np.float32)
+    table = np.zeros((V, H), np.float16)
+    if case == "last_wins":
+        table[-1] = 1.0
+    elif case == "dup_far_apart":
+        table[[90001, 3, 151935, 77777]] = 0.5
+    elif case == "nan_row":
+        table[5] = np.nan
+        table[6] = 0.25
+    elif case == "all_neg_inf":
+        table[:] = -np.inf
+    idx, val, logits = lm_head(table, h)
+    want = {"all_ties": 0, "last_wins": V - 1, "dup_far_apart": 3, "nan_row": 6, "all_neg_inf": 0}[case]
+    assert idx == want
+    oi, ov = O.argmax(logits)
+    assert idx == oi and val == ov
+    if case == "all_neg_inf":
+        assert val == float(np.float32(-3.4028234e38))
+
+
+@pytest.mark.parametrize("seq", [1, 7, 128, 256, 257, 700, 2049])
+@pytest.mark.parametrize("kv", ["f16", "f32"])
+def test_gqa_decode_vs_oracle(seq, kv):
+    rng = np.random.default_rng(seq)
+    q = rng.standard_normal(16 * 128).astype(np.float32)
+    k = rng.standard_normal((seq, 8, 128)).astype(np.float32)
+    v = rng.standard_normal((seq, 8, 128)).astype(np.float32)
+    if kv == "f16":
+        k, v = k.astype(np.float16), v.astype(np.float16)
+    y = R.gqa_decode(dev(q), dev(k), dev(v), seq, 16, 8)
+    torch.cuda.synchronize()
+    want = O.gqa_decode(q, k.astype(np.float32), v.astype(np.float32), seq, 16, 8, 128)
+    assert rel(y.cpu().numpy(), want) < TOL
+
+
+def test_gqa_decode_matches_golden_js_port():
+    refs = np.load(os.path.join(GOLDEN, "js_cpu_refs.npz"))
+    cv = lambda n, step, fn: np.array([fn(i * step) for i in range(n)], np.float64).astype(np.float32)  # noqa
+    q = cv(16 * 128, 0.011, math.sin)
+    k = cv(128 * 8 * 128, 0.007, math.cos)
+    v = cv(128 * 8 * 128, 0.013, math.sin)
+    y = R.gqa_decode(dev(q), dev(k), dev(v), 128, 16, 8)
+    torch.cuda.synchronize()
+    assert rel(y.cpu().numpy(), refs["gqa_y"]) < TOL
+
+
+# ---- whole engine ---------------------------------------------------------------
+
+@pytest.fixture(scope="module")
+def tiny_model(tiny_runtime):
+    return O.Model(tiny_runtime)
+
+
+@pytest.mark.parametrize("kv", ["f16", "f32"])
+def test_engine_layer_trace_matches_oracle(tiny_runtime, tiny_model, kv):
+    with R.Engine(tiny_runtime, max_seq=64, kv_dtype=kv) as eng:
+        sess = tiny_model.session(max_seq=64, kv_f16=(kv == "f16"))
+        for pos, tok in enumerate([11, 4000, 7, 123]):
+            got = eng.forward_trace(tok, pos)
+            want = sess.forward(tok, pos, trace=True)
+            for layer in range(got.shape[0]):
+                assert rel(got[layer], want[layer]) < TOL, (pos, layer)
+
+
+@pytest.mark.parametrize("use_graph", [True, False])
+def test_engine_greedy_tiny_matches_oracle_f16_kv(tiny_runtime, tiny_model, use_graph):
+    with open(os.path.join(GOLDEN, "tiny_seed2_greedy.json")) as f:
+        g = json.load(f)
+    with R.Engine(tiny_runtime, max_seq=64, use_graph=use_graph) as eng:
+        ids, st = eng.generate_greedy(g["prompt"], g["max_new"])
+        want, margins = tiny_model.session(max_seq=64, kv_f16=True).greedy(g["prompt"], g["max_new"])
+        assert ids == want
+        assert st["generated_tokens"] == g["max_new"]
+
+
+def test_engine_greedy_tiny_f32_kv_matches_js_port_golden(tiny_runtime):
+    with open(os.path.join(GOLDEN, "tiny_seed2_greedy.json")) as f:
+        g = json.load(f)
+    with R.Engine(tiny_runtime, max_seq=64, kv_dtype="f32") as eng:
+        ids, _ = eng.generate_greedy(g["prompt"], 1)
+        first = np.load(os.path.join(GOLDEN, "tiny_seed2_first_logits.npy"))
+        assert rel(eng.logits(), first) < TOL
+        ids, _ = eng.generate_greedy(g["prompt"], g["max_new"])
+        assert ids == g["generated"]
+
+
+def test_engine_callback_order_and_early_stop(tiny_runtime):
+    seen = []
+    with R.Engine(tiny_runtime, max_seq=64) as eng:
+        full, _ = eng.generate_greedy([1, 2, 3], 10)
+        ids, st = eng.generate_greedy([1, 2, 3], 10, on_token=seen.append)
+        assert seen == ids == full
+        seen2 = []
+        ids2, _ = eng.generate_greedy([1, 2, 3], 10, on_token=lambda t: (seen2.append(t), len(seen2) < 4)[1])
+        assert ids2 == full[:4] and seen2 == full[:4]
+
+
+def test_engine_rejects_bad_requests(tiny_runtime):
+    with R.Engine(tiny_runtime, max_seq=16) as eng:
+        with pytest.raises(R.QdError) as ex:
+            eng.generate_greedy(list(range(10)), 8)          # 10 + 8 - 1 > 16
+        assert ex.value.code == -5
+        with pytest.raises(R.QdError):
+            eng.generate_greedy([synth.TINY.vocab], 1)        # id outside the vocabulary
+        ids, _ = eng.generate_greedy(list(range(10)), 7)      # exactly fits
+        assert len(ids) == 7
+
+
+def test_reference_api_mirror(tiny_runtime):
+    ctx = R.createWebGpuContext(tiny_runtime)
+    prof = dict(R.qwenProfile, hiddenSize=synth.TINY.hidden, intermediateSize=synth.TINY.intermediate,
+                attentionHeads=synth.TINY.heads, kvHeads=synth.TINY.kv_heads)
+    toks, progress = [], []
+    out = R.runCustomQwenGreedyPrompt(device=ctx["device"], profile=prof, inputIds=[5, 6, 7], maxNewTokens=4,
+                                      onToken=toks.append, onProgress=progress.append)
+    assert set(out) == {"generated", "generatedTokens", "generateMs", "firstTokenMs", "outputText"}
+    assert out["generatedTokens"] == 4 and toks == [str(t) for t in out["generated"]]
+    assert out["outputText"] == " ".join(toks) and out["firstTokenMs"] <= out["generateMs"]
+    ctx["device"].close()
+
+
+@pytest.fixture(scope="module")
+def qwen_runtime(tmp_path_factory):
+    d = str(tmp_path_factory.mktemp("qwen_seed2"))
+    synth.write_runtime(d, synth.QWEN3_0_6B, seed=2)
+    return d
+
+
+def test_engine_qwen_shape_greedy_config2(qwen_runtime):
+    """Config 2: 28 layers, 8 seeded prompt ids, 24 generated tokens, f16 KV."""
+    rng = np.random.Generator(np.random.PCG64(2))
+    prompt = rng.integers(0, 151936, size=8).tolist()
+    model = O.Model(qwen_runtime)
+    want, margins = model.session(max_seq=64, kv_f16=True).greedy(prompt, 24)
+    with R.Engine(qwen_runtime, max_seq=64) as eng:
+        ids, _ = eng.generate_greedy(prompt, 24)
+        assert ids == want, (ids, want, margins.tolist())
+        got_h = eng.forward_trace(want[-1], 8 + 23)[-1]
+    sess = model.session(max_seq=64, kv_f16=True)
+    for i, t in enumerate(prompt + want[:-1]):
+        sess.forward(t, i)
+    want_h = sess.forward(want[-1], 8 + 23, trace=True)[-1]
+    assert rel(got_h, want_h) < 1e-3
+
+
+def test_stepping_interface_matches_generate_and_flags_overrun(tiny_runtime):
+    prompt = [9, 8, 7, 6]
+    with R.Engine(tiny_runtime, max_seq=16) as eng:
+        want, _ = eng.generate_greedy(prompt, 6)
+        stream = torch.cuda.Stream()
+        eng.set_stream(stream)
+        eng.decode_begin(prompt, 6)
+        for _ in range(6):
+            eng.decode_step()
+        assert eng.decode_sync(6) == want
+        # replay from a seek: same positions, same tokens
+        eng.decode_seek(len(prompt) - 1)
+        for _ in range(6):
+            eng.decode_step()
+        eng.decode_sync(0)
+        # stepping past max_seq is caught on the device and reported, never out of bounds
+        eng.decode_begin(prompt, 6)
+        for _ in range(16):
+            eng.decode_step()
+        with pytest.raises(R.QdError) as ex:
+            eng.decode_sync(0)
+        assert ex.value.code == -6
+        eng.set_stream(None)
+        ids, _ = eng.generate_greedy(prompt, 6)   # the engine stays usable
+        assert ids == want
