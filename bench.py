@@ -207,12 +207,25 @@ def run_reference(args, world, rank):
 
 # ---- GPU arm --------------------------------------------------------------------------
 
+def _timed_chain(torch, stream, enqueue, n):
+    """Device time of n back-to-back launches: a sleep kernel holds the stream
+    while the host enqueues them, so host launch overhead cannot show up as gaps."""
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        torch.cuda._sleep(50_000_000)
+        e0.record(stream)
+        for i in range(n):
+            enqueue(i)
+        e1.record(stream)
+    e1.synchronize()
+    return e0.elapsed_time(e1) / 1000.0 / n
+
+
 def kernel_rooflines(torch, R, peak):
-    """q4 matvec (gate 1024->3072, 128 distinct weight copies, 228 MB > L2) and the LM head
-    (311 MB table per launch), each launched back to back inside one CUDA graph."""
+    """q4 matvec (gate 1024->3072, 128 distinct weight copies = 228 MB > L2) and the LM head
+    (311 MB table per launch), each timed over back-to-back launches."""
     out = {}
     stream = torch.cuda.Stream()
-    # q4 matvec, gate shape
     x, w, s = synth.matvec_case(3072, 1024, seed=0)
     copies = 128
     xs = torch.from_numpy(x).cuda()
@@ -222,29 +235,14 @@ def kernel_rooflines(torch, R, peak):
     scs = [sd.clone() for _ in range(copies)]
     ys = torch.empty(copies, 3072, device="cuda")
     per = 4 * 1024 + 3072 * 1024 // 2 + 3072 * 32 * 2 + 3072 * 4
-    with torch.cuda.stream(stream):
-        for i in range(copies):
-            R.q4_matvec(xs, wcs[i], scs[i], ys[i], stream=stream)
-    g = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g, stream=stream):
-        for i in range(copies):
-            R.q4_matvec(xs, wcs[i], scs[i], ys[i], stream=stream)
-    for _ in range(3):
-        g.replay()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    reps = 20
-    e0.record(stream)
-    for _ in range(reps):
-        g.replay()
-    e1.record(stream)
-    e1.synchronize()
-    t = e0.elapsed_time(e1) / 1000.0 / (reps * copies)
+    run = lambda i: R.q4_matvec(xs, wcs[i % copies], scs[i % copies], ys[i % copies], stream=stream)  # noqa: E731
+    _timed_chain(torch, stream, run, copies)
+    t = _timed_chain(torch, stream, run, 4 * copies)
     out["q4_matvec_gate_1024x3072"] = {"us_per_launch": round(t * 1e6, 3), "bytes": per,
                                        "achieved_gbs": round(per / t / 1e9, 1),
-                                       "frac": round(per / t / 1e9 / peak, 4)}
-    del g, wcs, scs
-    # LM head + argmax
+                                       "frac": round(per / t / 1e9 / peak, 4),
+                                       "note": "isolated launches back to back (PDL), distinct weights"}
+    del wcs, scs
     table, xh, eps = synth.lm_head_case()
     tb = torch.from_numpy(table.view(np.uint16)).cuda().view(torch.float16)
     xd = torch.from_numpy(xh).cuda()
@@ -253,17 +251,9 @@ def kernel_rooflines(torch, R, peak):
     ws = R.LmHeadWorkspace(151936, "cuda")
     res = torch.zeros(2, dtype=torch.int32, device="cuda")
     per = 151936 * 1024 * 2 + 1024 * 4 * 2 + 151936 * 4 + 8
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with torch.cuda.stream(stream):
-        for _ in range(3):
-            R.lm_head_argmax(xd, tb, nw, eps, logits, ws, res, stream=stream)
-        e0.record(stream)
-        n = 30
-        for _ in range(n):
-            R.lm_head_argmax(xd, tb, nw, eps, logits, ws, res, stream=stream)
-        e1.record(stream)
-    e1.synchronize()
-    t = e0.elapsed_time(e1) / 1000.0 / n
+    run = lambda i: R.lm_head_argmax(xd, tb, nw, eps, logits, ws, res, stream=stream)  # noqa: E731
+    _timed_chain(torch, stream, run, 3)
+    t = _timed_chain(torch, stream, run, 30)
     out["lm_head_argmax_151936x1024"] = {"us_per_launch": round(t * 1e6, 3), "bytes": per,
                                          "achieved_gbs": round(per / t / 1e9, 1),
                                          "frac": round(per / t / 1e9 / peak, 4)}
@@ -302,6 +292,8 @@ def run_ours(args, world, rank, local):
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
+        with torch.cuda.stream(stream):
+            torch.cuda._sleep(20_000_000)
         e0.record(stream)
         for _ in range(args.steps):
             if pos_in_cycle == cycle:
@@ -322,6 +314,12 @@ def run_ours(args, world, rank, local):
     ms_per_step = t_max * 1000.0 / args.steps
     bytes_avg = sum(token_bytes(shape, p) for p in positions) / len(positions)
     achieved = bytes_avg / (t_local / args.steps) / 1e9
+
+    if args.decode_only:
+        eng.close()
+        if rank == 0:
+            print(json.dumps({"decode_only": True, "tok_s": round(value, 2), "ms_per_step": ms_per_step}))
+        return 0
 
     # e2e: the public C-ABI call with host buffers (prompt in, generated ids out)
     n_e2e = max(1, args.steps // NEW_TOKENS)
@@ -386,6 +384,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-steps", type=int, default=24)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--decode-only", action="store_true",
+                    help="prefill + warm-up + timed decode steps only (for profiler launch lists)")
     args = ap.parse_args()
     world, rank, local = dist_setup()
     try:
