@@ -131,6 +131,34 @@ int qd_gqa_decode(const float* q, const void* k_cache, const void* v_cache, int 
                   uint32_t seq_len, uint32_t q_heads, uint32_t kv_heads, uint32_t head_dim,
                   void* workspace, void* stream);
 
+/* ---- decode attention without device allocation ---------------------------- */
+
+/* Bytes of the fixed device array that qd_gqa_decode_noalloc keeps its scratch in
+ * (512 KiB: split-KV partials for 16 query heads up to 16128 positions). */
+#define QD_NOALLOC_SCRATCH_BYTES (512u * 1024u)
+
+/* No counterpart in the reference: its WebGPU runtime allocates every buffer up
+ * front and never frees one. This is qd_gqa_decode for callers that cannot
+ * allocate device memory when they call: a host whose own pool takes all device
+ * memory at start-up and forbids driver allocations afterwards, or a
+ * latency-critical loop that cannot take the device-wide synchronisation a
+ * cudaFree may cause. Same arguments and results as qd_gqa_decode, minus the
+ * workspace: the split-KV partials live in one array of QD_NOALLOC_SCRATCH_BYTES
+ * in device global memory owned by the library, which every GPU that loads the
+ * library holds until the process exits. The call allocates and frees nothing.
+ *  - Sizes whose partials do not fit (ceil(seq_len/256) * q_heads * 520 bytes,
+ *    about) are rejected with QD_E_RANGE; use qd_gqa_decode for those.
+ *  - The first call on each device looks up that array's device address (a CUDA
+ *    symbol query, with the device current); make that first call before any
+ *    stream capture begins.
+ *  - All calls on a device share the one array and it keeps the last call's
+ *    contents. Nothing in it needs to start at zero: each call writes every
+ *    partial it reads. Calls whose kernels overlap on the GPU (other streams,
+ *    other host threads) race on it: order them on one stream or serialise them. */
+int qd_gqa_decode_noalloc(const float* q, const void* k_cache, const void* v_cache, int kv_dtype,
+                          float* y, uint32_t seq_len, uint32_t q_heads, uint32_t kv_heads,
+                          uint32_t head_dim, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

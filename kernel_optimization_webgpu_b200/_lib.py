@@ -27,7 +27,7 @@ EXPORTS = (
     "qd_engine_forward_trace", "qd_q4_matvec", "qd_lm_head_argmax_workspace_bytes",
     "qd_lm_head_argmax", "qd_gqa_decode_workspace_bytes", "qd_gqa_decode",
     "qd_engine_set_stream", "qd_decode_begin", "qd_decode_step", "qd_decode_seek", "qd_decode_sync",
-    "qd_decode_step_kernels",
+    "qd_decode_step_kernels", "qd_gqa_decode_noalloc",
 )
 
 
@@ -115,6 +115,8 @@ def load(build_if_stale: bool = True):
     L.qd_gqa_decode_workspace_bytes.restype = C.c_size_t
     L.qd_gqa_decode.argtypes = [vp, vp, vp, i32, vp, u32, u32, u32, u32, vp, vp]
     L.qd_gqa_decode.restype = i32
+    L.qd_gqa_decode_noalloc.argtypes = [vp, vp, vp, i32, vp, u32, u32, u32, u32, vp]
+    L.qd_gqa_decode_noalloc.restype = i32
     _lib = L
     return L
 

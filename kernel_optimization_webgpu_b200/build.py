@@ -14,8 +14,8 @@ PKG = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
 LIB = os.path.join(PKG, "libqdecode.so")
-SOURCES = ["engine.cu"]
-DEPS = ["engine.cu", "kernels.cuh", "common.cuh", "json.hpp"]
+SOURCES = ["engine.cu", "noalloc.cu"]
+DEPS = ["engine.cu", "noalloc.cu", "kernels.cuh", "common.cuh", "json.hpp"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

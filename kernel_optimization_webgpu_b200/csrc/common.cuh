@@ -5,7 +5,12 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <string>
+
 namespace qd {
+
+// Sets the message qd_last_error(NULL) returns on this thread (defined in engine.cu).
+void set_thread_error(const std::string& msg);
 
 constexpr int kThreads = 256;                 // every decode kernel runs 8 warps
 constexpr int kWarps = kThreads / 32;

@@ -154,6 +154,11 @@ uint16_t f2h(float f) {
 
 }  // namespace
 
+namespace qd {
+// Lets other translation units of the library report through qd_last_error(NULL).
+void set_thread_error(const std::string& msg) { t_last_error = msg; }
+}  // namespace qd
+
 // ---------------------------------------------------------------------------
 struct LayerDev {
   const uint4 *w_qkv, *w_o, *w_gu, *w_d;

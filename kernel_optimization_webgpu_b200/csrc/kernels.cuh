@@ -353,7 +353,7 @@ __global__ void __launch_bounds__(kThreads, 2) k_attn(const AttnArgs a) {
 }
 
 // Standalone split combine (the engine fuses this into the O projection).
-__global__ void __launch_bounds__(kThreads) k_attn_combine(const float2* part_ml, const float* part_o,
+static __global__ void __launch_bounds__(kThreads) k_attn_combine(const float2* part_ml, const float* part_o,
                                                             int splits, int q_heads, float* y) {
   pdl_trigger();
   pdl_wait();
@@ -527,13 +527,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_lmhead(const LmArgs a) {
 }
 
 // Move the decode position (stepping interface); keeps the step counter.
-__global__ void k_seek(DevState* st, int pos) {
+static __global__ void k_seek(DevState* st, int pos) {
   pdl_wait();
   if (threadIdx.x == 0 && blockIdx.x == 0) st->pos = pos;
 }
 
 // Advance the position after a prompt token that needs no LM head.
-__global__ void k_advance(DevState* st) {
+static __global__ void k_advance(DevState* st) {
   pdl_wait();
   if (threadIdx.x == 0 && blockIdx.x == 0) st->pos += 1;
 }
