@@ -37,6 +37,7 @@ extern "C" {
 #define QD_E_NOMEM (-4)       /* device or pinned allocation failed */
 #define QD_E_RANGE (-5)       /* prompt + generation beyond max_seq, token id beyond vocab */
 #define QD_E_DEVICE (-6)      /* a kernel flagged a bad token or position (status word) */
+#define QD_E_TIMEOUT (-7)     /* a device-side wait expired; the launch was abandoned */
 
 #define QD_KV_F16 0           /* f16 KV cache (default) */
 #define QD_KV_F32 1           /* f32 KV cache, as the reference (cache_write.wgsl) */
@@ -50,6 +51,9 @@ typedef struct qd_options {
   int rope_row_stride;   /* cos/sin offset = position * stride + pair; 0 = head_dim (reference) */
   const char* variant;   /* "optimized" | "mixed" | "original": accepted, one B200 path */
   int use_graph;         /* 1 (default): each token is one CUDA graph launch */
+  int persistent;        /* 1 (default): one persistent kernel per token where the shape allows;
+                            0: one kernel per fused stage */
+  int timeline;          /* 1: record per-CTA stage timestamps of each persistent launch */
 } qd_options;
 
 typedef struct qd_profile {
@@ -86,6 +90,14 @@ int qd_generate_greedy(qd_engine* e, const int32_t* input_ids, int n_prompt, int
 /* Parity and inspection helpers. */
 int qd_engine_logits(qd_engine* e, float* host_logits);       /* logits of the last generated step */
 int qd_engine_hidden(qd_engine* e, float* host_hidden);       /* residual stream after the last layer */
+int qd_engine_uses_persistent(const qd_engine* e);            /* 1 if tokens run as one persistent kernel */
+/* Stage timestamps (ns, globaltimer) of the last persistent launch: host_out[cta][event]
+ * (needs qd_options.timeline = 1). Event order per CTA: start; per layer 14 events (QKV
+ * input ready, QKV weights ready, QKV stored, attention done, O input ready, O stored,
+ * gate/up input ready, gate/up stored, down input ready, down stored, QKV norm done, O
+ * weights ready, gate/up norm done, down weights ready); LM-head input ready, LM head
+ * done, merged (last CTA only). Pass host_out NULL to query the sizes. */
+int qd_engine_timeline(qd_engine* e, uint64_t* host_out, int* ctas, int* events_per_cta);
 /* One token through the layers at `position` (no LM head), with the residual
  * stream after every layer copied to host_trace[layers][hidden]. */
 int qd_engine_forward_trace(qd_engine* e, int32_t token, int position, float* host_trace);

@@ -17,6 +17,7 @@ QD_E_CUDA = -3
 QD_E_NOMEM = -4
 QD_E_RANGE = -5
 QD_E_DEVICE = -6
+QD_E_TIMEOUT = -7
 QD_KV_F16 = 0
 QD_KV_F32 = 1
 
@@ -24,7 +25,7 @@ QD_KV_F32 = 1
 EXPORTS = (
     "qd_options_default", "qd_engine_create", "qd_engine_destroy", "qd_last_error",
     "qd_engine_profile", "qd_generate_greedy", "qd_engine_logits", "qd_engine_hidden",
-    "qd_engine_forward_trace", "qd_q4_matvec", "qd_lm_head_argmax_workspace_bytes",
+    "qd_engine_forward_trace", "qd_engine_uses_persistent", "qd_engine_timeline", "qd_q4_matvec", "qd_lm_head_argmax_workspace_bytes",
     "qd_lm_head_argmax", "qd_gqa_decode_workspace_bytes", "qd_gqa_decode",
     "qd_engine_set_stream", "qd_decode_begin", "qd_decode_step", "qd_decode_seek", "qd_decode_sync",
     "qd_decode_step_kernels", "qd_gqa_decode_noalloc",
@@ -33,7 +34,8 @@ EXPORTS = (
 
 class QdOptions(C.Structure):
     _fields_ = [("device", C.c_int), ("max_seq", C.c_int), ("kv_dtype", C.c_int),
-                ("rope_row_stride", C.c_int), ("variant", C.c_char_p), ("use_graph", C.c_int)]
+                ("rope_row_stride", C.c_int), ("variant", C.c_char_p), ("use_graph", C.c_int),
+                ("persistent", C.c_int), ("timeline", C.c_int)]
 
 
 class QdProfile(C.Structure):
@@ -93,6 +95,10 @@ def load(build_if_stale: bool = True):
     L.qd_engine_hidden.restype = i32
     L.qd_engine_forward_trace.argtypes = [vp, C.c_int32, i32, vp]
     L.qd_engine_forward_trace.restype = i32
+    L.qd_engine_uses_persistent.argtypes = [vp]
+    L.qd_engine_uses_persistent.restype = i32
+    L.qd_engine_timeline.argtypes = [vp, vp, C.POINTER(C.c_int), C.POINTER(C.c_int)]
+    L.qd_engine_timeline.restype = i32
     L.qd_engine_set_stream.argtypes = [vp, vp]
     L.qd_engine_set_stream.restype = i32
     L.qd_decode_begin.argtypes = [vp, vp, i32, i32]

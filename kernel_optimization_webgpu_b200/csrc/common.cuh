@@ -31,6 +31,9 @@ struct DevState {
   int step;           // index of the next generated token
   int max_new;        // generated tokens requested
   int err;            // DevErr bits
+  // Below: owned by the device (the host only repairs them after a failure).
+  int epoch;          // launches of the persistent decode kernel so far (exchange-word tag)
+  int abort;          // set by a persistent kernel whose wait expired
 };
 
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }

@@ -1,7 +1,9 @@
 // qdecode engine: loads the reference's runtime directory, keeps every weight
 // resident in HBM, captures one token (all layers, plus LM head + argmax) as a
 // CUDA graph and runs the reference's greedy flow (webgpu-runtime.js:165-214).
+#include <algorithm>
 #include <chrono>
+#include <cstddef>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -13,6 +15,7 @@
 #include "../../include/qdecode.h"
 #include "json.hpp"
 #include "kernels.cuh"
+#include "persist.cuh"
 
 using namespace qd;
 
@@ -160,9 +163,16 @@ void set_thread_error(const std::string& msg) { t_last_error = msg; }
 }  // namespace qd
 
 // ---------------------------------------------------------------------------
+// Bytes of one q4 row record: nb 16-byte blocks then nb f16 scales, padded to 16.
+inline long long rec_bytes(int k) {
+  const long long nb = k / kBlockCols;
+  return (nb * 16 + nb * 2 + 15) / 16 * 16;
+}
+
+// Per layer, each matrix is an array of row records (gate/up: pair records
+// [gate row | up row]); a run of rows is one contiguous range of bytes.
 struct LayerDev {
-  const uint4 *w_qkv, *w_o, *w_gu, *w_d;
-  const __half *s_qkv, *s_o, *s_gu, *s_d;
+  const char *qkv, *o, *gu, *d;
   const float *n_in, *n_q, *n_k, *n_post;
   void *kc, *vc;
 };
@@ -197,6 +207,14 @@ struct qd_engine {
   DevState* pinned_state = nullptr;
   cudaGraphExec_t g_layers = nullptr, g_full = nullptr;
   cudaEvent_t ev[2] = {nullptr, nullptr};
+  // persistent decode kernel
+  bool persist = false;
+  PLayer* d_players = nullptr;
+  unsigned long long* xbuf = nullptr;
+  long long xstride = 0;
+  size_t persist_smem = 0;
+  int lm_rows = 0;
+  unsigned long long* timeline = nullptr;  // stage stamps of the last persistent launch (opt-in)
 };
 
 namespace {
@@ -210,6 +228,14 @@ struct Arena {
   }
 };
 
+void set_rows(StageArgs& a, const char* base, int k, bool pairs) {
+  const long long rec = rec_bytes(k), nb = k / kBlockCols;
+  a.w = base;
+  a.s = base + nb * 16;
+  a.w_stride = a.s_stride = pairs ? 2 * rec : rec;
+  a.w_sub = a.s_sub = pairs ? rec : 0;
+}
+
 void enqueue_layer(qd_engine* e, int l, cudaStream_t s) {
   const qd_profile& p = e->p;
   const LayerDev& L = e->layers[l];
@@ -217,7 +243,8 @@ void enqueue_layer(qd_engine* e, int l, cudaStream_t s) {
   // 1. RMSNorm + fused QKV projection (layer 0 gathers the embedding row on device).
   {
     StageArgs a{};
-    a.w = L.w_qkv; a.s = L.s_qkv; a.rows = e->rows_qkv; a.nb = p.hidden / kBlockCols; a.k_valid = p.hidden;
+    set_rows(a, L.qkv, p.hidden, false);
+    a.rows = e->rows_qkv; a.nb = p.hidden / kBlockCols; a.k_valid = p.hidden;
     a.src = e->h; a.norm_w = L.n_in; a.eps = p.eps; a.out = e->qkv;
     const StagePlan sp = plan_stage(a.rows, a.nb, e->sms);
     if (l == 0) {
@@ -242,7 +269,8 @@ void enqueue_layer(qd_engine* e, int l, cudaStream_t s) {
   // 3. Split combine + O projection + residual.
   {
     StageArgs a{};
-    a.w = L.w_o; a.s = L.s_o; a.rows = p.hidden; a.nb = qsize / kBlockCols; a.k_valid = qsize;
+    set_rows(a, L.o, qsize, false);
+    a.rows = p.hidden; a.nb = qsize / kBlockCols; a.k_valid = qsize;
     a.res = e->h; a.out = e->h_attn;
     a.part_ml = e->part_ml; a.part_o = e->part_o; a.splits = e->splits; a.q_heads = p.heads;
     launch_stage<kProCombine, kEpiResidual>(a, plan_stage(a.rows, a.nb, e->sms), s);
@@ -250,14 +278,16 @@ void enqueue_layer(qd_engine* e, int l, cudaStream_t s) {
   // 4. Post-attention RMSNorm + gate/up + silu_mul.
   {
     StageArgs a{};
-    a.w = L.w_gu; a.s = L.s_gu; a.rows = p.intermediate; a.nb = p.hidden / kBlockCols; a.k_valid = p.hidden;
+    set_rows(a, L.gu, p.hidden, true);
+    a.rows = p.intermediate; a.nb = p.hidden / kBlockCols; a.k_valid = p.hidden;
     a.src = e->h_attn; a.norm_w = L.n_post; a.eps = p.eps; a.out = e->act;
     launch_stage<kProRms, kEpiSilu>(a, plan_stage(a.rows, a.nb, e->sms, 2), s);
   }
   // 5. Down projection + residual into the stream state.
   {
     StageArgs a{};
-    a.w = L.w_d; a.s = L.s_d; a.rows = p.hidden; a.nb = p.intermediate / kBlockCols; a.k_valid = p.intermediate;
+    set_rows(a, L.d, p.intermediate, false);
+    a.rows = p.hidden; a.nb = p.intermediate / kBlockCols; a.k_valid = p.intermediate;
     a.src = e->act; a.res = e->h_attn; a.out = e->h;
     launch_stage<kProPlain, kEpiResidual>(a, plan_stage(a.rows, a.nb, e->sms), s);
   }
@@ -273,7 +303,111 @@ void enqueue_lmhead(qd_engine* e, cudaStream_t s) {
   launch_lmhead(a, e->lm_grid, s);
 }
 
+template <int G, typename KVT>
+void launch_persist_t(qd_engine* e, const PArgs& a, cudaStream_t s) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(e->sms);
+  cfg.blockDim = dim3(kPT);
+  cfg.dynamicSmemBytes = e->persist_smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;  // every CTA resident: they exchange data
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  QD_CK(cudaLaunchKernelEx(&cfg, k_decode_persistent<G, KVT>, a));
+}
+
+PArgs persist_args(qd_engine* e, bool with_head) {
+  const qd_profile& p = e->p;
+  PArgs a{};
+  a.layers = e->d_players;
+  a.L = p.layers; a.H = p.hidden; a.I = p.intermediate; a.NH = p.heads; a.NKV = p.kv_heads;
+  a.vocab = p.vocab; a.max_seq = e->opt.max_seq; a.row_stride = e->opt.rope_row_stride;
+  a.eps = p.eps; a.scale = 1.0f / std::sqrt((float)kHeadDim);
+  a.embed = e->embed; a.cos_t = e->cos_t; a.sin_t = e->sin_t; a.final_norm = e->final_norm;
+  a.xb = e->xbuf; a.xstride = e->xstride; a.st = e->st;
+  a.tokens = e->tokens; a.out_dev = e->out_dev; a.out_host = e->out_host_dev;
+  a.logits = e->logits; a.part_v = e->lm_pv; a.part_i = e->lm_pi; a.counter = e->lm_counter;
+  a.with_head = with_head ? 1 : 0; a.lm_rows = e->lm_rows; a.timeline = e->timeline;
+  a.rec_h = rec_bytes(p.hidden); a.rec_q = rec_bytes(p.heads * kHeadDim); a.rec_i = rec_bytes(p.intermediate);
+  return a;
+}
+
+void launch_persist(qd_engine* e, bool with_head, cudaStream_t s) {
+  const PArgs a = persist_args(e, with_head);
+  const int group = e->p.heads / e->p.kv_heads;
+  if (e->opt.kv_dtype == QD_KV_F32) {
+    if (group == 1) launch_persist_t<1, float>(e, a, s); else launch_persist_t<2, float>(e, a, s);
+  } else {
+    if (group == 1) launch_persist_t<1, __half>(e, a, s); else launch_persist_t<2, __half>(e, a, s);
+  }
+}
+
+template <int G, typename KVT>
+cudaError_t prepare_persist_t(size_t smem, int* blocks) {
+  cudaError_t rc = cudaFuncSetAttribute(k_decode_persistent<G, KVT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (rc != cudaSuccess) return rc;
+  return cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks, k_decode_persistent<G, KVT>, kPT, smem);
+}
+
+// Decide whether the persistent kernel fits this shape and device; set it up if so.
+void setup_persist(qd_engine* e) {
+  const qd_profile& p = e->p;
+  const int G = p.heads / p.kv_heads, H = p.hidden, I = p.intermediate, QS = p.heads * kHeadDim;
+  const int R = QS + 2 * p.kv_heads * kHeadDim, g = e->sms;
+  auto per_cta = [g](long long n, long long bytes) { return (n + g - 1) / g * bytes; };
+  int coop = 0, optin = 0;
+  cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, e->dev);
+  cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, e->dev);
+  const long long rec_h = rec_bytes(H), rec_q = rec_bytes(QS), rec_i = rec_bytes(I);
+  bool ok = e->opt.persistent && coop && G <= 2 && H <= 1024 && QS <= 2048 && I <= 3072 && p.kv_heads <= g &&
+            per_cta(R, rec_h) <= kSlotBytes && per_cta(H, rec_q) <= kSlotBytes &&
+            per_cta(I, 2 * rec_h) <= kSlotBytes && per_cta(H, rec_i) <= kSlotBytes && 2LL * H <= kSlotBytes;
+  if (!ok) return;
+  const int maxk = std::max(std::max(H, QS), I);
+  const long long xs_floats = std::max<long long>(maxk, (long long)kPW * G * kHeadDim);
+  const long long misc_floats = std::max<long long>((G + 2) * kHeadDim + G * kHeadDim + 2 * kHeadDim + 2 * kPW * G, 2 * kPW);
+  const size_t smem = (size_t)kSlots * kSlotBytes + (size_t)(xs_floats + 2 * H) * 4 + kSlots * 8 + kPW * 4 + 16 +
+                      (size_t)(kMaxRes + misc_floats) * 4;
+  // per-CTA row counts must fit the stage result buffer
+  if (per_cta(R, 1) > kMaxRes || 2 * per_cta(I, 1) > kMaxRes || 3 * per_cta(H, 1) > kMaxRes) return;
+  if ((long long)smem > optin) return;
+  int blocks = 0;
+  const cudaError_t rc = e->opt.kv_dtype == QD_KV_F32
+                             ? (G == 1 ? prepare_persist_t<1, float>(smem, &blocks) : prepare_persist_t<2, float>(smem, &blocks))
+                             : (G == 1 ? prepare_persist_t<1, __half>(smem, &blocks) : prepare_persist_t<2, __half>(smem, &blocks));
+  if (rc != cudaSuccess || blocks < 1) {
+    cudaGetLastError();
+    return;
+  }
+  e->persist_smem = smem;
+  e->lm_rows = kSlotBytes / (2 * H);
+  e->xstride = (long long)H + R + QS + H + I;
+  const size_t xbytes = (size_t)(p.layers + 1) * e->xstride * 8;
+  if (cudaMalloc(&e->xbuf, xbytes) != cudaSuccess) throw QdError{QD_E_NOMEM, "cannot allocate exchange buffers"};
+  QD_CK(cudaMemset(e->xbuf, 0, xbytes));
+  std::vector<PLayer> pl(p.layers);
+  for (int l = 0; l < p.layers; ++l) {
+    const LayerDev& L = e->layers[l];
+    pl[l] = PLayer{L.qkv, L.o, L.gu, L.d, L.n_in, L.n_q, L.n_k, L.n_post, L.kc, L.vc};
+  }
+  if (cudaMalloc(&e->d_players, sizeof(PLayer) * p.layers) != cudaSuccess)
+    throw QdError{QD_E_NOMEM, "cannot allocate the layer table"};
+  QD_CK(cudaMemcpy(e->d_players, pl.data(), sizeof(PLayer) * p.layers, cudaMemcpyHostToDevice));
+  if (e->opt.timeline) {
+    const size_t tb = (size_t)e->sms * timeline_events(p.layers) * 8;
+    if (cudaMalloc(&e->timeline, tb) != cudaSuccess) throw QdError{QD_E_NOMEM, "cannot allocate the timeline"};
+    QD_CK(cudaMemset(e->timeline, 0, tb));
+  }
+  e->persist = true;
+}
+
 void enqueue_token(qd_engine* e, bool with_head, cudaStream_t s) {
+  if (e->persist) {
+    launch_persist(e, with_head, s);
+    return;
+  }
   for (int l = 0; l < e->p.layers; ++l) enqueue_layer(e, l, s);
   if (with_head) enqueue_lmhead(e, s);
   else launch(k_advance, dim3(1), s, e->st);
@@ -380,7 +514,6 @@ void load_engine(qd_engine* e, const std::string& dir, const Json& m) {
   const qd_options& o = e->opt;
   const int H = p.hidden, I = p.intermediate, QS = p.heads * kHeadDim, KV = p.kv_heads * kHeadDim;
   e->rows_qkv = QS + 2 * KV;
-  const int nb_h = H / kBlockCols, nb_q = QS / kBlockCols, nb_i = I / kBlockCols;
   const int half = p.head_dim / 2;
 
   // Offsets in one weight arena.
@@ -389,17 +522,14 @@ void load_engine(qd_engine* e, const std::string& dir, const Json& m) {
   const size_t o_cos = ar.take((size_t)p.rope_rows * half * 4);
   const size_t o_sin = ar.take((size_t)p.rope_rows * half * 4);
   const size_t o_fn = ar.take((size_t)H * 4);
-  struct LOff { size_t w_qkv, s_qkv, w_o, s_o, w_gu, s_gu, w_d, s_d, n_in, n_q, n_k, n_post; };
+  struct LOff { size_t qkv, o, gu, d, n_in, n_q, n_k, n_post; };
+  const long long rec_h = rec_bytes(H), rec_q = rec_bytes(QS), rec_i = rec_bytes(I);
   std::vector<LOff> lo(p.layers);
   for (int l = 0; l < p.layers; ++l) {
-    lo[l].w_qkv = ar.take((size_t)e->rows_qkv * nb_h * 16);
-    lo[l].s_qkv = ar.take((size_t)e->rows_qkv * nb_h * 2);
-    lo[l].w_o = ar.take((size_t)H * nb_q * 16);
-    lo[l].s_o = ar.take((size_t)H * nb_q * 2);
-    lo[l].w_gu = ar.take((size_t)2 * I * nb_h * 16);
-    lo[l].s_gu = ar.take((size_t)2 * I * nb_h * 2);
-    lo[l].w_d = ar.take((size_t)H * nb_i * 16);
-    lo[l].s_d = ar.take((size_t)H * nb_i * 2);
+    lo[l].qkv = ar.take((size_t)e->rows_qkv * rec_h);
+    lo[l].o = ar.take((size_t)H * rec_q);
+    lo[l].gu = ar.take((size_t)2 * I * rec_h);
+    lo[l].d = ar.take((size_t)H * rec_i);
     lo[l].n_in = ar.take((size_t)H * 4);
     lo[l].n_q = ar.take(kHeadDim * 4);
     lo[l].n_k = ar.take(kHeadDim * 4);
@@ -448,26 +578,40 @@ void load_engine(qd_engine* e, const std::string& dir, const Json& m) {
       // Row offsets of each projection inside the fused device matrices.
       const int out_sz[7] = {QS, KV, KV, H, I, I, H};
       const int in_sz[7] = {H, H, H, QS, H, H, I};
-      const size_t w_base[7] = {lo[l].w_qkv, lo[l].w_qkv, lo[l].w_qkv, lo[l].w_o, lo[l].w_gu, lo[l].w_gu, lo[l].w_d};
-      const size_t s_base[7] = {lo[l].s_qkv, lo[l].s_qkv, lo[l].s_qkv, lo[l].s_o, lo[l].s_gu, lo[l].s_gu, lo[l].s_d};
-      const int row0[7] = {0, QS, QS + KV, 0, 0, I, 0};
+      // Record placement: (first record, record stride, offset inside the record).
+      const long long rec[7] = {rec_h, rec_h, rec_h, rec_q, rec_h, rec_h, rec_i};
+      const long long stride[7] = {rec_h, rec_h, rec_h, rec_q, 2 * rec_h, 2 * rec_h, rec_i};
+      const long long first[7] = {0, (long long)QS * rec_h, (long long)(QS + KV) * rec_h, 0, 0, rec_h, 0};
+      // Host staging of the four record matrices of this layer.
+      const size_t m_bytes[4] = {(size_t)e->rows_qkv * rec_h, (size_t)H * rec_q, (size_t)2 * I * rec_h,
+                                 (size_t)H * rec_i};
+      const int m_of[7] = {0, 0, 0, 1, 2, 2, 3};
+      std::vector<char> mats[4];
+      for (int k = 0; k < 4; ++k) mats[k].assign(m_bytes[k], 0);
       for (int j = 0; j < 7; ++j) {
         const Json& pj = le.at("projections").at(kProj[j]);
         const int outS = out_sz[j], bpr = in_sz[j] / kBlockCols;  // validated by parse_manifest
         auto wb = read_file(file(pj.at("weight")), (size_t)outS * bpr * 16);
-        up(w_base[j] + (size_t)row0[j] * bpr * 16, wb.data(), wb.size());
         auto sb = read_file(file(pj.at("scales")), (size_t)outS * bpr * 4);
         const float* sf = reinterpret_cast<const float*>(sb.data());
-        std::vector<uint16_t> sh(sb.size() / 4);
-        for (size_t i = 0; i < sh.size(); ++i) {
-          sh[i] = f2h(sf[i]);
-          const float back = h2f(sh[i]);
-          if (!(back == sf[i]) && !(std::isnan(back) && std::isnan(sf[i])))
-            throw QdError{QD_E_IO, std::string("layer ") + std::to_string(l) + " " + kProj[j] +
-                                       ": a block scale is not an f16 value (the q4f16 format stores f16 scales)"};
+        char* dst0 = mats[m_of[j]].data() + first[j];
+        for (int r = 0; r < outS; ++r) {
+          char* dst = dst0 + (size_t)r * stride[j];
+          std::memcpy(dst, wb.data() + (size_t)r * bpr * 16, (size_t)bpr * 16);
+          uint16_t* sc = reinterpret_cast<uint16_t*>(dst + (size_t)bpr * 16);
+          for (int b = 0; b < bpr; ++b) {
+            const float v = sf[(size_t)r * bpr + b];
+            sc[b] = f2h(v);
+            const float back = h2f(sc[b]);
+            if (!(back == v) && !(std::isnan(back) && std::isnan(v)))
+              throw QdError{QD_E_IO, std::string("layer ") + std::to_string(l) + " " + kProj[j] +
+                                         ": a block scale is not an f16 value (the q4f16 format stores f16 scales)"};
+          }
         }
-        up(s_base[j] + (size_t)row0[j] * bpr * 2, sh.data(), sh.size() * 2);
+        (void)rec;
       }
+      const size_t m_off[4] = {lo[l].qkv, lo[l].o, lo[l].gu, lo[l].d};
+      for (int k = 0; k < 4; ++k) up(m_off[k], mats[k].data(), m_bytes[k]);
     }
   } catch (const std::runtime_error& ex) {
     throw QdError{QD_E_IO, ex.what()};
@@ -487,14 +631,10 @@ void load_engine(qd_engine* e, const std::string& dir, const Json& m) {
   QD_CK(cudaMemset(e->kv, 0, kv_layer * 2 * p.layers));
   for (int l = 0; l < p.layers; ++l) {
     LayerDev& L = e->layers[l];
-    L.w_qkv = reinterpret_cast<const uint4*>(base + lo[l].w_qkv);
-    L.s_qkv = reinterpret_cast<const __half*>(base + lo[l].s_qkv);
-    L.w_o = reinterpret_cast<const uint4*>(base + lo[l].w_o);
-    L.s_o = reinterpret_cast<const __half*>(base + lo[l].s_o);
-    L.w_gu = reinterpret_cast<const uint4*>(base + lo[l].w_gu);
-    L.s_gu = reinterpret_cast<const __half*>(base + lo[l].s_gu);
-    L.w_d = reinterpret_cast<const uint4*>(base + lo[l].w_d);
-    L.s_d = reinterpret_cast<const __half*>(base + lo[l].s_d);
+    L.qkv = base + lo[l].qkv;
+    L.o = base + lo[l].o;
+    L.gu = base + lo[l].gu;
+    L.d = base + lo[l].d;
     L.n_in = reinterpret_cast<const float*>(base + lo[l].n_in);
     L.n_q = reinterpret_cast<const float*>(base + lo[l].n_q);
     L.n_k = reinterpret_cast<const float*>(base + lo[l].n_k);
@@ -539,6 +679,7 @@ void load_engine(qd_engine* e, const std::string& dir, const Json& m) {
   if (cudaHostAlloc(reinterpret_cast<void**>(&e->pinned_ids), (size_t)(o.max_seq + 1) * 4, cudaHostAllocDefault) != cudaSuccess ||
       cudaHostAlloc(reinterpret_cast<void**>(&e->pinned_state), sizeof(DevState), cudaHostAllocDefault) != cudaSuccess)
     throw QdError{QD_E_NOMEM, "cannot allocate pinned host memory"};
+  setup_persist(e);
   QD_CK(cudaEventCreateWithFlags(&e->ev[0], cudaEventDisableTiming));
   QD_CK(cudaEventCreateWithFlags(&e->ev[1], cudaEventDisableTiming));
   if (o.use_graph) {
@@ -563,6 +704,9 @@ void free_engine(qd_engine* e) {
   if (e->blob) cudaFree(e->blob);
   if (e->kv) cudaFree(e->kv);
   if (e->scratch) cudaFree(e->scratch);
+  if (e->xbuf) cudaFree(e->xbuf);
+  if (e->d_players) cudaFree(e->d_players);
+  if (e->timeline) cudaFree(e->timeline);
   if (e->out_host) cudaFreeHost(e->out_host);
   if (e->pinned_ids) cudaFreeHost(e->pinned_ids);
   if (e->pinned_state) cudaFreeHost(e->pinned_state);
@@ -582,13 +726,25 @@ void set_state(qd_engine* e, int pos, int max_new) {
   e->pinned_state->step = 0;
   e->pinned_state->max_new = max_new;
   e->pinned_state->err = 0;
-  QD_CK(cudaMemcpyAsync(e->st, e->pinned_state, sizeof(DevState), cudaMemcpyHostToDevice, e->stream));
+  // pos, step, max_new, err only: epoch and abort belong to the device
+  QD_CK(cudaMemcpyAsync(e->st, e->pinned_state, offsetof(DevState, epoch), cudaMemcpyHostToDevice, e->stream));
 }
 
 void check_state(qd_engine* e) {
   QD_CK(cudaMemcpyAsync(e->pinned_state, e->st, sizeof(DevState), cudaMemcpyDeviceToHost, e->stream));
   QD_CK(cudaStreamSynchronize(e->stream));
   const int err = e->pinned_state->err;
+  if (err || e->pinned_state->abort) {
+    // Repair for the next launch: skip past any epoch a failed launch may have
+    // tagged words with, clear the abort flag and the merge counter.
+    e->pinned_state->epoch += 2;
+    e->pinned_state->abort = 0;
+    e->pinned_state->err = 0;
+    QD_CK(cudaMemcpyAsync(e->st, e->pinned_state, sizeof(DevState), cudaMemcpyHostToDevice, e->stream));
+    QD_CK(cudaMemsetAsync(e->lm_counter, 0, 4, e->stream));
+    QD_CK(cudaStreamSynchronize(e->stream));
+  }
+  if (err & kErrTimeout) throw QdError{QD_E_TIMEOUT, "device: a persistent-kernel wait expired; the launch was abandoned"};
   if (err & kErrToken) throw QdError{QD_E_DEVICE, "device: token id outside the vocabulary"};
   if (err & kErrPosition) throw QdError{QD_E_DEVICE, "device: position beyond max_seq"};
 }
@@ -610,6 +766,8 @@ void qd_options_default(qd_options* opt) {
   opt->rope_row_stride = 0;
   opt->variant = "optimized";
   opt->use_graph = 1;
+  opt->persistent = 1;
+  opt->timeline = 0;
 }
 
 int qd_engine_create(const char* runtime_dir, const qd_options* opt, qd_engine** out) {
@@ -729,8 +887,19 @@ int qd_engine_hidden(qd_engine* e, float* host_hidden) {
   if (!e || !host_hidden) return fail(e, QdError{QD_E_INVALID, "NULL argument"});
   try {
     QD_CK(cudaSetDevice(e->dev));
-    QD_CK(cudaMemcpyAsync(host_hidden, e->h, (size_t)e->p.hidden * 4, cudaMemcpyDeviceToHost, e->stream));
-    QD_CK(cudaStreamSynchronize(e->stream));
+    if (e->persist) {  // the persistent kernel leaves it in the exchange words after the last layer
+      std::vector<unsigned long long> w(e->p.hidden);
+      QD_CK(cudaMemcpyAsync(w.data(), e->xbuf + (long long)e->p.layers * e->xstride, w.size() * 8,
+                            cudaMemcpyDeviceToHost, e->stream));
+      QD_CK(cudaStreamSynchronize(e->stream));
+      for (int i = 0; i < e->p.hidden; ++i) {
+        const uint32_t bits = (uint32_t)w[i];
+        std::memcpy(host_hidden + i, &bits, 4);
+      }
+    } else {
+      QD_CK(cudaMemcpyAsync(host_hidden, e->h, (size_t)e->p.hidden * 4, cudaMemcpyDeviceToHost, e->stream));
+      QD_CK(cudaStreamSynchronize(e->stream));
+    }
   } catch (const QdError& err) {
     return fail(e, err);
   }
@@ -825,7 +994,27 @@ int qd_decode_sync(qd_engine* e, int32_t* out_ids, int n) {
   return QD_OK;
 }
 
-int qd_decode_step_kernels(const qd_engine* e) { return e ? e->p.layers * 5 + 1 : 0; }
+int qd_engine_uses_persistent(const qd_engine* e) { return e && e->persist ? 1 : 0; }
+
+int qd_engine_timeline(qd_engine* e, uint64_t* host_out, int* ctas, int* events_per_cta) {
+  if (!e) return fail(nullptr, QdError{QD_E_INVALID, "engine is NULL"});
+  try {
+    if (!e->timeline) throw QdError{QD_E_INVALID, "timeline not enabled (qd_options.timeline) or no persistent kernel"};
+    const int ev = timeline_events(e->p.layers);
+    if (ctas) *ctas = e->sms;
+    if (events_per_cta) *events_per_cta = ev;
+    if (host_out) {
+      QD_CK(cudaSetDevice(e->dev));
+      QD_CK(cudaMemcpyAsync(host_out, e->timeline, (size_t)e->sms * ev * 8, cudaMemcpyDeviceToHost, e->stream));
+      QD_CK(cudaStreamSynchronize(e->stream));
+    }
+  } catch (const QdError& err) {
+    return fail(e, err);
+  }
+  return QD_OK;
+}
+
+int qd_decode_step_kernels(const qd_engine* e) { return e ? (e->persist ? 1 : e->p.layers * 5 + 1) : 0; }
 
 // ---- kernel level -------------------------------------------------------------
 
@@ -840,8 +1029,10 @@ int qd_q4_matvec(const float* x, const uint32_t* weights, const uint16_t* scales
       throw QdError{QD_E_INVALID, "bad matvec dimensions (in_size <= blocks_per_row * 32 <= 4096)"};
     if ((reinterpret_cast<uintptr_t>(weights) & 15) != 0) throw QdError{QD_E_INVALID, "weights must be 16-byte aligned"};
     StageArgs a{};
-    a.w = reinterpret_cast<const uint4*>(weights);
-    a.s = reinterpret_cast<const __half*>(scales_f16);
+    a.w = reinterpret_cast<const char*>(weights);
+    a.s = reinterpret_cast<const char*>(scales_f16);
+    a.w_stride = (long long)blocks_per_row * 16;
+    a.s_stride = (long long)blocks_per_row * 2;
     a.rows = (int)out_size; a.nb = (int)blocks_per_row; a.k_valid = (int)in_size; a.src = x; a.out = y;
     launch_stage<kProPlain, kEpiStore>(a, plan_stage(a.rows, a.nb, current_sms()), static_cast<cudaStream_t>(stream));
   } catch (const QdError& err) {

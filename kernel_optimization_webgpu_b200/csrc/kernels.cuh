@@ -28,9 +28,14 @@ enum Epi : int {
   kEpiSilu = 2,     // out[r] = silu(y_gate[r]) * y_up[r]       (silu_mul.wgsl:13-23)
 };
 
+// Row r (sub-row j: 0, or 1 for the up row of a gate/up pair) keeps its nb
+// 16-byte blocks at w + r*w_stride + j*w_sub and its nb f16 scales at
+// s + r*s_stride + j*s_sub. The engine interleaves them into one row record
+// ([q4 blocks | scales], 16-byte aligned); the standalone entry passes two arrays.
 struct StageArgs {
-  const uint4* w;          // [rows * (silu ? 2 : 1)][nb]; for silu the up rows follow the gate rows
-  const __half* s;
+  const char* w;
+  const char* s;
+  long long w_stride, w_sub, s_stride, s_sub;
   int rows;                // output rows
   int nb;                  // blocks per row (= in_size / 32, rounded up)
   int k_valid;             // in_size: activations at or beyond it count as zero
@@ -71,9 +76,8 @@ __global__ void __launch_bounds__(kThreads, 2) k_stage(const StageArgs a) {
       for (int c = 0; c < KC; ++c) {
         const int b = c * 32 + lane;
         if (r < a.rows && b < a.nb) {
-          const size_t off = (size_t)(r + j * a.rows) * a.nb + b;
-          wr[i][j][c] = ld_stream(a.w + off);
-          sr[i][j][c] = a.s[off];
+          wr[i][j][c] = ld_stream(reinterpret_cast<const uint4*>(a.w + r * a.w_stride + j * a.w_sub) + b);
+          sr[i][j][c] = reinterpret_cast<const __half*>(a.s + r * a.s_stride + j * a.s_sub)[b];
         } else {
           wr[i][j][c] = make_uint4(0u, 0u, 0u, 0u);
           sr[i][j][c] = __float2half_rn(0.0f);

@@ -1,0 +1,793 @@
+// Batch-1 decode of one token as ONE persistent kernel (one CTA per SM,
+// cooperative launch so every CTA is resident).
+//
+// Weights: every stage's rows are split into one contiguous slice per CTA; each
+// CTA streams its layer slices, in consumption order, into an 8-slot shared-
+// memory ring with cp.async.bulk (completion on one mbarrier per slot). A slot
+// is refilled as soon as the stage that used it is done, so the weight stream
+// runs up to 8 stages (two layers) ahead of the dependency chain. The LM head
+// (one pass over the 311 MB table) streams with direct 128-bit loads.
+//
+// Activations: a stage's outputs go to global memory as 64-bit words
+// {f32 value, epoch}; consumers poll the words they need until each carries
+// this launch's epoch. Value and "ready" travel in one store, so a stage
+// boundary costs one store-to-load trip through L2 instead of a grid barrier.
+// Every wait has a deadline (globaltimer) and an abort flag: on expiry the
+// kernel sets an error bit, waits for its own copies in flight and returns.
+#pragma once
+
+#include "kernels.cuh"
+
+namespace qd {
+
+constexpr int kPT = 512;                   // threads per CTA
+constexpr int kPW = kPT / 32;              // warps per CTA
+constexpr int kSlots = 8;                  // ring slots
+constexpr int kSlotBytes = 24576;          // per slot (the largest per-CTA slice at Qwen3-0.6B shapes)
+constexpr unsigned long long kWaitNs = 200ull * 1000 * 1000;  // deadline of any single wait
+constexpr int kErrTimeout = 4;             // DevErr bit: a wait expired (kernel aborted)
+constexpr int kMaxRes = 256;               // per-CTA row results of one stage (floats)
+constexpr unsigned kPollBackoffNs = 100;   // pause between re-polls of exchange words
+
+// Stage timeline (opt-in): per CTA, event 0 = start, then per layer
+// 14 events (QKV input ready, QKV weights ready, QKV stored, attention done,
+// O input ready, O stored, gate/up input ready, gate/up stored, down input
+// ready, down stored, QKV norm done, O weights ready, gate/up norm done,
+// down weights ready), then LM-head input ready, LM-head done, merged.
+constexpr int kTimelinePerLayer = 14;
+__host__ __device__ constexpr int timeline_events(int layers) { return 1 + kTimelinePerLayer * layers + 3; }
+
+struct PLayer {
+  const char *qkv, *o, *gu, *d;            // row records (gate/up: pair records)
+  const float *n_in, *n_q, *n_k, *n_post;
+  void *kc, *vc;
+};
+
+struct PArgs {
+  const PLayer* layers;
+  int L, H, I, NH, NKV, vocab, max_seq, row_stride;
+  float eps, scale;
+  const __half* embed;
+  const float *cos_t, *sin_t, *final_norm;
+  unsigned long long* xb;                  // exchange words
+  long long xstride;                       // words per layer: h | qkv | attn | h_attn | act
+  DevState* st;
+  int *tokens, *out_dev, *out_host;
+  float* logits;
+  float* part_v;
+  uint32_t* part_i;
+  unsigned* counter;
+  int with_head;
+  int lm_rows;                             // unused (kept for the host's slot-size check)
+  unsigned long long* timeline;            // optional [gridDim.x][timeline_events(L)] stage stamps (ns)
+  long long rec_h, rec_q, rec_i;           // row record bytes for K = H, NH*128, I
+};
+
+// ---- small PTX helpers --------------------------------------------------------
+__device__ __forceinline__ unsigned smem_u32(const void* p) {
+  return static_cast<unsigned>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ unsigned long long gtimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ unsigned long long ld_word(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_word(unsigned long long* p, float v, unsigned epoch) {
+  const unsigned long long w = ((unsigned long long)epoch << 32) | __float_as_uint(v);
+  asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ void mbar_init(unsigned long long* b, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_tx(unsigned long long* b, unsigned bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_test(unsigned long long* b, unsigned parity) {
+  unsigned ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(b)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, unsigned bytes, unsigned long long* b) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(b))
+               : "memory");
+}
+__device__ __forceinline__ void stamp(unsigned long long* tl, int ev) {
+  if (tl && threadIdx.x == 0) tl[ev] = gtimer();
+}
+
+// Contiguous split of n rows over g CTAs (n * g < 2^31 for every shape served).
+__device__ __forceinline__ void range_of(int n, int c, int g, int& lo, int& hi) {
+  lo = (int)((unsigned)n * (unsigned)c / (unsigned)g);
+  hi = (int)((unsigned)n * (unsigned)(c + 1) / (unsigned)g);
+}
+
+struct PShared {
+  char* ring;
+  float* xs;            // activation staging (swizzled; also the attention merge area)
+  float* hs;            // layer input h (kept for the O residual)
+  float* has;           // h_attn (kept for the down residual)
+  unsigned long long* mbar;
+  float* red;           // [kPW]
+  int* flag;            // [0]: this CTA is the last to finish
+  float* res;           // [kMaxRes] stage row results
+  float* misc;          // attention: raw q/k/v, normed q, new k/v, warp (m, l); merge partials
+};
+
+// Row ranges of this CTA, computed once per launch.
+struct Ranges {
+  int qkv_lo, qkv_hi, h_lo, h_hi, i_lo, i_hi, v_lo, v_hi;
+};
+
+// The layer-weight chunk i of this CTA: chunks 4l..4l+3 are layer l's QKV, O,
+// gate/up and down slices.
+__device__ __forceinline__ void chunk_src(const PArgs& a, const Ranges& rg, int i, const char*& src, unsigned& bytes) {
+  const PLayer& P = a.layers[i >> 2];
+  switch (i & 3) {
+    case 0: src = P.qkv + rg.qkv_lo * a.rec_h; bytes = (unsigned)((rg.qkv_hi - rg.qkv_lo) * a.rec_h); break;
+    case 1: src = P.o + rg.h_lo * a.rec_q; bytes = (unsigned)((rg.h_hi - rg.h_lo) * a.rec_q); break;
+    case 2: src = P.gu + rg.i_lo * 2 * a.rec_h; bytes = (unsigned)((rg.i_hi - rg.i_lo) * 2 * a.rec_h); break;
+    default: src = P.d + rg.h_lo * a.rec_i; bytes = (unsigned)((rg.h_hi - rg.h_lo) * a.rec_i); break;
+  }
+}
+
+// Thread 0 only: put chunk i in flight into its slot.
+__device__ __forceinline__ void issue_chunk(const PArgs& a, const PShared& S, const Ranges& rg, int i, int n) {
+  if (i >= n) return;
+  const char* src;
+  unsigned bytes;
+  chunk_src(a, rg, i, src, bytes);
+  const int slot = i % kSlots;
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  mbar_arrive_tx(&S.mbar[slot], bytes);
+  if (bytes) bulk_load(S.ring + slot * kSlotBytes, src, bytes, &S.mbar[slot]);
+}
+
+__device__ __forceinline__ bool aborted(const PArgs& a) { return *reinterpret_cast<volatile int*>(&a.st->abort) != 0; }
+
+// Every thread: wait for chunk i to land. False on timeout/abort.
+__device__ __forceinline__ bool wait_chunk(const PArgs& a, const PShared& S, int i) {
+  const int slot = i % kSlots;
+  const unsigned parity = (unsigned)(i / kSlots) & 1u;
+  if (mbar_test(&S.mbar[slot], parity)) return true;
+  const unsigned long long t0 = gtimer();
+  for (unsigned it = 1;; ++it) {
+    if (mbar_test(&S.mbar[slot], parity)) return true;
+    if ((it & 63) == 0 && (aborted(a) || gtimer() - t0 > kWaitNs)) return false;
+  }
+}
+
+// Every thread: wait until word p carries this launch's epoch. False on timeout/abort.
+__device__ __forceinline__ bool poll_word(const PArgs& a, const unsigned long long* p, unsigned epoch, float& out) {
+  unsigned long long v = ld_word(p);
+  unsigned long long t0 = 0;
+  for (unsigned it = 0; (unsigned)(v >> 32) != epoch; ++it) {
+    if (it == 0) t0 = gtimer();
+    else if ((it & 15) == 0 && (aborted(a) || gtimer() - t0 > kWaitNs)) return false;
+    __nanosleep(kPollBackoffNs);
+    v = ld_word(p);
+  }
+  out = __uint_as_float((unsigned)v);
+  return true;
+}
+
+// On failure: wait (bounded, ignoring the abort flag) for this CTA's chunks
+// still in flight, so no bulk copy targets shared memory after the CTA exits.
+__device__ __forceinline__ void drain(const PShared& S, int next, int n_chunks) {
+  const int end = min(next + kSlots, n_chunks);
+  for (int i = next; i < end; ++i) {
+    const int slot = i % kSlots;
+    const unsigned parity = (unsigned)(i / kSlots) & 1u;
+    const unsigned long long t0 = gtimer();
+    while (!mbar_test(&S.mbar[slot], parity))
+      if (gtimer() - t0 > kWaitNs) break;
+  }
+}
+
+// Raise the abort flag (any thread).
+__device__ __forceinline__ void raise_abort(const PArgs& a) {
+  atomicOr(&a.st->err, kErrTimeout);
+  atomicExch(&a.st->abort, 1);
+}
+
+// All threads agree whether to continue (also a block barrier).
+__device__ __forceinline__ bool stage_ok(const PArgs& a, bool mine) {
+  if (!mine) raise_abort(a);
+  return __syncthreads_and(mine ? 1 : 0) != 0;
+}
+
+// Sum over the warp of 4 per-lane values at once (transposing butterfly, 6
+// shuffles): on return lane l holds the total of value l >> 3.
+__device__ __forceinline__ float reduce4(float p0, float p1, float p2, float p3) {
+  const int lane = threadIdx.x & 31;
+  const bool hi16 = lane & 16, hi8 = lane & 8;
+  float a0 = (hi16 ? p2 : p0) + __shfl_xor_sync(0xffffffffu, hi16 ? p0 : p2, 16);
+  float a1 = (hi16 ? p3 : p1) + __shfl_xor_sync(0xffffffffu, hi16 ? p1 : p3, 16);
+  float r = (hi8 ? a1 : a0) + __shfl_xor_sync(0xffffffffu, hi8 ? a0 : a1, 8);
+  r += __shfl_xor_sync(0xffffffffu, r, 4);
+  r += __shfl_xor_sync(0xffffffffu, r, 2);
+  r += __shfl_xor_sync(0xffffffffu, r, 1);
+  return r;
+}
+
+// Block dots of one stage from the ring slot into res[c * n_items + item].
+// Items are (row, sub-row) pairs: item = row * nw + j; a row record holds nw
+// sub-rows of `rec` bytes. Warps are grouped by 32-block column chunk c
+// (kPW / kc warps per chunk, each holding only that chunk's activations) and
+// process 4 items at a time, so four independent dot chains overlap and share
+// one 6-shuffle reduction.
+__device__ __forceinline__ void stage_dots(const char* slot, int n_rows, int nw, int rec, int nb, int kc,
+                                        const float* xs, float* res) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int wpc = kPW / kc;
+  const int c = warp / wpc, u = warp - c * wpc;
+  if (c >= kc) return;
+  const int b = c * 32 + lane;
+  const bool live = b < nb;
+  float2 xr[16];
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (live) v = reinterpret_cast<const float4*>(xs)[xs_slot(b * 8 + q)];
+    xr[2 * q] = make_float2(v.x, v.y);
+    xr[2 * q + 1] = make_float2(v.z, v.w);
+  }
+  // A warp takes 4 consecutive items at a time: the activation chunk each warp
+  // loads from shared memory (4 KB) is the dominant cost, so few warps with more
+  // items each beat many warps with one item each.
+  const int n_items = n_rows * nw;
+  for (int i0 = u * 4; i0 < n_items; i0 += wpc * 4) {
+    uint4 w[4];
+    float s[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int it = i0 + k;
+      w[k] = make_uint4(0u, 0u, 0u, 0u);
+      s[k] = 0.0f;
+      if (live && it < n_items) {
+        const int row = nw == 1 ? it : (it >> 1), j = nw == 1 ? 0 : (it & 1);
+        const char* r = slot + row * nw * rec + j * rec;
+        w[k] = reinterpret_cast<const uint4*>(r)[b];
+        s[k] = __half2float(reinterpret_cast<const __half*>(r + nb * 16)[b]);
+      }
+    }
+    float p[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) p[k] = s[k] * q4_block_dot(w[k], xr);
+    const float t = reduce4(p[0], p[1], p[2], p[3]);
+    const int it = i0 + (lane >> 3);
+    if ((lane & 7) == 0 && it < n_items) res[c * n_items + it] = t;
+  }
+}
+
+// Every thread: poll words src[e], e = threadIdx.x + k*kPT < n, into shared
+// memory (swizzled staging when swz, else dst[e]). A thread's words are
+// re-polled together, so it pays one round trip after its last word lands.
+// Misses back off briefly so that pollers do not flood L2. False on timeout/abort.
+__device__ __forceinline__ bool poll_to_smem(const PArgs& a, const unsigned long long* src, int n, unsigned epoch,
+                                          float* dst, bool swz) {
+  constexpr int K = 8;
+  unsigned long long v[K];
+  unsigned need = 0;
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    const int e = threadIdx.x + k * kPT;
+    v[k] = 0ull;
+    if (e < n) {
+      v[k] = ld_word(src + e);
+      need |= 1u << k;
+    }
+  }
+  unsigned long long t0 = 0;
+  for (unsigned it = 0;; ++it) {
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      if ((need >> k) & 1u) {
+        if ((unsigned)(v[k] >> 32) == epoch) {
+          need &= ~(1u << k);
+          const int e = threadIdx.x + k * kPT;
+          const float f = __uint_as_float((unsigned)v[k]);
+          if (swz) xs_store(dst, e, f);
+          else dst[e] = f;
+        }
+      }
+    }
+    if (!need) return true;
+    if (it == 0) t0 = gtimer();
+    else if ((it & 15) == 0 && (aborted(a) || gtimer() - t0 > kWaitNs)) return false;
+    __nanosleep(kPollBackoffNs);
+#pragma unroll
+    for (int k = 0; k < K; ++k)
+      if ((need >> k) & 1u) v[k] = ld_word(src + threadIdx.x + k * kPT);
+  }
+}
+
+// ---- attention for one KV head (G query heads) -----------------------------------
+template <int G, typename KVT>
+__device__ __forceinline__ bool attn_stage(const PArgs& a, const PShared& S, int l, int g, int pos, unsigned epoch,
+                           const unsigned long long* xq, unsigned long long* xo) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const PLayer& P = a.layers[l];
+  KVT* kc = reinterpret_cast<KVT*>(P.kc);
+  KVT* vc = reinterpret_cast<KVT*>(P.vc);
+  const long long row_el = (long long)a.NKV * kHeadDim;
+  const int QS = a.NH * kHeadDim, KVS = a.NKV * kHeadDim;
+  float* raw = S.misc;                      // [(G + 2) * 128]
+  float* qs = raw + (G + 2) * kHeadDim;     // [G * 128]
+  float* kn = qs + G * kHeadDim;            // [128]
+  float* vn = kn + kHeadDim;                // [128]
+  float2* wml = reinterpret_cast<float2*>(vn + kHeadDim);  // [kPW * G]
+
+  // Everything that does not depend on this token's q/k/v, loaded before the wait:
+  // the norm weights, this position's RoPE row and this warp's first cached K/V row.
+  const float4 wq4 = reinterpret_cast<const float4*>(P.n_q)[lane];
+  const float4 wk4 = reinterpret_cast<const float4*>(P.n_k)[lane];
+  const int pair0 = (4 * lane) & (kHeadDim / 2 - 1);
+  const long long toff = (long long)pos * a.row_stride + pair0;
+  const float4 cr = *reinterpret_cast<const float4*>(a.cos_t + toff);
+  const float4 sr = *reinterpret_cast<const float4*>(a.sin_t + toff);
+  float4 k_pf = make_float4(0.f, 0.f, 0.f, 0.f), v_pf = k_pf;
+  if (warp < pos) {
+    k_pf = ld4<KVT>(kc + warp * row_el + g * kHeadDim + 4 * lane);
+    v_pf = ld4<KVT>(vc + warp * row_el + g * kHeadDim + 4 * lane);
+  }
+  // q heads g*G.., k head g, v head g from the QKV exchange words (one word per thread for G <= 2).
+  bool ok = true;
+  for (int e0 = 0; e0 < (G + 2) * kHeadDim; e0 += kPT) {
+    const int e = e0 + threadIdx.x;
+    if (e < (G + 2) * kHeadDim) {
+      const int t = e / kHeadDim, d = e % kHeadDim;
+      const int src = t < G ? (g * G + t) * kHeadDim + d : (t == G ? QS + g * kHeadDim + d : QS + KVS + g * kHeadDim + d);
+      ok = ok && poll_word(a, xq + src, epoch, raw[e]);
+    }
+  }
+  if (!stage_ok(a, ok)) return false;
+
+  // head RMSNorm + RoPE (q heads, k), cache append (k, v)
+  for (int t = warp; t < G + 2; t += kPW) {
+    const float4 x = reinterpret_cast<const float4*>(raw + t * kHeadDim)[lane];
+    KVT* krow = kc + (long long)pos * row_el + g * kHeadDim + 4 * lane;
+    KVT* vrow = vc + (long long)pos * row_el + g * kHeadDim + 4 * lane;
+    if (t == G + 1) {
+      reinterpret_cast<float4*>(vn)[lane] = st4<KVT>(vrow, x);
+      continue;
+    }
+    const float4 w4 = t < G ? wq4 : wk4;
+    float ss = x.x * x.x + x.y * x.y + x.z * x.z + x.w * x.w;
+    ss = warp_sum(ss);
+    const float inv = rsqrtf(ss / (float)kHeadDim + a.eps);
+    const float4 y = make_float4(x.x * inv * w4.x, x.y * inv * w4.y, x.z * inv * w4.z, x.w * inv * w4.w);
+    float4 p;
+    p.x = __shfl_xor_sync(0xffffffffu, y.x, 16);
+    p.y = __shfl_xor_sync(0xffffffffu, y.y, 16);
+    p.z = __shfl_xor_sync(0xffffffffu, y.z, 16);
+    p.w = __shfl_xor_sync(0xffffffffu, y.w, 16);
+    const float sign = (lane >= 16) ? 1.0f : -1.0f;
+    const float4 r = make_float4(y.x * cr.x + sign * p.x * sr.x, y.y * cr.y + sign * p.y * sr.y,
+                                 y.z * cr.z + sign * p.z * sr.z, y.w * cr.w + sign * p.w * sr.w);
+    if (t < G) reinterpret_cast<float4*>(qs + t * kHeadDim)[lane] = r;
+    else reinterpret_cast<float4*>(kn)[lane] = st4<KVT>(krow, r);
+  }
+  __syncthreads();
+
+  // Online softmax per warp over positions warp, warp + kPW, ... <= pos.
+  float4 q[G];
+#pragma unroll
+  for (int h = 0; h < G; ++h) q[h] = reinterpret_cast<const float4*>(qs + h * kHeadDim)[lane];
+  float m[G], lsum[G];
+  float4 acc[G];
+#pragma unroll
+  for (int h = 0; h < G; ++h) { m[h] = -INFINITY; lsum[h] = 0.0f; acc[h] = make_float4(0.f, 0.f, 0.f, 0.f); }
+  for (int p = warp; p <= pos; p += kPW) {
+    float4 k4, v4;
+    if (p == pos) {
+      k4 = reinterpret_cast<const float4*>(kn)[lane];
+      v4 = reinterpret_cast<const float4*>(vn)[lane];
+    } else {
+      k4 = k_pf;
+      v4 = v_pf;
+    }
+    const int pn = p + kPW;
+    if (pn < pos) {  // prefetch the next cached row
+      k_pf = ld4<KVT>(kc + pn * row_el + g * kHeadDim + 4 * lane);
+      v_pf = ld4<KVT>(vc + pn * row_el + g * kHeadDim + 4 * lane);
+    }
+#pragma unroll
+    for (int h = 0; h < G; ++h) {
+      float d = q[h].x * k4.x + q[h].y * k4.y + q[h].z * k4.z + q[h].w * k4.w;
+      const float sc = warp_sum(d) * a.scale;
+      const float mn = fmaxf(m[h], sc);
+      const float co = expf(m[h] - mn), cn = expf(sc - mn);
+      lsum[h] = lsum[h] * co + cn;
+      acc[h] = make_float4(acc[h].x * co + cn * v4.x, acc[h].y * co + cn * v4.y, acc[h].z * co + cn * v4.z,
+                           acc[h].w * co + cn * v4.w);
+      m[h] = mn;
+    }
+  }
+  // Merge the warps in a fixed order (deterministic).
+  float* wacc = S.xs;  // [kPW][G][128]
+#pragma unroll
+  for (int h = 0; h < G; ++h) {
+    reinterpret_cast<float4*>(wacc + (warp * G + h) * kHeadDim)[lane] = acc[h];
+    if (lane == 0) wml[warp * G + h] = make_float2(m[h], lsum[h]);
+  }
+  __syncthreads();
+  // Per (head, warp) rescale factors exp(m_w - M) / L, computed once: one lane
+  // per (head, warp), reductions over the kPW lanes of a head by shuffles.
+  static_assert(kPW == 16, "the merge pairs two heads per warp");
+  float* fw = raw;  // [G][kPW] (raw is no longer needed)
+  if (threadIdx.x < ((G * kPW + 31) / 32) * 32) {
+    const int h = threadIdx.x / kPW, w = threadIdx.x % kPW;
+    const bool on = h < G;
+    const float2 mw = on ? wml[w * G + h] : make_float2(-INFINITY, 0.0f);
+    float M = mw.x;
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    const float e = mw.y > 0.0f ? expf(mw.x - M) : 0.0f;
+    float Ls = mw.y * e;
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) Ls += __shfl_xor_sync(0xffffffffu, Ls, o);
+    if (on) fw[h * kPW + w] = e / Ls;
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < G * kHeadDim; e += kPT) {
+    const int h = e / kHeadDim, d = e % kHeadDim;
+    float o = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kPW; ++w) o += wacc[(w * G + h) * kHeadDim + d] * fw[h * kPW + w];
+    st_word(xo + (g * G + h) * kHeadDim + d, o, epoch);
+  }
+  return true;
+}
+
+// RMSNorm of v[e] (shared memory, e = tid, tid + kPT) with the thread's
+// prefetched weights w into the swizzled staging; all threads must call it.
+__device__ __forceinline__ void rms_own(const float* v, const float (&w)[2], int n, float eps, float* xs,
+                                        float* red) {
+  float x[2] = {0.0f, 0.0f}, ss = 0.0f;
+#pragma unroll
+  for (int k = 0; k < 2; ++k)
+    if (threadIdx.x + k * kPT < n) {
+      x[k] = v[threadIdx.x + k * kPT];
+      ss += x[k] * x[k];
+    }
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float t = 0.0f;
+#pragma unroll
+  for (int k = 0; k < kPW; ++k) t += red[k];
+  const float inv = rsqrtf(t / (float)n + eps);
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    const int e = threadIdx.x + k * kPT;
+    if (e < n) xs_store(xs, e, x[k] * inv * w[k]);
+  }
+}
+
+// ---- the kernel -------------------------------------------------------------------
+template <int G, typename KVT>
+__global__ void __launch_bounds__(kPT, 1) k_decode_persistent(const __grid_constant__ PArgs a) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  const int cta = blockIdx.x, ng = gridDim.x;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int H = a.H, I = a.I, QS = a.NH * kHeadDim, R = QS + 2 * a.NKV * kHeadDim;
+  const int maxk = max(max(H, QS), I);
+
+  PShared S;
+  S.ring = reinterpret_cast<char*>(smem);
+  S.xs = reinterpret_cast<float*>(smem + kSlots * kSlotBytes);
+  const int xs_floats = max(maxk, kPW * G * kHeadDim);
+  S.hs = S.xs + xs_floats;
+  S.has = S.hs + H;
+  S.mbar = reinterpret_cast<unsigned long long*>(S.has + H);
+  S.red = reinterpret_cast<float*>(S.mbar + kSlots);
+  S.flag = reinterpret_cast<int*>(S.red + kPW);
+  S.res = reinterpret_cast<float*>(S.flag + 4);
+  S.misc = S.res + kMaxRes;
+
+  const int pos = a.st->pos;
+  const unsigned epoch = (unsigned)a.st->epoch + 1u;
+  if (pos < 0 || pos >= a.max_seq) {  // the host keeps positions in range; never index out of bounds
+    if (threadIdx.x == 0) atomicOr(&a.st->err, kErrPosition);
+    return;
+  }
+  unsigned long long* tl = a.timeline ? a.timeline + (long long)cta * timeline_events(a.L) : nullptr;
+  stamp(tl, 0);
+  Ranges rg;
+  range_of(R, cta, ng, rg.qkv_lo, rg.qkv_hi);
+  range_of(H, cta, ng, rg.h_lo, rg.h_hi);
+  range_of(I, cta, ng, rg.i_lo, rg.i_hi);
+  range_of(a.vocab, cta, ng, rg.v_lo, rg.v_hi);
+  const int n_chunks = 4 * a.L;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kSlots; ++s) mbar_init(&S.mbar[s], 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  if (threadIdx.x == 0)
+    for (int i = 0; i < kSlots; ++i) issue_chunk(a, S, rg, i, n_chunks);
+
+  // Layer-0 input: the embedding row of tokens[pos], computed by every CTA.
+  {
+    int tok = a.tokens[pos];
+    if (tok < 0 || tok >= a.vocab) {
+      if (cta == 0 && threadIdx.x == 0) atomicOr(&a.st->err, kErrToken);
+      tok = 0;
+    }
+    const __half* er = a.embed + (long long)tok * H;
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int e = threadIdx.x + k * kPT;
+      if (e < H) S.hs[e] = __half2float(er[e]);
+    }
+  }
+
+  int chunk = 0;
+#define QD_FAIL_IF(cond)              \
+  if (cond) {                         \
+    drain(S, chunk, n_chunks);        \
+    return;                           \
+  }
+  for (int l = 0; l < a.L; ++l) {
+    const PLayer& P = a.layers[l];
+    unsigned long long* X = a.xb + (long long)l * a.xstride;
+    unsigned long long *xh = X, *xq = X + H, *xa = X + H + R, *xha = X + H + R + QS, *xact = xha + H;
+    unsigned long long* xnext = a.xb + (long long)(l + 1) * a.xstride;
+    const int ev = 1 + l * kTimelinePerLayer;
+
+    // 1. input RMSNorm + QKV rows
+    {
+      float nw[2];
+#pragma unroll
+      for (int k = 0; k < 2; ++k) nw[k] = threadIdx.x + k * kPT < H ? P.n_in[threadIdx.x + k * kPT] : 0.0f;
+      if (l > 0) QD_FAIL_IF(!stage_ok(a, poll_to_smem(a, xh, H, epoch, S.hs, false)));
+      stamp(tl, ev + 0);
+      rms_own(S.hs, nw, H, a.eps, S.xs, S.red);
+      stamp(tl, ev + 10);
+      QD_FAIL_IF(!stage_ok(a, wait_chunk(a, S, chunk)));
+      stamp(tl, ev + 1);
+      const int n = rg.qkv_hi - rg.qkv_lo;
+      stage_dots(S.ring + (chunk % kSlots) * kSlotBytes, n, 1, (int)a.rec_h, H / kBlockCols, 1, S.xs, S.res);
+      __syncthreads();
+      if (threadIdx.x < n) st_word(xq + rg.qkv_lo + threadIdx.x, S.res[threadIdx.x], epoch);
+      __syncthreads();
+      stamp(tl, ev + 2);
+      if (threadIdx.x == 0) issue_chunk(a, S, rg, chunk + kSlots, n_chunks);
+      ++chunk;
+    }
+
+    // 2. attention (CTAs 0..NKV-1, one KV head each)
+    if (cta < a.NKV) QD_FAIL_IF((!attn_stage<G, KVT>(a, S, l, cta, pos, epoch, xq, xa)));
+    __syncthreads();
+    stamp(tl, ev + 3);
+
+    // 3. O projection + residual
+    {
+      QD_FAIL_IF(!stage_ok(a, poll_to_smem(a, xa, QS, epoch, S.xs, true)));
+      stamp(tl, ev + 4);
+      QD_FAIL_IF(!stage_ok(a, wait_chunk(a, S, chunk)));
+      stamp(tl, ev + 11);
+      const int n = rg.h_hi - rg.h_lo;
+      stage_dots(S.ring + (chunk % kSlots) * kSlotBytes, n, 1, (int)a.rec_q, QS / kBlockCols, 2, S.xs, S.res);
+      __syncthreads();
+      if (threadIdx.x < n) {
+        const int r = rg.h_lo + threadIdx.x;
+        st_word(xha + r, S.hs[r] + (S.res[threadIdx.x] + S.res[n + threadIdx.x]), epoch);
+      }
+      __syncthreads();
+      stamp(tl, ev + 5);
+      if (threadIdx.x == 0) issue_chunk(a, S, rg, chunk + kSlots, n_chunks);
+      ++chunk;
+    }
+
+    // 4. post-attention RMSNorm + gate/up + silu * up
+    {
+      float nw[2];
+#pragma unroll
+      for (int k = 0; k < 2; ++k) nw[k] = threadIdx.x + k * kPT < H ? P.n_post[threadIdx.x + k * kPT] : 0.0f;
+      QD_FAIL_IF(!stage_ok(a, poll_to_smem(a, xha, H, epoch, S.has, false)));
+      stamp(tl, ev + 6);
+      rms_own(S.has, nw, H, a.eps, S.xs, S.red);
+      stamp(tl, ev + 12);
+      QD_FAIL_IF(!stage_ok(a, wait_chunk(a, S, chunk)));
+      const int n = rg.i_hi - rg.i_lo;
+      stage_dots(S.ring + (chunk % kSlots) * kSlotBytes, n, 2, (int)a.rec_h, H / kBlockCols, 1, S.xs, S.res);
+      __syncthreads();
+      if (threadIdx.x < n) {
+        const float gt = S.res[2 * threadIdx.x], upv = S.res[2 * threadIdx.x + 1];
+        st_word(xact + rg.i_lo + threadIdx.x, (gt / (1.0f + expf(-gt))) * upv, epoch);
+      }
+      __syncthreads();
+      stamp(tl, ev + 7);
+      if (threadIdx.x == 0) issue_chunk(a, S, rg, chunk + kSlots, n_chunks);
+      ++chunk;
+    }
+
+    // 5. down projection + residual
+    {
+      QD_FAIL_IF(!stage_ok(a, poll_to_smem(a, xact, I, epoch, S.xs, true)));
+      stamp(tl, ev + 8);
+      QD_FAIL_IF(!stage_ok(a, wait_chunk(a, S, chunk)));
+      stamp(tl, ev + 13);
+      const int n = rg.h_hi - rg.h_lo;
+      stage_dots(S.ring + (chunk % kSlots) * kSlotBytes, n, 1, (int)a.rec_i, I / kBlockCols, 3, S.xs, S.res);
+      __syncthreads();
+      if (threadIdx.x < n) {
+        const int r = rg.h_lo + threadIdx.x;
+        st_word(xnext + r, S.has[r] + ((S.res[threadIdx.x] + S.res[n + threadIdx.x]) + S.res[2 * n + threadIdx.x]),
+                epoch);
+      }
+      __syncthreads();
+      stamp(tl, ev + 9);
+      if (threadIdx.x == 0) issue_chunk(a, S, rg, chunk + kSlots, n_chunks);
+      ++chunk;
+    }
+  }
+#undef QD_FAIL_IF
+
+  // ---- LM head + argmax (or, for a prompt token, just finish) ----
+  // Every ring chunk has been consumed here: nothing is in flight, so a failure
+  // below may return directly.
+  float bv = kNegMax;
+  uint32_t bi = 0;
+  if (a.with_head) {
+    // This warp streams rows v_lo + (i*kPW + warp)*4 + k (k < 4): 4 rows at once,
+    // lane holding uint4 c*32 + lane of each row. The first batch is loaded
+    // before waiting for the final hidden state.
+    const int kc8 = H / 256;
+    const int n_rows = rg.v_hi - rg.v_lo;
+    const uint4* tab = reinterpret_cast<const uint4*>(a.embed);
+    const int rpr = H / 8;
+    uint4 cur[4][4];
+    int i0 = warp * 4;
+    auto load_batch = [&](int first) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const int rr = first + k;
+          cur[k][c] = (c < kc8 && rr < n_rows) ? ld_stream(tab + (long long)(rg.v_lo + rr) * rpr + c * 32 + lane)
+                                               : make_uint4(0u, 0u, 0u, 0u);
+        }
+    };
+    load_batch(i0);
+    float fw[2];
+#pragma unroll
+    for (int k = 0; k < 2; ++k) fw[k] = threadIdx.x + k * kPT < H ? a.final_norm[threadIdx.x + k * kPT] : 0.0f;
+    unsigned long long* xf = a.xb + (long long)a.L * a.xstride;
+    if (!stage_ok(a, poll_to_smem(a, xf, H, epoch, S.hs, false))) return;
+    float fv[2];
+#pragma unroll
+    for (int k = 0; k < 2; ++k) fv[k] = threadIdx.x + k * kPT < H ? S.hs[threadIdx.x + k * kPT] : 0.0f;
+    stamp(tl, 1 + kTimelinePerLayer * a.L);
+    // final RMSNorm into plain staging; lane holds columns (c*32+lane)*8 .. +7
+    {
+      float ss = 0.0f;
+#pragma unroll
+      for (int k = 0; k < 2; ++k)
+        if (threadIdx.x + k * kPT < H) ss += fv[k] * fv[k];
+      ss = warp_sum(ss);
+      if (lane == 0) S.red[warp] = ss;
+      __syncthreads();
+      float t = 0.0f;
+#pragma unroll
+      for (int k = 0; k < kPW; ++k) t += S.red[k];
+      const float inv = rsqrtf(t / (float)H + a.eps);
+#pragma unroll
+      for (int k = 0; k < 2; ++k)
+        if (threadIdx.x + k * kPT < H) S.xs[threadIdx.x + k * kPT] = fv[k] * inv * fw[k];
+      __syncthreads();
+    }
+    float2 xr[4][4];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      if (c < kc8) {
+        const float4* p = reinterpret_cast<const float4*>(S.xs + (c * 32 + lane) * 8);
+        const float4 v0 = p[0], v1 = p[1];
+        xr[c][0] = make_float2(v0.x, v0.y);
+        xr[c][1] = make_float2(v0.z, v0.w);
+        xr[c][2] = make_float2(v1.x, v1.y);
+        xr[c][3] = make_float2(v1.z, v1.w);
+      } else {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) xr[c][k] = make_float2(0.f, 0.f);
+      }
+    }
+    for (; i0 < n_rows; i0 += kPW * 4) {
+      float p[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        float2 acc = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) acc = f16x8_dot(cur[k][c], xr[c], acc);
+        p[k] = acc.x + acc.y;
+      }
+      if (i0 + kPW * 4 < n_rows) load_batch(i0 + kPW * 4);
+      const float v = reduce4(p[0], p[1], p[2], p[3]);
+      const int rr = i0 + (lane >> 3);
+      if ((lane & 7) == 0 && rr < n_rows) {
+        const int r = rg.v_lo + rr;
+        a.logits[r] = v;
+        if (am_better(v, (uint32_t)r, bv, bi)) { bv = v; bi = (uint32_t)r; }
+      }
+    }
+    // warp argmax (total order: larger value, then lower index)
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const uint32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (am_better(ov, oi, bv, bi)) { bv = ov; bi = oi; }
+    }
+  }
+  stamp(tl, 2 + kTimelinePerLayer * a.L);
+
+  // CTA partial -> last CTA merges, emits the token and advances the state.
+  float* bvs = S.misc;
+  uint32_t* bis = reinterpret_cast<uint32_t*>(S.misc + kPW);
+  __syncthreads();
+  if (lane == 0) { bvs[warp] = bv; bis[warp] = bi; }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float v = bvs[0];
+    uint32_t i = bis[0];
+    for (int w = 1; w < kPW; ++w)
+      if (am_better(bvs[w], bis[w], v, i)) { v = bvs[w]; i = bis[w]; }
+    a.part_v[cta] = v;
+    a.part_i[cta] = i;
+    __threadfence();
+    const unsigned prev = atomicAdd(a.counter, 1u);
+    S.flag[0] = (prev == (unsigned)ng - 1);
+  }
+  __syncthreads();
+  if (!S.flag[0]) return;
+  __threadfence();
+  float v = kNegMax;
+  uint32_t i = 0;
+  if (a.with_head) {
+    for (int b = threadIdx.x; b < ng; b += kPT) {
+      const float pv = __ldcg(a.part_v + b);
+      const uint32_t pi = __ldcg(a.part_i + b);
+      if (am_better(pv, pi, v, i)) { v = pv; i = pi; }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+      const uint32_t oi = __shfl_xor_sync(0xffffffffu, i, o);
+      if (am_better(ov, oi, v, i)) { v = ov; i = oi; }
+    }
+    if (lane == 0) { bvs[warp] = v; bis[warp] = i; }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    if (a.with_head) {
+      v = bvs[0];
+      i = bis[0];
+      for (int w = 1; w < kPW; ++w)
+        if (am_better(bvs[w], bis[w], v, i)) { v = bvs[w]; i = bis[w]; }
+      const int step = a.st->step;
+      if (pos + 1 <= a.max_seq) a.tokens[pos + 1] = (int)i;
+      if (step < a.st->max_new) {
+        a.out_dev[step] = (int)i;
+        if (a.out_host) *reinterpret_cast<volatile int*>(a.out_host + step) = (int)i;
+      }
+      a.st->step = step + 1;
+    }
+    a.st->pos = pos + 1;
+    a.st->epoch = (int)epoch;
+    *a.counter = 0u;
+    stamp(tl, 3 + kTimelinePerLayer * a.L);
+  }
+}
+
+}  // namespace qd

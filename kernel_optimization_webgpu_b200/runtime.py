@@ -45,7 +45,8 @@ class Engine:
     """One model resident on one GPU (qd_engine_create / qd_generate_greedy)."""
 
     def __init__(self, runtime_dir: str, device: int = 0, max_seq: int = 256, kv_dtype: str = "f16",
-                 rope_row_stride: int = 0, variant: str = "optimized", use_graph: bool = True):
+                 rope_row_stride: int = 0, variant: str = "optimized", use_graph: bool = True,
+                 persistent: bool = True, timeline: bool = False):
         L = _lib.load()
         opt = QdOptions()
         L.qd_options_default(C.byref(opt))
@@ -56,6 +57,8 @@ class Engine:
         self._variant = variant.encode()
         opt.variant = self._variant
         opt.use_graph = int(use_graph)
+        opt.persistent = int(persistent)
+        opt.timeline = int(timeline)
         h = C.c_void_p()
         check(L.qd_engine_create(os.fsencode(runtime_dir), C.byref(opt), C.byref(h)))
         self._h = h
@@ -66,9 +69,9 @@ class Engine:
         self.profile = {f: getattr(p, f) for f, _ in QdProfile._fields_}
 
     def close(self) -> None:
-        if getattr(self, "_h", None):
-            _lib.load().qd_engine_destroy(self._h)
-            self._h = None
+        if getattr(self, "_h", None) and _lib is not None and _lib._lib is not None:
+            _lib._lib.qd_engine_destroy(self._h)
+        self._h = None
 
     def __del__(self):
         self.close()
@@ -122,6 +125,19 @@ class Engine:
         out = np.zeros(max(n, 1), np.int32)
         check(_lib.load().qd_decode_sync(self._h, out.ctypes.data, int(n)), self._h)
         return out[:n].tolist()
+
+    def timeline(self) -> np.ndarray:
+        """Stage stamps (ns) of the last persistent launch, shape [ctas][events]."""
+        L = _lib.load()
+        ctas, ev = C.c_int(), C.c_int()
+        check(L.qd_engine_timeline(self._h, None, C.byref(ctas), C.byref(ev)), self._h)
+        out = np.zeros((ctas.value, ev.value), np.uint64)
+        check(L.qd_engine_timeline(self._h, out.ctypes.data, None, None), self._h)
+        return out
+
+    @property
+    def persistent(self) -> bool:
+        return bool(_lib.load().qd_engine_uses_persistent(self._h))
 
     @property
     def step_kernels(self) -> int:

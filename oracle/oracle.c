@@ -447,6 +447,7 @@ void qo_session_free(qo_session* s) {
 
 void qo_session_set_trace(qo_session* s, float* trace) { s->trace = trace; }
 const float* qo_session_final_hidden(const qo_session* s) { return s->final_out; }
+const float* qo_session_hidden(const qo_session* s) { return s->h; }
 
 static void proj(const qo_layer* l, int which, const qo_model* m, const float* x, float* y) {
   uint32_t out_size, in_size;

@@ -70,6 +70,8 @@ void qo_session_set_trace(qo_session* s, float* trace);
 /* One token through all layers plus the final norm (enqueueAutoregressiveToken). */
 int qo_forward(qo_session* s, int32_t token, int position);
 const float* qo_session_final_hidden(const qo_session* s);
+/* Residual stream after the last layer of the last forward (before the final norm). */
+const float* qo_session_hidden(const qo_session* s);
 /* LM head + argmax on the last forward's final hidden (greedyNextTokenResident). */
 int qo_next_token(qo_session* s, float* logits_out, uint32_t result[2], float* top2_margin);
 /* runCustomQwenGreedyPrompt's token flow. Returns 0 or a negative error. */

@@ -58,6 +58,7 @@ def lib():
         L.qo_session_set_trace.argtypes = [vp, vp]
         L.qo_forward.argtypes = [vp, i32, i32]; L.qo_forward.restype = i32
         L.qo_session_final_hidden.argtypes = [vp]; L.qo_session_final_hidden.restype = C.POINTER(f32)
+        L.qo_session_hidden.argtypes = [vp]; L.qo_session_hidden.restype = C.POINTER(f32)
         L.qo_next_token.argtypes = [vp, vp, _u32p, vp]; L.qo_next_token.restype = i32
         L.qo_greedy.argtypes = [vp, vp, i32, i32, vp, vp]; L.qo_greedy.restype = i32
         L.qo_num_threads.restype = i32
@@ -215,6 +216,11 @@ class Session:
 
     def final_hidden(self) -> np.ndarray:
         p = lib().qo_session_final_hidden(self._h)
+        return np.ctypeslib.as_array(p, shape=(self.model.hidden,)).copy()
+
+    def hidden(self) -> np.ndarray:
+        """Residual stream after the last layer (before the final RMSNorm)."""
+        p = lib().qo_session_hidden(self._h)
         return np.ctypeslib.as_array(p, shape=(self.model.hidden,)).copy()
 
     def next_token(self):
