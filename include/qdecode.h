@@ -127,6 +127,16 @@ int qd_q4_matvec(const float* x, const uint32_t* weights, const uint16_t* scales
                  uint32_t in_size, uint32_t out_size, uint32_t blocks_per_row,
                  uint32_t block_size, void* stream);
 
+/* Batched q4 MatMulNBits on the tcgen05 tensor cores: y[m][out_size] = dequant(weights) . x[m]
+ * for m < M (x: [M][in_size] f32, same weight layout as qd_q4_matvec). The MMA inputs are
+ * f16 hi/lo splits of the exact f32 weights and of x (three MMAs per step), so results agree
+ * with f32 arithmetic to ~1e-6 relative. in_size must be a multiple of 64 (<= 4096). The
+ * workspace holds the split x (qd_q4_gemm_workspace_bytes). Replaces M dispatches of
+ * matmul_nbits_q4.wgsl (matmul_nbits_q4.wgsl:43-92). */
+size_t qd_q4_gemm_workspace_bytes(uint32_t M, uint32_t in_size);
+int qd_q4_gemm(const float* x, const uint32_t* weights, const uint16_t* scales_f16, float* y, uint32_t M,
+               uint32_t in_size, uint32_t out_size, uint32_t block_size, void* workspace, void* stream);
+
 /* Workspace (device, zeroed once by the caller; left zeroed by each call). */
 size_t qd_lm_head_argmax_workspace_bytes(uint32_t vocab);
 /* logits[vocab] = embed_f16 . h where h = rms_norm(hidden) * norm_weight when norm_weight

@@ -25,7 +25,8 @@ QD_KV_F32 = 1
 EXPORTS = (
     "qd_options_default", "qd_engine_create", "qd_engine_destroy", "qd_last_error",
     "qd_engine_profile", "qd_generate_greedy", "qd_engine_logits", "qd_engine_hidden",
-    "qd_engine_forward_trace", "qd_engine_uses_persistent", "qd_engine_timeline", "qd_q4_matvec", "qd_lm_head_argmax_workspace_bytes",
+    "qd_engine_forward_trace", "qd_engine_uses_persistent", "qd_engine_timeline", "qd_q4_matvec",
+    "qd_q4_gemm_workspace_bytes", "qd_q4_gemm", "qd_lm_head_argmax_workspace_bytes",
     "qd_lm_head_argmax", "qd_gqa_decode_workspace_bytes", "qd_gqa_decode",
     "qd_engine_set_stream", "qd_decode_begin", "qd_decode_step", "qd_decode_seek", "qd_decode_sync",
     "qd_decode_step_kernels", "qd_gqa_decode_noalloc",
@@ -113,6 +114,10 @@ def load(build_if_stale: bool = True):
     L.qd_decode_step_kernels.restype = i32
     L.qd_q4_matvec.argtypes = [vp, vp, vp, vp, u32, u32, u32, u32, vp]
     L.qd_q4_matvec.restype = i32
+    L.qd_q4_gemm_workspace_bytes.argtypes = [u32, u32]
+    L.qd_q4_gemm_workspace_bytes.restype = C.c_size_t
+    L.qd_q4_gemm.argtypes = [vp, vp, vp, vp, u32, u32, u32, u32, vp, vp]
+    L.qd_q4_gemm.restype = i32
     L.qd_lm_head_argmax_workspace_bytes.argtypes = [u32]
     L.qd_lm_head_argmax_workspace_bytes.restype = C.c_size_t
     L.qd_lm_head_argmax.argtypes = [vp, vp, f32, vp, vp, vp, u32, u32, vp, vp]

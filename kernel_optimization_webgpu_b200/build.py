@@ -15,7 +15,7 @@ ROOT = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
 LIB = os.path.join(PKG, "libqdecode.so")
 SOURCES = ["engine.cu", "noalloc.cu"]
-DEPS = ["engine.cu", "noalloc.cu", "kernels.cuh", "persist.cuh", "common.cuh", "json.hpp"]
+DEPS = ["engine.cu", "noalloc.cu", "kernels.cuh", "persist.cuh", "gemm_tc.cuh", "common.cuh", "json.hpp"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

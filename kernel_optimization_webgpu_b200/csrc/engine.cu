@@ -14,6 +14,7 @@
 
 #include "../../include/qdecode.h"
 #include "json.hpp"
+#include "gemm_tc.cuh"
 #include "kernels.cuh"
 #include "persist.cuh"
 
@@ -756,6 +757,38 @@ double ms_since(std::chrono::steady_clock::time_point t0) {
 }  // namespace
 
 // ---------------------------------------------------------------------------
+// ---- tcgen05 GEMM ---------------------------------------------------------------
+
+namespace {
+
+size_t tc_smem_bytes(int bn) { return (size_t)2 * (2 * kTcM * kTcK * 2 + 2 * bn * kTcK * 2) + 1024; }
+
+template <int BN, int EPI>
+void launch_tc_t(const TcArgs& a, cudaStream_t s) {
+  const size_t smem = tc_smem_bytes(BN);
+  static bool configured = false;  // per process; the attribute is per function
+  if (!configured) {
+    QD_CK(cudaFuncSetAttribute(k_q4_gemm_tc<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    configured = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((a.n_rows + kTcM - 1) / kTcM, (a.B + BN - 1) / BN);
+  cfg.blockDim = dim3(kTcThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  QD_CK(cudaLaunchKernelEx(&cfg, k_q4_gemm_tc<BN, EPI>, a));
+}
+
+template <int EPI>
+void launch_tc(const TcArgs& a, cudaStream_t s) {
+  if (a.B <= 64) launch_tc_t<64, EPI>(a, s);
+  else if (a.B <= 128) launch_tc_t<128, EPI>(a, s);
+  else launch_tc_t<256, EPI>(a, s);
+}
+
+}  // namespace
+
+
 extern "C" {
 
 void qd_options_default(qd_options* opt) {
@@ -1035,6 +1068,41 @@ int qd_q4_matvec(const float* x, const uint32_t* weights, const uint16_t* scales
     a.s_stride = (long long)blocks_per_row * 2;
     a.rows = (int)out_size; a.nb = (int)blocks_per_row; a.k_valid = (int)in_size; a.src = x; a.out = y;
     launch_stage<kProPlain, kEpiStore>(a, plan_stage(a.rows, a.nb, current_sms()), static_cast<cudaStream_t>(stream));
+  } catch (const QdError& err) {
+    return fail(nullptr, err);
+  }
+  return QD_OK;
+}
+
+size_t qd_q4_gemm_workspace_bytes(uint32_t M, uint32_t in_size) { return 256 + (size_t)M * in_size * 4; }
+
+int qd_q4_gemm(const float* x, const uint32_t* weights, const uint16_t* scales_f16, float* y, uint32_t M,
+               uint32_t in_size, uint32_t out_size, uint32_t block_size, void* workspace, void* stream) {
+  try {
+    if (!x || !weights || !scales_f16 || !y || !workspace) throw QdError{QD_E_INVALID, "NULL pointer"};
+    if (block_size != (uint32_t)kBlockCols) throw QdError{QD_E_INVALID, "only block_size 32 is supported"};
+    if (M == 0 || out_size == 0 || in_size == 0 || in_size % kTcK || in_size > 4096)
+      throw QdError{QD_E_INVALID, "qd_q4_gemm: in_size must be a positive multiple of 64, at most 4096"};
+    if ((reinterpret_cast<uintptr_t>(weights) & 15) || (reinterpret_cast<uintptr_t>(workspace) & 15))
+      throw QdError{QD_E_INVALID, "weights and workspace must be 16-byte aligned"};
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    __half* xh = reinterpret_cast<__half*>(static_cast<char*>(workspace) + 256);
+    __half* xl = xh + (size_t)M * in_size;
+    const int n = (int)(M * in_size);
+    launch(k_split_hilo, dim3(std::min((n + kThreads - 1) / kThreads, 4096)), s, x, n, xh, xl);
+    TcArgs a{};
+    a.w = reinterpret_cast<const char*>(weights);
+    a.s = reinterpret_cast<const char*>(scales_f16);
+    a.w_stride = (long long)in_size / 2;
+    a.s_stride = (long long)in_size / kBlockCols * 2;
+    a.n_rows = (int)out_size;
+    a.K = (int)in_size;
+    a.x_hi = xh;
+    a.x_lo = xl;
+    a.B = (int)M;
+    a.y = y;
+    a.ldy = (int)out_size;
+    launch_tc<kTcStore>(a, s);
   } catch (const QdError& err) {
     return fail(nullptr, err);
   }

@@ -268,6 +268,19 @@ def q4_matvec(x, weights, scales_f16, y=None, in_size: Optional[int] = None, str
     return y
 
 
+def q4_gemm(x, weights, scales_f16, y=None, stream=None):
+    """Y[m] = dequant(weights) . x[m] for every row of x [M][K] on tcgen05 (qd_q4_gemm)."""
+    import torch
+    M, K = x.shape
+    n = weights.shape[0]
+    if y is None:
+        y = torch.empty(M, n, dtype=torch.float32, device=x.device)
+    ws = torch.empty(_lib.load().qd_q4_gemm_workspace_bytes(M, K), dtype=torch.uint8, device=x.device)
+    check(_lib.load().qd_q4_gemm(x.data_ptr(), weights.data_ptr(), scales_f16.data_ptr(), y.data_ptr(), M, K, n,
+                                 32, ws.data_ptr(), _stream(stream)))
+    return y
+
+
 class LmHeadWorkspace:
     def __init__(self, vocab: int, device):
         import torch
