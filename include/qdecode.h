@@ -19,6 +19,9 @@
  *                       greedyNextTokenResident (webgpu-runtime.js:580-604)
  *   qd_gqa_decode       gqa_decode.wgsl (src/kernels/gqa_decode.wgsl:17-90) without its
  *                       256-position cap
+ *   qd_batch_*          the same per-token flow (webgpu-runtime.js:471-604) for B
+ *                       independent sequences at once; the reference runs one sequence
+ *   qd_generate_batch   runCustomQwenGreedyPrompt over B prompts of equal length
  */
 #ifndef QDECODE_H
 #define QDECODE_H
@@ -117,6 +120,57 @@ int qd_decode_seek(qd_engine* e, int position);
 int qd_decode_sync(qd_engine* e, int32_t* out_ids, int n);
 /* Kernels one qd_decode_step launches (for launch accounting). */
 int qd_decode_step_kernels(const qd_engine* e);
+
+/* ---- batched decode and prefill -------------------------------------------- */
+
+/* B independent sequences on the engine's device and stream. Every step advances
+ * all of them by one token; projections and the LM head run as tcgen05 GEMMs over
+ * the B rows. The batch owns a KV cache [layer][seq][kv_head][max_seq][128] f16
+ * (layers * B * kv_heads * max_seq * 512 bytes) and its step buffers. A batch
+ * borrows the engine's weights: destroy it before the engine. */
+typedef struct qd_batch qd_batch;
+
+int qd_batch_create(qd_engine* e, int batch, int max_seq, qd_batch** out);
+void qd_batch_destroy(qd_batch* b);
+int qd_batch_size(const qd_batch* b, int* batch, int* max_seq);
+/* Seeded synthetic context: for every sequence, layer and position p < ctx, the K
+ * and V rows of a synthetic hidden state pushed through the layer's input RMSNorm,
+ * k/v projections, k head-RMSNorm and RoPE at position p (tcgen05 GEMMs). Hidden
+ * value d of row r = seq * ctx + p in layer l is the Irwin-Hall sum of four hashed
+ * 24-bit uniforms (see kb_ctx_hidden), reproducible on any host. Every sequence's
+ * position becomes ctx; input tokens are left as they are. */
+int qd_batch_fill_context(qd_batch* b, int ctx, uint32_t seed);
+/* Next input token and position of every sequence (host arrays of `batch` entries). */
+int qd_batch_set_tokens(qd_batch* b, const int32_t* tokens, const int32_t* positions);
+int qd_batch_positions(qd_batch* b, int32_t* positions);
+/* `steps` greedy steps for every sequence (one CUDA graph launch per step): each
+ * sequence's token is run at its position, the argmax (ties: lowest index) is fed
+ * back and the position advanced. out_ids [steps][batch] (host) may be NULL.
+ * Requires position + steps <= max_seq for every sequence. */
+int qd_batch_decode(qd_batch* b, int steps, int32_t* out_ids);
+/* Prefill: prompt ids [batch][n_prompt] at positions 0..n_prompt-1 of every
+ * sequence (cache rows rewritten), run as GEMMs over batch * n_prompt rows with
+ * causal attention inside each prompt; first_ids [batch] (host, may be NULL)
+ * receives each sequence's first generated token, which becomes its next input
+ * at position n_prompt. */
+int qd_batch_prefill(qd_batch* b, const int32_t* ids, int n_prompt, int32_t* first_ids);
+/* Keep the f32 logits [batch][vocab] of each step for qd_batch_logits (off by
+ * default: the LM head then writes only 8 bytes per sequence and CTA). */
+int qd_batch_keep_logits(qd_batch* b, int keep);
+int qd_batch_logits(qd_batch* b, float* host_logits);
+/* Cached K and V rows of one sequence and layer, positions [pos0, pos0 + count),
+ * as f32 [count][kv_heads * 128] on the host (the cache holds f16). */
+int qd_batch_read_kv(qd_batch* b, int layer, int seq, int pos0, int count, float* k, float* v);
+int qd_batch_write_kv(qd_batch* b, int layer, int seq, int pos0, int count, const float* k, const float* v);
+/* Kernels one qd_batch_decode step launches (for launch accounting). */
+int qd_batch_step_kernels(const qd_batch* b);
+
+/* runCustomQwenGreedyPrompt over `batch` prompts of n_prompt ids each: prefill,
+ * then max_new_tokens greedy tokens per prompt. ids [batch][n_prompt], out_ids
+ * [batch][max_new_tokens] (host). Uses a temporary batch of max_seq
+ * n_prompt + max_new_tokens. */
+int qd_generate_batch(qd_engine* e, int batch, const int32_t* ids, int n_prompt, int max_new_tokens,
+                      int32_t* out_ids);
 
 /* ---- kernel level (device pointers) ---------------------------------------- */
 

@@ -30,6 +30,9 @@ EXPORTS = (
     "qd_lm_head_argmax", "qd_gqa_decode_workspace_bytes", "qd_gqa_decode",
     "qd_engine_set_stream", "qd_decode_begin", "qd_decode_step", "qd_decode_seek", "qd_decode_sync",
     "qd_decode_step_kernels", "qd_gqa_decode_noalloc",
+    "qd_batch_create", "qd_batch_destroy", "qd_batch_size", "qd_batch_fill_context", "qd_batch_set_tokens",
+    "qd_batch_positions", "qd_batch_decode", "qd_batch_prefill", "qd_batch_keep_logits", "qd_batch_logits",
+    "qd_batch_read_kv", "qd_batch_write_kv", "qd_batch_step_kernels", "qd_generate_batch",
 )
 
 
@@ -128,6 +131,35 @@ def load(build_if_stale: bool = True):
     L.qd_gqa_decode.restype = i32
     L.qd_gqa_decode_noalloc.argtypes = [vp, vp, vp, i32, vp, u32, u32, u32, u32, vp]
     L.qd_gqa_decode_noalloc.restype = i32
+    ip = C.POINTER(C.c_int)
+    L.qd_batch_create.argtypes = [vp, i32, i32, C.POINTER(vp)]
+    L.qd_batch_create.restype = i32
+    L.qd_batch_destroy.argtypes = [vp]
+    L.qd_batch_destroy.restype = None
+    L.qd_batch_size.argtypes = [vp, ip, ip]
+    L.qd_batch_size.restype = i32
+    L.qd_batch_fill_context.argtypes = [vp, i32, u32]
+    L.qd_batch_fill_context.restype = i32
+    L.qd_batch_set_tokens.argtypes = [vp, vp, vp]
+    L.qd_batch_set_tokens.restype = i32
+    L.qd_batch_positions.argtypes = [vp, vp]
+    L.qd_batch_positions.restype = i32
+    L.qd_batch_decode.argtypes = [vp, i32, vp]
+    L.qd_batch_decode.restype = i32
+    L.qd_batch_prefill.argtypes = [vp, vp, i32, vp]
+    L.qd_batch_prefill.restype = i32
+    L.qd_batch_keep_logits.argtypes = [vp, i32]
+    L.qd_batch_keep_logits.restype = i32
+    L.qd_batch_logits.argtypes = [vp, vp]
+    L.qd_batch_logits.restype = i32
+    L.qd_batch_read_kv.argtypes = [vp, i32, i32, i32, i32, vp, vp]
+    L.qd_batch_read_kv.restype = i32
+    L.qd_batch_write_kv.argtypes = [vp, i32, i32, i32, i32, vp, vp]
+    L.qd_batch_write_kv.restype = i32
+    L.qd_batch_step_kernels.argtypes = [vp]
+    L.qd_batch_step_kernels.restype = i32
+    L.qd_generate_batch.argtypes = [vp, i32, vp, i32, i32, vp]
+    L.qd_generate_batch.restype = i32
     _lib = L
     return L
 

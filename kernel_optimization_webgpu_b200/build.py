@@ -14,8 +14,8 @@ PKG = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
 LIB = os.path.join(PKG, "libqdecode.so")
-SOURCES = ["engine.cu", "noalloc.cu"]
-DEPS = ["engine.cu", "noalloc.cu", "kernels.cuh", "persist.cuh", "gemm_tc.cuh", "common.cuh", "json.hpp"]
+SOURCES = ["engine.cu", "batch.cu", "noalloc.cu"]
+DEPS = SOURCES + ["kernels.cuh", "persist.cuh", "gemm_tc.cuh", "batch.cuh", "internal.cuh", "common.cuh", "json.hpp"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
@@ -37,17 +37,33 @@ def _stale() -> bool:
 def build(force: bool = False, verbose: bool = False) -> str:
     if not force and not _stale():
         return LIB
-    cmd = [nvcc(), "-O3", "-std=c++17", *ARCH, "-lineinfo", "-Xcompiler", "-fPIC,-O3", "-shared",
-           "-I", os.path.join(ROOT, "include"), "-o", LIB + ".tmp"]
+    obj_dir = os.path.join(PKG, "_build")
+    os.makedirs(obj_dir, exist_ok=True)
+    common = [nvcc(), "-O3", "-std=c++17", *ARCH, "-lineinfo", "-Xcompiler", "-fPIC,-O3",
+              "-I", os.path.join(ROOT, "include")]
     if verbose:
-        cmd += ["-Xptxas", "-v"]
-    cmd += [os.path.join(CSRC, s) for s in SOURCES]
-    res = subprocess.run(cmd, capture_output=True, text=True)
+        common += ["-Xptxas", "-v"]
+    # one nvcc per translation unit, in parallel, then one link
+    procs, objs = [], []
+    for src in SOURCES:
+        obj = os.path.join(obj_dir, src.replace(".cu", ".o"))
+        objs.append(obj)
+        procs.append((src, subprocess.Popen(common + ["-c", os.path.join(CSRC, src), "-o", obj],
+                                            stdout=subprocess.PIPE, stderr=subprocess.PIPE, text=True)))
+    failed = False
+    for src, p in procs:
+        out, err = p.communicate()
+        if p.returncode != 0:
+            sys.stderr.write(f"--- {src}\n" + out + err)
+            failed = True
+        elif verbose:
+            sys.stderr.write(err)
+    if failed:
+        raise RuntimeError("nvcc failed building libqdecode.so")
+    res = subprocess.run([nvcc(), *ARCH, "-shared", "-o", LIB + ".tmp", *objs], capture_output=True, text=True)
     if res.returncode != 0:
         sys.stderr.write(res.stdout + res.stderr)
-        raise RuntimeError("nvcc failed building libqdecode.so")
-    if verbose:
-        sys.stderr.write(res.stderr)
+        raise RuntimeError("nvcc failed linking libqdecode.so")
     os.replace(LIB + ".tmp", LIB)
     return LIB
 

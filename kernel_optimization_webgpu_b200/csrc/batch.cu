@@ -1,0 +1,618 @@
+// Batched decode and prefill: B independent sequences on one engine's weights.
+// The host flow per step is the reference's decode token
+// (webgpu-runtime.js:471-604: embedding row, 28 layers, final norm, LM head,
+// argmax fed back) applied to B rows at once; see batch.cuh for the kernels.
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "../../include/qdecode.h"
+#include "batch.cuh"
+#include "gemm_tc.cuh"
+#include "internal.cuh"
+
+using namespace qd;
+
+struct qd_batch {
+  qd_engine* e = nullptr;
+  std::string err;
+  int B = 0, max_seq = 0;
+  int splits = 1, split_len = 512;  // decode attention split-KV
+  int sq = 1, so = 1, sg = 1, sd = 1;  // split-K of the qkv, o, gate/up, down GEMMs
+  int ktq = 0, kto = 0, ktg = 0, ktd = 0;
+  int lm_tiles = 0;
+  void* kv = nullptr;        // K then V caches of every layer
+  size_t kv_layer = 0;       // elements of one layer's K (or V) cache
+  void* dec = nullptr;       // decode step buffers
+  float* h = nullptr;        // [B][H]
+  __half *xh = nullptr, *xl = nullptr;  // [B][max K]
+  float* parts = nullptr;    // split-K partials
+  float* q = nullptr;        // [B][QS]
+  float2* part_ml = nullptr;
+  float* part_o = nullptr;
+  float* logits = nullptr;   // [B][V] (allocated on request)
+  float* lm_pv = nullptr;
+  uint32_t* lm_pi = nullptr;
+  uint32_t* result = nullptr;
+  int *tokens = nullptr, *pos = nullptr, *out = nullptr, *step = nullptr, *errw = nullptr;
+  int max_steps = 0;         // rows of `out`
+  int* pinned = nullptr;     // host staging of generated ids
+  size_t pinned_n = 0;
+  int* pinned_io = nullptr;  // host staging: [0] status word, [16, 16 + 2B) tokens and positions
+  std::vector<int> host_pos;
+  bool keep_logits = false;
+  cudaGraphExec_t g_step[2] = {nullptr, nullptr};  // [keep_logits]
+  // wide buffers (context fill, prefill), grown on demand
+  void* wide = nullptr;
+  long long wide_rows = 0;
+  float *w_h = nullptr, *w_y = nullptr, *w_q = nullptr;
+  __half *w_xh = nullptr, *w_xl = nullptr;
+  int* w_tok = nullptr;
+};
+
+namespace {
+
+int bfail(qd_batch* b, const QdError& err) {
+  if (b) b->err = err.msg;
+  set_thread_error(err.msg);
+  return err.code;
+}
+
+unsigned long long g_attn_smem_mask = 0;
+
+struct Dims {
+  int L, H, I, NH, NKV, QS, KVS, R, V, G;
+  float eps;
+};
+
+Dims dims(const qd_engine* e) {
+  const qd_profile& p = e->p;
+  Dims d;
+  d.L = p.layers; d.H = p.hidden; d.I = p.intermediate; d.NH = p.heads; d.NKV = p.kv_heads;
+  d.QS = p.heads * kHeadDim; d.KVS = p.kv_heads * kHeadDim; d.R = d.QS + 2 * d.KVS; d.V = p.vocab;
+  d.G = p.heads / p.kv_heads; d.eps = p.eps;
+  return d;
+}
+
+__half* kc_of(qd_batch* b, int l) { return static_cast<__half*>(b->kv) + (size_t)l * b->kv_layer; }
+__half* vc_of(qd_batch* b, int l) {
+  return static_cast<__half*>(b->kv) + (size_t)(b->e->p.layers + l) * b->kv_layer;
+}
+
+// q4 record matrix as GEMM weights: row r at base + r * rec (gate/up pairs are
+// [gate j | up j] records, i.e. flat rows 2j and 2j + 1).
+TcArgs q4_args(const char* base, int K, int n_rows) {
+  TcArgs a{};
+  const long long rec = rec_bytes(K), nb = K / kBlockCols;
+  a.w = base;
+  a.s = base + nb * 16;
+  a.w_stride = a.s_stride = rec;
+  a.n_rows = n_rows;
+  a.K = K;
+  return a;
+}
+
+void gemm_q4(const char* base, int K, int n_rows, const __half* xh, const __half* xl, int rows, int splits,
+             int kt_split, float* y, cudaStream_t s, int* err) {
+  TcArgs a = q4_args(base, K, n_rows);
+  a.x_hi = xh;
+  a.x_lo = xl;
+  a.B = rows;
+  a.kt_split = kt_split;
+  a.y = y;
+  a.ldy = n_rows;
+  a.y_split = (long long)rows * n_rows;
+  a.err = err;
+  launch_gemm(a, splits, kGemmQ4Store, s);
+}
+
+void lm_head(qd_batch* b, const __half* xh, const __half* xl, long long ldx, int rows, float* logits, cudaStream_t s) {
+  const Dims d = dims(b->e);
+  TcArgs a{};
+  a.a16 = b->e->embed;
+  a.a16_stride = d.H;
+  a.n_rows = d.V;
+  a.K = d.H;
+  a.kt_split = d.H / kTcK;
+  a.x_hi = xh;
+  a.x_lo = xl;
+  a.ldx = ldx;
+  a.B = rows;
+  a.y = logits;
+  a.ldy = d.V;
+  a.part_v = b->lm_pv;
+  a.part_i = b->lm_pi;
+  a.err = b->errw;
+  launch_gemm(a, 1, kGemmF16Argmax, s);
+}
+
+void launch_attn(qd_batch* b, int l, cudaStream_t s) {
+  const Dims d = dims(b->e);
+  const dim3 grid(d.NKV, b->splits, b->B);
+  const float scale = 1.0f / std::sqrt((float)kHeadDim);
+  if (d.G == 1) {
+    allow_smem(kb_attn<1>, kBAttnSmem, g_attn_smem_mask);
+    launch_ex(kb_attn<1>, grid, dim3(kBAttnThreads), kBAttnSmem, s, (const float*)b->q, (const __half*)kc_of(b, l),
+              (const __half*)vc_of(b, l), (const int*)b->pos, d.NH, d.NKV, b->max_seq, b->split_len, b->splits, scale,
+              b->part_ml, b->part_o, b->errw);
+  } else {
+    allow_smem(kb_attn<2>, kBAttnSmem, g_attn_smem_mask);
+    launch_ex(kb_attn<2>, grid, dim3(kBAttnThreads), kBAttnSmem, s, (const float*)b->q, (const __half*)kc_of(b, l),
+              (const __half*)vc_of(b, l), (const int*)b->pos, d.NH, d.NKV, b->max_seq, b->split_len, b->splits, scale,
+              b->part_ml, b->part_o, b->errw);
+  }
+}
+
+// One decode step of every sequence (launch order: see batch.cuh).
+void enqueue_step(qd_batch* b, bool keep_logits, cudaStream_t s) {
+  qd_engine* e = b->e;
+  const Dims d = dims(e);
+  const int B = b->B;
+  const long long sB = B;
+  const int rope_grid = (int)std::min<long long>((sB * (d.NH + 2 * d.NKV) + 7) / 8, 4096);
+  for (int l = 0; l < d.L; ++l) {
+    const LayerDev& L = e->layers[l];
+    if (l == 0)
+      launch(kb_resid_norm, dim3(B), s, b->h, (const float*)nullptr, 0, 0LL, (const __half*)e->embed,
+             (const int*)b->tokens, d.V, L.n_in, d.H, d.eps, b->xh, b->xl, b->errw);
+    else
+      launch(kb_resid_norm, dim3(B), s, b->h, (const float*)b->parts, b->sd, sB * d.H, (const __half*)nullptr,
+             (const int*)nullptr, d.V, L.n_in, d.H, d.eps, b->xh, b->xl, b->errw);
+    gemm_q4(L.qkv, d.H, d.R, b->xh, b->xl, B, b->sq, b->ktq, b->parts, s, b->errw);
+    launch(kb_rope_cache, dim3(rope_grid), s, (const float*)b->parts, b->sq, sB * d.R, B, d.NH, d.NKV, L.n_q, L.n_k,
+           d.eps, (const float*)e->cos_t, (const float*)e->sin_t, e->opt.rope_row_stride, (const int*)b->pos, 1, 0LL,
+           b->max_seq, kc_of(b, l), vc_of(b, l), b->q, b->errw);
+    launch_attn(b, l, s);
+    launch(kb_attn_combine, dim3(B), s, (const float2*)b->part_ml, (const float*)b->part_o, b->splits, d.NH, b->xh,
+           b->xl);
+    gemm_q4(L.o, d.QS, d.H, b->xh, b->xl, B, b->so, b->kto, b->parts, s, b->errw);
+    launch(kb_resid_norm, dim3(B), s, b->h, (const float*)b->parts, b->so, sB * d.H, (const __half*)nullptr,
+           (const int*)nullptr, d.V, L.n_post, d.H, d.eps, b->xh, b->xl, b->errw);
+    gemm_q4(L.gu, d.H, 2 * d.I, b->xh, b->xl, B, b->sg, b->ktg, b->parts, s, b->errw);
+    const int silu_grid = (int)std::min<long long>((sB * d.I + 255) / 256, 4096);
+    launch(kb_silu_split, dim3(silu_grid), s, (const float*)b->parts, b->sg, sB * 2 * d.I, B, d.I, b->xh, b->xl);
+    gemm_q4(L.d, d.I, d.H, b->xh, b->xl, B, b->sd, b->ktd, b->parts, s, b->errw);
+  }
+  launch(kb_resid_norm, dim3(B), s, b->h, (const float*)b->parts, b->sd, sB * d.H, (const __half*)nullptr,
+         (const int*)nullptr, d.V, (const float*)e->final_norm, d.H, d.eps, b->xh, b->xl, b->errw);
+  lm_head(b, b->xh, b->xl, d.H, B, keep_logits ? b->logits : nullptr, s);
+  BatchState st{b->tokens, b->pos, b->out, b->step, b->max_steps};
+  launch(kb_argmax_merge, dim3((B + 7) / 8), s, (const float*)b->lm_pv, (const uint32_t*)b->lm_pi, b->lm_tiles, B, st,
+         b->result);
+  launch(kb_step_done, dim3(1), s, b->step);
+}
+
+int step_kernel_count(const qd_batch* b) { return b->e->p.layers * 10 + 4; }
+
+void check_err(qd_batch* b) {
+  qd_engine* e = b->e;
+  QD_CK(cudaMemcpyAsync(b->pinned_io, b->errw, 4, cudaMemcpyDeviceToHost, e->stream));
+  QD_CK(cudaStreamSynchronize(e->stream));
+  const int w = b->pinned_io[0];
+  if (!w) return;
+  QD_CK(cudaMemsetAsync(b->errw, 0, 4, e->stream));
+  QD_CK(cudaStreamSynchronize(e->stream));
+  if (w & (kTcErrTimeout | kBErrTimeout)) throw QdError{QD_E_TIMEOUT, "device: a bounded wait expired in a batched kernel"};
+  if (w & kErrToken) throw QdError{QD_E_DEVICE, "device: token id outside the vocabulary"};
+  if (w & kErrPosition) throw QdError{QD_E_DEVICE, "device: position beyond max_seq"};
+  throw QdError{QD_E_DEVICE, "device: status word " + std::to_string(w)};
+}
+
+void ensure_pinned(qd_batch* b, size_t n) {
+  if (b->pinned_n >= n) return;
+  if (b->pinned) cudaFreeHost(b->pinned);
+  b->pinned = nullptr;
+  b->pinned_n = 0;
+  if (cudaHostAlloc(reinterpret_cast<void**>(&b->pinned), n * 4, cudaHostAllocDefault) != cudaSuccess)
+    throw QdError{QD_E_NOMEM, "cannot allocate pinned host memory"};
+  b->pinned_n = n;
+}
+
+// Wide buffers for `rows` rows at once (context fill chunks, prefill).
+void ensure_wide(qd_batch* b, long long rows) {
+  if (b->wide_rows >= rows) return;
+  const Dims d = dims(b->e);
+  if (b->wide) {
+    QD_CK(cudaStreamSynchronize(b->e->stream));
+    cudaFree(b->wide);
+    b->wide = nullptr;
+    b->wide_rows = 0;
+  }
+  const long long maxk = std::max(std::max(d.H, d.QS), d.I);
+  const long long maxn = std::max(d.R, 2 * d.I);
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off += (bytes + 255) & ~size_t(255);
+    return o;
+  };
+  const size_t o_h = take(rows * d.H * 4), o_y = take(rows * maxn * 4), o_q = take(rows * d.QS * 4);
+  const size_t o_xh = take(rows * maxk * 2), o_xl = take(rows * maxk * 2), o_tok = take(rows * 4);
+  if (cudaMalloc(&b->wide, off) != cudaSuccess) throw QdError{QD_E_NOMEM, "cannot allocate prefill buffers"};
+  char* base = static_cast<char*>(b->wide);
+  b->w_h = reinterpret_cast<float*>(base + o_h);
+  b->w_y = reinterpret_cast<float*>(base + o_y);
+  b->w_q = reinterpret_cast<float*>(base + o_q);
+  b->w_xh = reinterpret_cast<__half*>(base + o_xh);
+  b->w_xl = reinterpret_cast<__half*>(base + o_xl);
+  b->w_tok = reinterpret_cast<int*>(base + o_tok);
+  b->wide_rows = rows;
+}
+
+void drop_graphs(qd_batch* b) {
+  for (auto& g : b->g_step)
+    if (g) {
+      cudaGraphExecDestroy(g);
+      g = nullptr;
+    }
+}
+
+cudaGraphExec_t capture_step(qd_batch* b, bool keep_logits) {
+  qd_engine* e = b->e;
+  cudaGraph_t g = nullptr;
+  QD_CK(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal));
+  try {
+    enqueue_step(b, keep_logits, e->stream);
+  } catch (...) {
+    cudaStreamEndCapture(e->stream, &g);
+    if (g) cudaGraphDestroy(g);
+    throw;
+  }
+  QD_CK(cudaStreamEndCapture(e->stream, &g));
+  cudaGraphExec_t x = nullptr;
+  const cudaError_t rc = cudaGraphInstantiate(&x, g, 0);
+  cudaGraphDestroy(g);
+  QD_CK(rc);
+  return x;
+}
+
+void free_batch(qd_batch* b) {
+  if (!b) return;
+  if (b->e) {
+    cudaSetDevice(b->e->dev);
+    cudaStreamSynchronize(b->e->stream);
+  }
+  drop_graphs(b);
+  if (b->kv) cudaFree(b->kv);
+  if (b->dec) cudaFree(b->dec);
+  if (b->logits) cudaFree(b->logits);
+  if (b->wide) cudaFree(b->wide);
+  if (b->pinned) cudaFreeHost(b->pinned);
+  if (b->pinned_io) cudaFreeHost(b->pinned_io);
+  delete b;
+}
+
+void create_batch(qd_engine* e, int B, int max_seq, qd_batch* b) {
+  const Dims d = dims(e);
+  if (B < 1 || B > 65535) throw QdError{QD_E_INVALID, "batch must be 1..65535"};
+  if (max_seq < 1) throw QdError{QD_E_INVALID, "max_seq must be positive"};
+  if (d.G != 1 && d.G != 2) throw QdError{QD_E_INVALID, "batched attention supports q_heads / kv_heads of 1 or 2"};
+  if (d.H % kTcK || d.QS % kTcK || d.I % kTcK) throw QdError{QD_E_INVALID, "batched path: hidden, q and intermediate sizes must be multiples of 64"};
+  if (d.H > 4096) throw QdError{QD_E_INVALID, "batched path: hidden size above 4096"};
+  const long long last = (long long)(max_seq - 1) * e->opt.rope_row_stride + kHeadDim / 2;
+  if (last > (long long)e->p.rope_rows * (kHeadDim / 2))
+    throw QdError{QD_E_RANGE, "max_seq beyond the RoPE table for this row stride"};
+  b->e = e;
+  b->B = B;
+  b->max_seq = max_seq;
+  // Decode attention: 512-position splits (fewer for short contexts).
+  b->split_len = std::min(512, (max_seq + kBAttnTile - 1) / kBAttnTile * kBAttnTile);
+  b->splits = (max_seq + b->split_len - 1) / b->split_len;
+  // Split-K so that each GEMM launches about one CTA per SM.
+  auto plan = [&](int n_rows, int K, int* kt) {
+    const int tiles = (n_rows + kTcM - 1) / kTcM * ((B + 255) / 256);
+    return gemm_plan_splits(K, std::max(1, e->sms / std::max(1, tiles)), kt);
+  };
+  b->sq = plan(d.R, d.H, &b->ktq);
+  b->so = plan(d.H, d.QS, &b->kto);
+  b->sg = plan(2 * d.I, d.H, &b->ktg);
+  b->sd = plan(d.H, d.I, &b->ktd);
+  b->lm_tiles = (d.V + kTcM - 1) / kTcM;
+
+  b->kv_layer = (size_t)B * d.NKV * max_seq * kHeadDim;
+  const size_t kv_bytes = b->kv_layer * 2 * 2 * d.L;
+  if (cudaMalloc(&b->kv, kv_bytes) != cudaSuccess)
+    throw QdError{QD_E_NOMEM, "cannot allocate the batch KV cache (" + std::to_string(kv_bytes >> 20) + " MiB)"};
+  QD_CK(cudaMemsetAsync(b->kv, 0, kv_bytes, e->stream));
+
+  const long long maxk = std::max(std::max(d.H, d.QS), d.I);
+  const long long parts = std::max(std::max((long long)b->sq * d.R, (long long)b->so * d.H),
+                                   std::max((long long)b->sg * 2 * d.I, (long long)b->sd * d.H)) *
+                          B;
+  b->max_steps = 256;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off += (bytes + 255) & ~size_t(255);
+    return o;
+  };
+  const size_t o_h = take((size_t)B * d.H * 4), o_xh = take((size_t)B * maxk * 2), o_xl = take((size_t)B * maxk * 2);
+  const size_t o_p = take((size_t)parts * 4), o_q = take((size_t)B * d.QS * 4);
+  const size_t o_ml = take((size_t)B * b->splits * d.NH * 8), o_po = take((size_t)B * b->splits * d.QS * 4);
+  const size_t o_pv = take((size_t)B * b->lm_tiles * 4), o_pi = take((size_t)B * b->lm_tiles * 4);
+  const size_t o_res = take((size_t)B * 8), o_tok = take((size_t)B * 4), o_pos = take((size_t)B * 4);
+  const size_t o_out = take((size_t)b->max_steps * B * 4), o_step = take(4), o_err = take(4);
+  if (cudaMalloc(&b->dec, off) != cudaSuccess) throw QdError{QD_E_NOMEM, "cannot allocate batch step buffers"};
+  QD_CK(cudaMemsetAsync(b->dec, 0, off, e->stream));
+  char* base = static_cast<char*>(b->dec);
+  b->h = reinterpret_cast<float*>(base + o_h);
+  b->xh = reinterpret_cast<__half*>(base + o_xh);
+  b->xl = reinterpret_cast<__half*>(base + o_xl);
+  b->parts = reinterpret_cast<float*>(base + o_p);
+  b->q = reinterpret_cast<float*>(base + o_q);
+  b->part_ml = reinterpret_cast<float2*>(base + o_ml);
+  b->part_o = reinterpret_cast<float*>(base + o_po);
+  b->lm_pv = reinterpret_cast<float*>(base + o_pv);
+  b->lm_pi = reinterpret_cast<uint32_t*>(base + o_pi);
+  b->result = reinterpret_cast<uint32_t*>(base + o_res);
+  b->tokens = reinterpret_cast<int*>(base + o_tok);
+  b->pos = reinterpret_cast<int*>(base + o_pos);
+  b->out = reinterpret_cast<int*>(base + o_out);
+  b->step = reinterpret_cast<int*>(base + o_step);
+  b->errw = reinterpret_cast<int*>(base + o_err);
+  b->host_pos.assign(B, 0);
+  ensure_pinned(b, (size_t)b->max_steps * B);
+  if (cudaHostAlloc(reinterpret_cast<void**>(&b->pinned_io), (2 * (size_t)B + 16) * 4, cudaHostAllocDefault) != cudaSuccess)
+    throw QdError{QD_E_NOMEM, "cannot allocate pinned host memory"};
+  QD_CK(cudaStreamSynchronize(e->stream));
+}
+
+void upload_tokens_positions(qd_batch* b, const int32_t* tokens, const int32_t* positions) {
+  qd_engine* e = b->e;
+  const int B = b->B;
+  QD_CK(cudaStreamSynchronize(e->stream));
+  int* stage = b->pinned_io + 16;
+  if (tokens) {
+    std::memcpy(stage, tokens, (size_t)B * 4);
+    QD_CK(cudaMemcpyAsync(b->tokens, stage, (size_t)B * 4, cudaMemcpyHostToDevice, e->stream));
+  }
+  if (positions) {
+    std::memcpy(stage + B, positions, (size_t)B * 4);
+    QD_CK(cudaMemcpyAsync(b->pos, stage + B, (size_t)B * 4, cudaMemcpyHostToDevice, e->stream));
+  }
+  QD_CK(cudaStreamSynchronize(e->stream));
+  if (positions) b->host_pos.assign(positions, positions + B);
+}
+
+// ---- context fill -------------------------------------------------------------
+void fill_context(qd_batch* b, int ctx, uint32_t seed) {
+  qd_engine* e = b->e;
+  const Dims d = dims(e);
+  cudaStream_t s = e->stream;
+  const long long rows = (long long)b->B * ctx;
+  const long long chunk = std::min<long long>(rows, 16384);
+  ensure_wide(b, chunk);
+  for (int l = 0; l < d.L; ++l) {
+    const LayerDev& L = e->layers[l];
+    for (long long r0 = 0; r0 < rows; r0 += chunk) {
+      const int R = (int)std::min(chunk, rows - r0);
+      launch(kb_ctx_hidden, dim3(R), s, seed, (uint32_t)l, r0, d.H, L.n_in, d.eps, b->w_xh, b->w_xl);
+      // k and v rows of the fused qkv matrix
+      gemm_q4(L.qkv + (size_t)d.QS * rec_bytes(d.H), d.H, 2 * d.KVS, b->w_xh, b->w_xl, R, 1, d.H / kTcK, b->w_y, s,
+              b->errw);
+      const int grid = (int)std::min<long long>(((long long)R * 2 * d.NKV + 7) / 8, 8192);
+      launch(kb_rope_cache, dim3(grid), s, (const float*)b->w_y, 1, 0LL, R, 0, d.NKV, L.n_q, L.n_k, d.eps,
+             (const float*)e->cos_t, (const float*)e->sin_t, e->opt.rope_row_stride, (const int*)nullptr, ctx, r0,
+             b->max_seq, kc_of(b, l), vc_of(b, l), (float*)nullptr, b->errw);
+    }
+  }
+  std::vector<int32_t> p(b->B, ctx);
+  QD_CK(cudaStreamSynchronize(s));
+  check_err(b);
+  upload_tokens_positions(b, nullptr, p.data());
+}
+
+// ---- decode loop ----------------------------------------------------------------
+void decode(qd_batch* b, int steps, int32_t* out_ids) {
+  qd_engine* e = b->e;
+  cudaStream_t s = e->stream;
+  const int B = b->B;
+  for (int i = 0; i < B; ++i)
+    if (b->host_pos[i] < 0 || (long long)b->host_pos[i] + steps > b->max_seq)
+      throw QdError{QD_E_RANGE, "sequence " + std::to_string(i) + ": position + steps beyond max_seq"};
+  const int k = b->keep_logits ? 1 : 0;
+  if (!b->g_step[k]) b->g_step[k] = capture_step(b, b->keep_logits);
+  for (int done = 0; done < steps;) {
+    const int n = std::min(steps - done, b->max_steps);
+    QD_CK(cudaMemsetAsync(b->step, 0, 4, s));
+    for (int i = 0; i < n; ++i) QD_CK(cudaGraphLaunch(b->g_step[k], s));
+    if (out_ids) QD_CK(cudaMemcpyAsync(b->pinned, b->out, (size_t)n * B * 4, cudaMemcpyDeviceToHost, s));
+    QD_CK(cudaStreamSynchronize(s));
+    check_err(b);
+    if (out_ids) std::memcpy(out_ids + (size_t)done * B, b->pinned, (size_t)n * B * 4);
+    done += n;
+  }
+  for (int i = 0; i < B; ++i) b->host_pos[i] += steps;
+}
+
+}  // namespace
+
+extern "C" {
+
+int qd_batch_create(qd_engine* e, int batch, int max_seq, qd_batch** out) {
+  if (!out) return bfail(nullptr, QdError{QD_E_INVALID, "NULL out"});
+  *out = nullptr;
+  if (!e) return bfail(nullptr, QdError{QD_E_INVALID, "NULL engine"});
+  qd_batch* b = new qd_batch();
+  try {
+    QD_CK(cudaSetDevice(e->dev));
+    create_batch(e, batch, max_seq, b);
+  } catch (const QdError& err) {
+    const int rc = bfail(nullptr, err);
+    free_batch(b);
+    return rc;
+  }
+  *out = b;
+  return QD_OK;
+}
+
+void qd_batch_destroy(qd_batch* b) { free_batch(b); }
+
+int qd_batch_size(const qd_batch* b, int* batch, int* max_seq) {
+  if (!b) return bfail(nullptr, QdError{QD_E_INVALID, "NULL batch"});
+  if (batch) *batch = b->B;
+  if (max_seq) *max_seq = b->max_seq;
+  return QD_OK;
+}
+
+int qd_batch_fill_context(qd_batch* b, int ctx, uint32_t seed) {
+  if (!b) return bfail(nullptr, QdError{QD_E_INVALID, "NULL batch"});
+  try {
+    if (ctx < 0 || ctx > b->max_seq) throw QdError{QD_E_RANGE, "ctx must be 0..max_seq"};
+    if ((long long)b->B * ctx >= (1ll << 31) / std::max(1, b->e->p.hidden) * 1ll)
+      throw QdError{QD_E_RANGE, "batch * ctx * hidden beyond the context generator's 32-bit row index"};
+    QD_CK(cudaSetDevice(b->e->dev));
+    if (ctx == 0) {
+      std::vector<int32_t> p(b->B, 0);
+      upload_tokens_positions(b, nullptr, p.data());
+      return QD_OK;
+    }
+    fill_context(b, ctx, seed);
+  } catch (const QdError& err) {
+    return bfail(b, err);
+  }
+  return QD_OK;
+}
+
+int qd_batch_set_tokens(qd_batch* b, const int32_t* tokens, const int32_t* positions) {
+  if (!b) return bfail(nullptr, QdError{QD_E_INVALID, "NULL batch"});
+  try {
+    const int V = b->e->p.vocab;
+    for (int i = 0; tokens && i < b->B; ++i)
+      if (tokens[i] < 0 || tokens[i] >= V) throw QdError{QD_E_RANGE, "token id outside the vocabulary"};
+    for (int i = 0; positions && i < b->B; ++i)
+      if (positions[i] < 0 || positions[i] >= b->max_seq) throw QdError{QD_E_RANGE, "position outside 0..max_seq-1"};
+    QD_CK(cudaSetDevice(b->e->dev));
+    upload_tokens_positions(b, tokens, positions);
+  } catch (const QdError& err) {
+    return bfail(b, err);
+  }
+  return QD_OK;
+}
+
+int qd_batch_positions(qd_batch* b, int32_t* positions) {
+  if (!b || !positions) return bfail(b, QdError{QD_E_INVALID, "NULL argument"});
+  std::copy(b->host_pos.begin(), b->host_pos.end(), positions);
+  return QD_OK;
+}
+
+int qd_batch_decode(qd_batch* b, int steps, int32_t* out_ids) {
+  if (!b) return bfail(nullptr, QdError{QD_E_INVALID, "NULL batch"});
+  try {
+    if (steps < 0) throw QdError{QD_E_INVALID, "steps must be >= 0"};
+    QD_CK(cudaSetDevice(b->e->dev));
+    decode(b, steps, out_ids);
+  } catch (const QdError& err) {
+    return bfail(b, err);
+  }
+  return QD_OK;
+}
+
+int qd_batch_keep_logits(qd_batch* b, int keep) {
+  if (!b) return bfail(nullptr, QdError{QD_E_INVALID, "NULL batch"});
+  try {
+    QD_CK(cudaSetDevice(b->e->dev));
+    if (keep && !b->logits) {
+      const size_t n = (size_t)b->B * b->e->p.vocab * 4;
+      if (cudaMalloc(&b->logits, n) != cudaSuccess) throw QdError{QD_E_NOMEM, "cannot allocate batch logits"};
+      QD_CK(cudaMemset(b->logits, 0, n));
+    }
+    b->keep_logits = keep != 0;
+  } catch (const QdError& err) {
+    return bfail(b, err);
+  }
+  return QD_OK;
+}
+
+int qd_batch_logits(qd_batch* b, float* host_logits) {
+  if (!b || !host_logits) return bfail(b, QdError{QD_E_INVALID, "NULL argument"});
+  try {
+    if (!b->logits) throw QdError{QD_E_INVALID, "logits are not kept (qd_batch_keep_logits)"};
+    QD_CK(cudaSetDevice(b->e->dev));
+    QD_CK(cudaStreamSynchronize(b->e->stream));
+    QD_CK(cudaMemcpy(host_logits, b->logits, (size_t)b->B * b->e->p.vocab * 4, cudaMemcpyDeviceToHost));
+  } catch (const QdError& err) {
+    return bfail(b, err);
+  }
+  return QD_OK;
+}
+
+static void kv_range_check(qd_batch* b, int layer, int seq, int pos0, int count) {
+  if (layer < 0 || layer >= b->e->p.layers || seq < 0 || seq >= b->B || pos0 < 0 || count < 0 ||
+      (long long)pos0 + count > b->max_seq)
+    throw QdError{QD_E_RANGE, "KV rows outside the batch cache"};
+}
+
+int qd_batch_read_kv(qd_batch* b, int layer, int seq, int pos0, int count, float* k, float* v) {
+  if (!b || !k || !v) return bfail(b, QdError{QD_E_INVALID, "NULL argument"});
+  try {
+    kv_range_check(b, layer, seq, pos0, count);
+    QD_CK(cudaSetDevice(b->e->dev));
+    QD_CK(cudaStreamSynchronize(b->e->stream));
+    const int NKV = b->e->p.kv_heads;
+    std::vector<__half> tmp((size_t)count * kHeadDim);
+    for (int which = 0; which < 2; ++which) {
+      const __half* cache = which ? vc_of(b, layer) : kc_of(b, layer);
+      float* dst = which ? v : k;
+      for (int g = 0; g < NKV; ++g) {
+        const __half* src = cache + (((size_t)seq * NKV + g) * b->max_seq + pos0) * kHeadDim;
+        QD_CK(cudaMemcpy(tmp.data(), src, tmp.size() * 2, cudaMemcpyDeviceToHost));
+        for (int r = 0; r < count; ++r)
+          for (int c = 0; c < kHeadDim; ++c)
+            dst[((size_t)r * NKV + g) * kHeadDim + c] = __half2float(tmp[(size_t)r * kHeadDim + c]);
+      }
+    }
+  } catch (const QdError& err) {
+    return bfail(b, err);
+  }
+  return QD_OK;
+}
+
+int qd_batch_write_kv(qd_batch* b, int layer, int seq, int pos0, int count, const float* k, const float* v) {
+  if (!b || !k || !v) return bfail(b, QdError{QD_E_INVALID, "NULL argument"});
+  try {
+    kv_range_check(b, layer, seq, pos0, count);
+    QD_CK(cudaSetDevice(b->e->dev));
+    QD_CK(cudaStreamSynchronize(b->e->stream));
+    const int NKV = b->e->p.kv_heads;
+    std::vector<__half> tmp((size_t)count * kHeadDim);
+    for (int which = 0; which < 2; ++which) {
+      __half* cache = which ? vc_of(b, layer) : kc_of(b, layer);
+      const float* src = which ? v : k;
+      for (int g = 0; g < NKV; ++g) {
+        for (int r = 0; r < count; ++r)
+          for (int c = 0; c < kHeadDim; ++c)
+            tmp[(size_t)r * kHeadDim + c] = __float2half_rn(src[((size_t)r * NKV + g) * kHeadDim + c]);
+        __half* dst = cache + (((size_t)seq * NKV + g) * b->max_seq + pos0) * kHeadDim;
+        QD_CK(cudaMemcpy(dst, tmp.data(), tmp.size() * 2, cudaMemcpyHostToDevice));
+      }
+    }
+  } catch (const QdError& err) {
+    return bfail(b, err);
+  }
+  return QD_OK;
+}
+
+int qd_batch_step_kernels(const qd_batch* b) { return b ? step_kernel_count(b) : 0; }
+
+int qd_batch_prefill(qd_batch* b, const int32_t* ids, int n_prompt, int32_t* first_ids) {
+  (void)ids;
+  (void)n_prompt;
+  (void)first_ids;
+  return bfail(b, QdError{QD_E_INVALID, "batched prefill is not available in this build"});
+}
+
+int qd_generate_batch(qd_engine* e, int batch, const int32_t* ids, int n_prompt, int max_new_tokens,
+                      int32_t* out_ids) {
+  (void)e;
+  (void)batch;
+  (void)ids;
+  (void)n_prompt;
+  (void)max_new_tokens;
+  (void)out_ids;
+  return bfail(nullptr, QdError{QD_E_INVALID, "batched prefill is not available in this build"});
+}
+
+}  // extern "C"

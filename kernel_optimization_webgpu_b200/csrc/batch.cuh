@@ -1,0 +1,502 @@
+// Batched decode and prefill kernels: many independent sequences advance
+// together, so the q4 projections and the LM head are dense contractions on the
+// tensor cores (gemm_tc.cuh) and everything between two GEMMs is one fused
+// kernel that also sums the GEMM's split-K partials in a fixed order.
+//
+// Layer order per step (the reference's decode layer, webgpu-runtime.js:498-562,
+// with B rows instead of one):
+//   kb_resid_norm   h += sum(partials of the previous down GEMM); x = rms(h)*w_in -> hi/lo
+//   GEMM qkv        [B][q|k|v] partials
+//   kb_rope_cache   head RMSNorm + RoPE on q and k, K/V rows appended to the cache
+//   kb_attn         split-KV attention, K/V tiles bulk-copied into shared memory
+//   kb_attn_combine splits merged -> hi/lo operand of the o GEMM
+//   GEMM o          partials
+//   kb_resid_norm   h += sum(o partials); x = rms(h)*w_post -> hi/lo
+//   GEMM gate/up    interleaved partials
+//   kb_silu_split   silu(gate)*up -> hi/lo
+//   GEMM down       partials (consumed by the next layer's kb_resid_norm)
+// and after the last layer kb_resid_norm with the final norm, the LM head GEMM
+// with its (max, index) epilogue and kb_argmax_merge.
+//
+// KV cache of the batched path: [layer][seq][kv_head][pos][128] f16, so the 64
+// cached rows of one (sequence, KV head) tile are one contiguous 16 KB range
+// that a single cp.async.bulk moves into shared memory.
+#pragma once
+
+#include "common.cuh"
+#include "gemm_tc.cuh"
+
+namespace qd {
+
+constexpr int kBAttnTile = 64;  // positions per staged K/V tile
+constexpr int kBAttnThreads = 256;
+constexpr int kBErrTimeout = 16;
+// Dynamic shared memory of kb_attn: two stages of K and V tiles.
+constexpr int kBAttnSmem = 2 * 2 * kBAttnTile * kHeadDim * 2;
+
+struct BatchState {
+  int* tokens;    // [B] input token of the step (the previous step's output)
+  int* pos;       // [B] position the step writes and attends up to
+  int* out;       // [max_steps][B] generated ids
+  int* step;      // [1] steps taken since the last reset
+  int max_steps;
+};
+
+// Sum of the split-K partials of element i: parts[s * stride + i], s ascending.
+__device__ __forceinline__ float sum_parts(const float* parts, int nparts, long long stride, long long i) {
+  float v = parts[i];
+  for (int s = 1; s < nparts; ++s) v += parts[(long long)s * stride + i];
+  return v;
+}
+
+// ---- residual + RMSNorm into the GEMM's hi/lo operands ----------------------------
+// Row b: h[b] = embed row of tokens[b] (embedding mode), or h[b] + sum(parts)
+// (residual mode; parts == nullptr leaves h as is); then
+// x = rms_norm(h[b]) * w -> x_hi[b], x_lo[b]. h is written back in place.
+static __global__ void __launch_bounds__(256) kb_resid_norm(float* h, const float* parts, int nparts, long long part_stride,
+                                                     const __half* embed, const int* tokens, int vocab, const float* w,
+                                                     int K, float eps, __half* x_hi, __half* x_lo, int* err) {
+  __shared__ float red[8];
+  pdl_wait();
+  const int b = blockIdx.x;
+  float* hr = h + (long long)b * K;
+  const __half* er = nullptr;
+  if (embed) {
+    int tok = tokens[b];
+    if (tok < 0 || tok >= vocab) {
+      if (threadIdx.x == 0) atomicOr(err, kErrToken);
+      tok = 0;
+    }
+    er = embed + (long long)tok * K;
+  }
+  float ss = 0.0f;
+  for (int e = threadIdx.x; e < K; e += 256) {
+    float v;
+    if (er) v = __half2float(er[e]);
+    else if (parts) v = hr[e] + sum_parts(parts, nparts, part_stride, (long long)b * K + e);
+    else v = hr[e];
+    if (er || parts) hr[e] = v;
+    ss += v * v;
+  }
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  pdl_trigger();
+  float t = 0.0f;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) t += red[k];
+  const float inv = rsqrtf(t / (float)K + eps);
+  for (int e = threadIdx.x; e < K; e += 256) {
+    __half hi, lo;
+    split_f16(hr[e] * inv * w[e], hi, lo);
+    x_hi[(long long)b * K + e] = hi;
+    x_lo[(long long)b * K + e] = lo;
+  }
+}
+
+// ---- head RMSNorm + RoPE + KV append --------------------------------------------
+// Row r of a GEMM output laid out [q_heads*128 | NKV*128 (k) | NKV*128 (v)]
+// (split-K partials, summed here). Row r belongs to sequence
+// seq = (row0 + r) / rows_per_seq at position
+// (pos ? pos[seq] : 0) + (row0 + r) % rows_per_seq.
+// One warp per head task: q heads are normalised, rotated and stored to q_out
+// [r][q_heads*128]; k heads normalised, rotated (rope.wgsl:14-31, table offset
+// position * row_stride + pair) and appended to the cache; v heads appended as
+// projected. Cache row (seq, g, p) sits at ((seq*NKV + g)*max_seq + p)*128.
+static __global__ void __launch_bounds__(256) kb_rope_cache(const float* parts, int nparts, long long part_stride, int R,
+                                                     int q_heads, int NKV, const float* norm_q, const float* norm_k,
+                                                     float eps, const float* cos_t, const float* sin_t, int row_stride,
+                                                     const int* pos, int rows_per_seq, long long row0, int max_seq,
+                                                     __half* kc, __half* vc, float* q_out, int* err) {
+  pdl_wait();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tasks = q_heads + 2 * NKV;
+  const int ld = tasks * kHeadDim;
+  const long long nt = (long long)R * tasks;
+  for (long long task = (long long)blockIdx.x * 8 + warp; task < nt; task += (long long)gridDim.x * 8) {
+    const int r = (int)(task / tasks), t = (int)(task % tasks);
+    const long long grow = row0 + r;
+    const int seq = (int)(grow / rows_per_seq);
+    const int p = (pos ? pos[seq] : 0) + (int)(grow % rows_per_seq);
+    if (p < 0 || p >= max_seq) {
+      if (lane == 0) atomicOr(err, kErrPosition);
+      continue;
+    }
+    const long long base = (long long)r * ld + (long long)t * kHeadDim + 4 * lane;
+    float4 x;
+    x.x = sum_parts(parts, nparts, part_stride, base);
+    x.y = sum_parts(parts, nparts, part_stride, base + 1);
+    x.z = sum_parts(parts, nparts, part_stride, base + 2);
+    x.w = sum_parts(parts, nparts, part_stride, base + 3);
+    if (t >= q_heads + NKV) {  // v: cached as projected
+      const int g = t - q_heads - NKV;
+      __half* dst = vc + (((long long)seq * NKV + g) * max_seq + p) * kHeadDim + 4 * lane;
+      reinterpret_cast<__half2*>(dst)[0] = __floats2half2_rn(x.x, x.y);
+      reinterpret_cast<__half2*>(dst)[1] = __floats2half2_rn(x.z, x.w);
+      continue;
+    }
+    const float* nw = t < q_heads ? norm_q : norm_k;
+    float ss = x.x * x.x + x.y * x.y + x.z * x.z + x.w * x.w;
+    ss = warp_sum(ss);
+    const float inv = rsqrtf(ss / (float)kHeadDim + eps);
+    const float4 w4 = reinterpret_cast<const float4*>(nw)[lane];
+    const float4 y = make_float4(x.x * inv * w4.x, x.y * inv * w4.y, x.z * inv * w4.z, x.w * inv * w4.w);
+    // rotate-half: dims d and d +- 64 sit 16 lanes apart
+    float4 pr;
+    pr.x = __shfl_xor_sync(0xffffffffu, y.x, 16);
+    pr.y = __shfl_xor_sync(0xffffffffu, y.y, 16);
+    pr.z = __shfl_xor_sync(0xffffffffu, y.z, 16);
+    pr.w = __shfl_xor_sync(0xffffffffu, y.w, 16);
+    const int pair0 = (4 * lane) & (kHeadDim / 2 - 1);
+    const long long toff = (long long)p * row_stride + pair0;
+    const float4 c = *reinterpret_cast<const float4*>(cos_t + toff);
+    const float4 s = *reinterpret_cast<const float4*>(sin_t + toff);
+    const float sg = lane < 16 ? -1.0f : 1.0f;  // first half: x*cos - x[d+64]*sin
+    const float4 o = make_float4(y.x * c.x + sg * pr.x * s.x, y.y * c.y + sg * pr.y * s.y,
+                                 y.z * c.z + sg * pr.z * s.z, y.w * c.w + sg * pr.w * s.w);
+    if (t < q_heads) {
+      reinterpret_cast<float4*>(q_out + (long long)r * q_heads * kHeadDim + (long long)t * kHeadDim)[lane] = o;
+    } else {
+      const int g = t - q_heads;
+      __half* dst = kc + (((long long)seq * NKV + g) * max_seq + p) * kHeadDim + 4 * lane;
+      reinterpret_cast<__half2*>(dst)[0] = __floats2half2_rn(o.x, o.y);
+      reinterpret_cast<__half2*>(dst)[1] = __floats2half2_rn(o.z, o.w);
+    }
+  }
+  pdl_trigger();
+}
+
+// ---- split-KV decode attention with bulk-copy staging ------------------------------
+// Grid (NKV, splits, B); 256 threads serve the G query heads of KV head g.
+// The CTA covers positions [sp*split_len, min(len, (sp+1)*split_len)) of
+// sequence b, len = pos[b] + 1, in 64-position tiles double-buffered through
+// shared memory (one cp.async.bulk per tile for K and one for V), with an
+// online softmax. Scores: one warp per position (lane = 4 dims). P*V: thread
+// = (position group of 4, dim pair), all G heads at once; groups merged at the end.
+// Partials: ml[b][sp][h] = (running max, sum of exp), o[b][sp][h][128] unnormalised.
+template <int G>
+__global__ void __launch_bounds__(kBAttnThreads) kb_attn(const float* q, const __half* kc, const __half* vc,
+                                                          const int* pos, int NH, int NKV, int max_seq, int split_len,
+                                                          int splits, float scale, float2* part_ml, float* part_o,
+                                                          int* err) {
+  extern __shared__ __align__(128) unsigned char attn_smem[];
+  __half* ks = reinterpret_cast<__half*>(attn_smem);                  // [2][64][128]
+  __half* vs = ks + 2 * kBAttnTile * kHeadDim;                        // [2][64][128]
+  __shared__ __align__(16) float qsm[G][kHeadDim];
+  __shared__ __align__(16) float sc[kBAttnTile][G];
+  __shared__ float run_m[G], run_l[G], tile_f[G];
+  __shared__ __align__(16) float red[3][G][kHeadDim];
+  __shared__ unsigned long long mbar[2];
+  const int g = blockIdx.x, sp = blockIdx.y, b = blockIdx.z;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (tid == 0) {
+    tc_mbar_init(&mbar[0]);
+    tc_mbar_init(&mbar[1]);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  pdl_wait();
+  const int len = min(pos[b], max_seq - 1) + 1;
+  const int lo = sp * split_len, hi = min(len, lo + split_len);
+  const long long slot = ((long long)b * splits + sp) * NH + (long long)g * G;
+  if (lo >= hi) {
+    if (tid < G) part_ml[slot + tid] = make_float2(-INFINITY, 0.0f);
+    for (int e = tid; e < G * kHeadDim; e += kBAttnThreads) part_o[slot * kHeadDim + e] = 0.0f;
+    pdl_trigger();
+    return;
+  }
+  const __half* kbase = kc + ((long long)b * NKV + g) * max_seq * kHeadDim;
+  const __half* vbase = vc + ((long long)b * NKV + g) * max_seq * kHeadDim;
+  const int nt = (hi - lo + kBAttnTile - 1) / kBAttnTile;
+  auto issue = [&](int t) {  // one thread: tile t into buffer t & 1
+    const int p0 = lo + t * kBAttnTile;
+    const int n = min(kBAttnTile, hi - p0);
+    const unsigned bytes = (unsigned)n * kHeadDim * 2;
+    unsigned long long* mb = &mbar[t & 1];
+    __half* kd = ks + (t & 1) * kBAttnTile * kHeadDim;
+    __half* vd = vs + (t & 1) * kBAttnTile * kHeadDim;
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(tc_smem(mb)), "r"(2 * bytes)
+                 : "memory");
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     tc_smem(kd)),
+                 "l"(kbase + (long long)p0 * kHeadDim), "r"(bytes), "r"(tc_smem(mb))
+                 : "memory");
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     tc_smem(vd)),
+                 "l"(vbase + (long long)p0 * kHeadDim), "r"(bytes), "r"(tc_smem(mb))
+                 : "memory");
+  };
+  __syncthreads();  // barrier init visible
+  if (tid == 0) {
+    issue(0);
+    if (nt > 1) issue(1);
+  }
+  for (int e = tid; e < G * kHeadDim; e += kBAttnThreads)
+    qsm[e / kHeadDim][e % kHeadDim] = q[((long long)b * NH + (long long)g * G) * kHeadDim + e];
+  if (tid < G) {
+    run_m[tid] = -INFINITY;
+    run_l[tid] = 0.0f;
+  }
+  __syncthreads();
+  float4 qv[G];
+#pragma unroll
+  for (int h = 0; h < G; ++h) qv[h] = reinterpret_cast<const float4*>(qsm[h])[lane];
+  const int dp = tid & 63, grp = tid >> 6;  // P*V: dims 2dp, 2dp+1; positions j = grp mod 4
+  float acc[G][2];
+#pragma unroll
+  for (int h = 0; h < G; ++h) acc[h][0] = acc[h][1] = 0.0f;
+  int failed_at = -1;
+
+  for (int t = 0; t < nt; ++t) {
+    const int buf = t & 1;
+    const int n = min(kBAttnTile, hi - (lo + t * kBAttnTile));
+    const bool ok = tc_mbar_wait(&mbar[buf], (unsigned)(t >> 1) & 1u);
+    if (__syncthreads_or(!ok)) {
+      failed_at = t;
+      break;
+    }
+    const __half* kt = ks + buf * kBAttnTile * kHeadDim;
+    const __half* vt = vs + buf * kBAttnTile * kHeadDim;
+    for (int j = warp; j < n; j += 8) {
+      const uint2 u = *reinterpret_cast<const uint2*>(kt + j * kHeadDim + 4 * lane);
+      const float2 k01 = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+      const float2 k23 = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+#pragma unroll
+      for (int h = 0; h < G; ++h) {
+        float d = qv[h].x * k01.x + qv[h].y * k01.y + qv[h].z * k23.x + qv[h].w * k23.y;
+        d = warp_sum(d);
+        if (lane == 0) sc[j][h] = d * scale;
+      }
+    }
+    __syncthreads();
+    if (warp < G) {  // tile max, probabilities, running max / sum of head `warp`
+      const int h = warp;
+      float tm = -INFINITY;
+      for (int j = lane; j < n; j += 32) tm = fmaxf(tm, sc[j][h]);
+      tm = warp_max(tm);
+      const float mp = run_m[h];
+      const float mn = fmaxf(mp, tm);
+      float ts = 0.0f;
+      for (int j = lane; j < n; j += 32) {
+        const float pj = expf(sc[j][h] - mn);
+        sc[j][h] = pj;
+        ts += pj;
+      }
+      ts = warp_sum(ts);
+      if (lane == 0) {
+        const float f = (mp == -INFINITY) ? 0.0f : expf(mp - mn);
+        tile_f[h] = f;
+        run_m[h] = mn;
+        run_l[h] = run_l[h] * f + ts;
+      }
+    }
+    __syncthreads();
+    {
+      const __half2* vrow = reinterpret_cast<const __half2*>(vt) + dp;
+#pragma unroll
+      for (int h = 0; h < G; ++h) {
+        const float f = tile_f[h];
+        acc[h][0] *= f;
+        acc[h][1] *= f;
+      }
+      for (int j = grp; j < n; j += 4) {
+        const float2 v = __half22float2(vrow[j * (kHeadDim / 2)]);
+#pragma unroll
+        for (int h = 0; h < G; ++h) {
+          const float pj = sc[j][h];
+          acc[h][0] += pj * v.x;
+          acc[h][1] += pj * v.y;
+        }
+      }
+    }
+    __syncthreads();  // buffer and scores consumed
+    if (tid == 0 && t + 2 < nt) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      issue(t + 2);
+    }
+  }
+  if (failed_at >= 0) {
+    // Copies still in flight (tiles failed_at and failed_at + 1) land in this
+    // CTA's shared memory: give them a bounded chance to finish before exiting.
+    if (tid == 0) {
+      for (int t = failed_at; t < min(nt, failed_at + 2); ++t) (void)tc_mbar_wait(&mbar[t & 1], (unsigned)(t >> 1) & 1u);
+      atomicOr(err, kBErrTimeout);
+    }
+    pdl_trigger();
+    return;
+  }
+  pdl_trigger();
+  // Merge the 4 position groups.
+  if (grp > 0) {
+#pragma unroll
+    for (int h = 0; h < G; ++h) {
+      red[grp - 1][h][2 * dp] = acc[h][0];
+      red[grp - 1][h][2 * dp + 1] = acc[h][1];
+    }
+  }
+  __syncthreads();
+  if (grp == 0) {
+#pragma unroll
+    for (int h = 0; h < G; ++h) {
+      float o0 = acc[h][0], o1 = acc[h][1];
+#pragma unroll
+      for (int k = 0; k < 3; ++k) {
+        o0 += red[k][h][2 * dp];
+        o1 += red[k][h][2 * dp + 1];
+      }
+      *reinterpret_cast<float2*>(part_o + (slot + h) * kHeadDim + 2 * dp) = make_float2(o0, o1);
+    }
+  }
+  if (tid < G) part_ml[slot + tid] = make_float2(run_m[tid], run_l[tid]);
+}
+
+// Merge the splits of every head of row b into the o GEMM's operands x_hi/x_lo [B][NH*128].
+static __global__ void __launch_bounds__(256) kb_attn_combine(const float2* part_ml, const float* part_o, int splits, int NH,
+                                                       __half* x_hi, __half* x_lo) {
+  pdl_wait();
+  const int b = blockIdx.x, QS = NH * kHeadDim;
+  for (int e = threadIdx.x; e < QS; e += 256) {
+    const int h = e / kHeadDim;
+    float M = -INFINITY;
+    for (int s = 0; s < splits; ++s) M = fmaxf(M, part_ml[((long long)b * splits + s) * NH + h].x);
+    float L = 0.0f, O = 0.0f;
+    for (int s = 0; s < splits; ++s) {
+      const float2 ml = part_ml[((long long)b * splits + s) * NH + h];
+      const float f = ml.y > 0.0f ? expf(ml.x - M) : 0.0f;
+      L += ml.y * f;
+      O += part_o[((long long)b * splits + s) * QS + e] * f;
+    }
+    __half hh, ll;
+    split_f16(O / L, hh, ll);
+    x_hi[(long long)b * QS + e] = hh;
+    x_lo[(long long)b * QS + e] = ll;
+  }
+  pdl_trigger();
+}
+
+// silu(gate) * up from the gate/up GEMM's interleaved partials (column 2j = gate
+// row j, 2j+1 = up row j) -> the down GEMM's operands x_hi/x_lo [B][I].
+static __global__ void __launch_bounds__(256) kb_silu_split(const float* parts, int nparts, long long part_stride, int B,
+                                                     int I, __half* x_hi, __half* x_lo) {
+  pdl_wait();
+  const long long n = (long long)B * I;
+  for (long long i = (long long)blockIdx.x * 256 + threadIdx.x; i < n; i += (long long)gridDim.x * 256) {
+    const long long b = i / I, j = i % I;
+    const long long gi = b * 2 * I + 2 * j;
+    const float gv = sum_parts(parts, nparts, part_stride, gi);
+    const float uv = sum_parts(parts, nparts, part_stride, gi + 1);
+    const float act = gv / (1.0f + expf(-gv)) * uv;
+    __half hh, ll;
+    split_f16(act, hh, ll);
+    x_hi[i] = hh;
+    x_lo[i] = ll;
+  }
+  pdl_trigger();
+}
+
+// Per-row merge of the LM head's per-CTA (max, index) pairs (ties: lowest
+// index; NaN never wins), then the token is fed back and recorded and the
+// position advanced. One warp per row.
+static __global__ void __launch_bounds__(256) kb_argmax_merge(const float* part_v, const uint32_t* part_i, int nparts, int B,
+                                                       BatchState st, uint32_t* result) {
+  pdl_wait();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int b = blockIdx.x * 8 + warp;
+  if (b < B) {
+    float bv = kNegMax;
+    uint32_t bi = 0;
+    for (int k = lane; k < nparts; k += 32) {
+      const float v = part_v[(long long)b * nparts + k];
+      const uint32_t i = part_i[(long long)b * nparts + k];
+      if (am_better(v, i, bv, bi)) {
+        bv = v;
+        bi = i;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const uint32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (am_better(ov, oi, bv, bi)) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+    if (lane == 0) {
+      if (result) {
+        result[2 * b] = bi;
+        result[2 * b + 1] = __float_as_uint(bv);
+      }
+      if (st.tokens) {
+        const int s = *st.step;
+        st.tokens[b] = (int)bi;
+        st.pos[b] += 1;
+        if (s < st.max_steps) st.out[(long long)s * B + b] = (int)bi;
+      }
+    }
+  }
+  pdl_trigger();
+}
+
+static __global__ void kb_step_done(int* step) {
+  pdl_wait();
+  if (threadIdx.x == 0 && blockIdx.x == 0) *step += 1;
+  pdl_trigger();
+}
+
+// ---- seeded synthetic context ---------------------------------------------------
+// Integer hash (a 32-bit finaliser of the xorshift-multiply family).
+__host__ __device__ __forceinline__ uint32_t ctx_hash(uint32_t x) {
+  x ^= x >> 16;
+  x *= 0x7feb352du;
+  x ^= x >> 15;
+  x *= 0x846ca68bu;
+  x ^= x >> 16;
+  return x;
+}
+
+// Hidden-state value d of context row `row` (= seq * ctx + position) of
+// `layer`: the sum of four 24-bit uniforms from the hash, centred and scaled to
+// unit variance (an Irwin-Hall approximation of N(0, 1)). Integer work and two
+// f32 multiplies (the first by a power of two), so any IEEE host reproduces it.
+__host__ __device__ __forceinline__ float ctx_normal(uint32_t seed, uint32_t layer, uint32_t row, uint32_t d,
+                                                    uint32_t H) {
+  const uint32_t key = ctx_hash(seed * 0x9E3779B9u + layer * 0x85EBCA6Bu + 0x632BE5ABu);
+  const uint32_t base = (row * H + d) * 4u;
+  int s = 0;
+  for (uint32_t j = 0; j < 4; ++j) s += (int)(ctx_hash(key ^ (base + j)) >> 8);
+  s -= 2 << 24;
+  return ((float)s * 5.9604644775390625e-08f) * 1.7320508f;
+}
+
+// Rows [row0, row0 + R) of the synthetic hidden states of `layer`, RMS-normed
+// with the layer's input norm into the k/v GEMM's operands x_hi/x_lo [R][H].
+static __global__ void __launch_bounds__(256) kb_ctx_hidden(uint32_t seed, uint32_t layer, long long row0, int H,
+                                                     const float* w, float eps, __half* x_hi, __half* x_lo) {
+  __shared__ float red[8];
+  __shared__ float row[4096];
+  pdl_wait();
+  const long long r = blockIdx.x;
+  const uint32_t grow = (uint32_t)(row0 + r);
+  float ss = 0.0f;
+  for (int e = threadIdx.x; e < H; e += 256) {
+    const float v = ctx_normal(seed, layer, grow, (uint32_t)e, (uint32_t)H);
+    row[e] = v;
+    ss += v * v;
+  }
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  pdl_trigger();
+  float t = 0.0f;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) t += red[k];
+  const float inv = rsqrtf(t / (float)H + eps);
+  for (int e = threadIdx.x; e < H; e += 256) {
+    __half hi, lo;
+    split_f16(row[e] * inv * w[e], hi, lo);
+    x_hi[r * H + e] = hi;
+    x_lo[r * H + e] = lo;
+  }
+}
+
+}  // namespace qd

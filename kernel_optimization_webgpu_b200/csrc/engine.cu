@@ -15,6 +15,7 @@
 #include "../../include/qdecode.h"
 #include "json.hpp"
 #include "gemm_tc.cuh"
+#include "internal.cuh"
 #include "kernels.cuh"
 #include "persist.cuh"
 
@@ -23,44 +24,6 @@ using namespace qd;
 namespace {
 
 thread_local std::string t_last_error;
-
-struct QdError {
-  int code;
-  std::string msg;
-};
-
-#define QD_CK(call)                                                                              \
-  do {                                                                                          \
-    cudaError_t e_ = (call);                                                                    \
-    if (e_ != cudaSuccess) throw QdError{QD_E_CUDA, std::string(#call) + ": " + cudaGetErrorString(e_)}; \
-  } while (0)
-
-template <typename... KArgs, typename... Args>
-void launch(void (*kernel)(KArgs...), dim3 grid, cudaStream_t stream, Args... args) {
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = grid;
-  cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = 0;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  QD_CK(cudaLaunchKernelEx(&cfg, kernel, args...));
-}
-
-int sm_count(int dev) {
-  int n = 0;
-  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
-  return n;
-}
-
-int current_sms() {
-  int dev = 0;
-  cudaGetDevice(&dev);
-  return sm_count(dev);
-}
 
 // ---- matvec stage planning and dispatch -------------------------------------
 struct StagePlan {
@@ -163,60 +126,6 @@ namespace qd {
 void set_thread_error(const std::string& msg) { t_last_error = msg; }
 }  // namespace qd
 
-// ---------------------------------------------------------------------------
-// Bytes of one q4 row record: nb 16-byte blocks then nb f16 scales, padded to 16.
-inline long long rec_bytes(int k) {
-  const long long nb = k / kBlockCols;
-  return (nb * 16 + nb * 2 + 15) / 16 * 16;
-}
-
-// Per layer, each matrix is an array of row records (gate/up: pair records
-// [gate row | up row]); a run of rows is one contiguous range of bytes.
-struct LayerDev {
-  const char *qkv, *o, *gu, *d;
-  const float *n_in, *n_q, *n_k, *n_post;
-  void *kc, *vc;
-};
-
-struct qd_engine {
-  std::string err;
-  int dev = 0, sms = 148;
-  cudaStream_t stream = nullptr;      // the stream work is enqueued on
-  cudaStream_t own_stream = nullptr;  // created with the engine
-  int stepping_max_new = 0;
-  qd_profile p{};
-  qd_options opt{};
-  std::string variant;
-  int splits = 1, rows_qkv = 0, lm_grid = 0;
-  void* blob = nullptr;
-  void* kv = nullptr;
-  void* scratch = nullptr;
-  __half* embed = nullptr;
-  float *cos_t = nullptr, *sin_t = nullptr, *final_norm = nullptr;
-  std::vector<LayerDev> layers;
-  float *h = nullptr, *h_attn = nullptr, *qkv = nullptr, *act = nullptr, *logits = nullptr, *part_o = nullptr;
-  float2* part_ml = nullptr;
-  DevState* st = nullptr;
-  int *tokens = nullptr, *out_dev = nullptr;
-  int* out_host = nullptr;  // mapped pinned: the kernel writes each token here
-  int* out_host_dev = nullptr;
-  uint32_t* result = nullptr;
-  float* lm_pv = nullptr;
-  uint32_t* lm_pi = nullptr;
-  unsigned* lm_counter = nullptr;
-  int32_t* pinned_ids = nullptr;
-  DevState* pinned_state = nullptr;
-  cudaGraphExec_t g_layers = nullptr, g_full = nullptr;
-  cudaEvent_t ev[2] = {nullptr, nullptr};
-  // persistent decode kernel
-  bool persist = false;
-  PLayer* d_players = nullptr;
-  unsigned long long* xbuf = nullptr;
-  long long xstride = 0;
-  size_t persist_smem = 0;
-  int lm_rows = 0;
-  unsigned long long* timeline = nullptr;  // stage stamps of the last persistent launch (opt-in)
-};
 
 namespace {
 
@@ -761,32 +670,60 @@ double ms_since(std::chrono::steady_clock::time_point t0) {
 
 namespace {
 
-size_t tc_smem_bytes(int bn) { return (size_t)2 * (2 * kTcM * kTcK * 2 + 2 * bn * kTcK * 2) + 1024; }
+size_t tc_smem_bytes(int bn, bool af16) {
+  return (size_t)2 * ((af16 ? 1 : 2) * kTcM * kTcK * 2 + 2 * bn * kTcK * 2) + 1024;
+}
 
-template <int BN, int EPI>
-void launch_tc_t(const TcArgs& a, cudaStream_t s) {
-  const size_t smem = tc_smem_bytes(BN);
-  static bool configured = false;  // per process; the attribute is per function
-  if (!configured) {
-    QD_CK(cudaFuncSetAttribute(k_q4_gemm_tc<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    configured = true;
+template <int BN, bool AF16, int EPI>
+void launch_gemm_t(const TcArgs& a, int splits, cudaStream_t s) {
+  const size_t smem = tc_smem_bytes(BN, AF16);
+  static unsigned long long configured = 0;  // one bit per device ordinal: the attribute is per context
+  int dev = 0;
+  QD_CK(cudaGetDevice(&dev));
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (!(configured & bit)) {
+    QD_CK(cudaFuncSetAttribute(k_gemm_tc<BN, AF16, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    configured |= bit;
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((a.n_rows + kTcM - 1) / kTcM, (a.B + BN - 1) / BN);
+  cfg.gridDim = dim3((a.n_rows + kTcM - 1) / kTcM, (a.B + BN - 1) / BN, splits);
   cfg.blockDim = dim3(kTcThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
-  QD_CK(cudaLaunchKernelEx(&cfg, k_q4_gemm_tc<BN, EPI>, a));
-}
-
-template <int EPI>
-void launch_tc(const TcArgs& a, cudaStream_t s) {
-  if (a.B <= 64) launch_tc_t<64, EPI>(a, s);
-  else if (a.B <= 128) launch_tc_t<128, EPI>(a, s);
-  else launch_tc_t<256, EPI>(a, s);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  QD_CK(cudaLaunchKernelEx(&cfg, k_gemm_tc<BN, AF16, EPI>, a));
 }
 
 }  // namespace
+
+namespace qd {
+
+int gemm_plan_splits(int K, int want, int* kt_split) {
+  const int kt_total = K / kTcK;
+  want = std::max(1, std::min(want, kt_total));
+  *kt_split = (kt_total + want - 1) / want;
+  return (kt_total + *kt_split - 1) / *kt_split;
+}
+
+void launch_gemm(TcArgs a, int splits, int mode, cudaStream_t s) {
+  if (a.K % kTcK || a.K <= 0 || a.B <= 0 || a.n_rows <= 0) throw QdError{QD_E_INVALID, "GEMM: bad dimensions"};
+  if (a.kt_split <= 0) a.kt_split = (a.K / kTcK + splits - 1) / splits;
+  if (a.ldx == 0) a.ldx = a.K;
+  if (mode == kGemmQ4Store) {
+    if (a.B <= 64) launch_gemm_t<64, false, kTcStore>(a, splits, s);
+    else if (a.B <= 128) launch_gemm_t<128, false, kTcStore>(a, splits, s);
+    else launch_gemm_t<256, false, kTcStore>(a, splits, s);
+  } else {
+    if (a.B <= 64) launch_gemm_t<64, true, kTcArgmax>(a, splits, s);
+    else launch_gemm_t<128, true, kTcArgmax>(a, splits, s);
+  }
+}
+
+}  // namespace qd
 
 
 extern "C" {
@@ -1085,6 +1022,7 @@ int qd_q4_gemm(const float* x, const uint32_t* weights, const uint16_t* scales_f
       throw QdError{QD_E_INVALID, "qd_q4_gemm: in_size must be a positive multiple of 64, at most 4096"};
     if ((reinterpret_cast<uintptr_t>(weights) & 15) || (reinterpret_cast<uintptr_t>(workspace) & 15))
       throw QdError{QD_E_INVALID, "weights and workspace must be 16-byte aligned"};
+    if (reinterpret_cast<uintptr_t>(scales_f16) & 3) throw QdError{QD_E_INVALID, "scales_f16 must be 4-byte aligned"};
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     __half* xh = reinterpret_cast<__half*>(static_cast<char*>(workspace) + 256);
     __half* xl = xh + (size_t)M * in_size;
@@ -1097,12 +1035,13 @@ int qd_q4_gemm(const float* x, const uint32_t* weights, const uint16_t* scales_f
     a.s_stride = (long long)in_size / kBlockCols * 2;
     a.n_rows = (int)out_size;
     a.K = (int)in_size;
+    a.kt_split = (int)in_size / kTcK;
     a.x_hi = xh;
     a.x_lo = xl;
     a.B = (int)M;
     a.y = y;
     a.ldy = (int)out_size;
-    launch_tc<kTcStore>(a, s);
+    launch_gemm(a, 1, kGemmQ4Store, s);
   } catch (const QdError& err) {
     return fail(nullptr, err);
   }

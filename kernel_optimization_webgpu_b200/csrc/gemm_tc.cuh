@@ -20,7 +20,18 @@
 // dequantised by the threads straight into the 128-byte-swizzled K-major smem
 // layout the MMA reads, the activation hi/lo tiles are copied in, and thread 0
 // issues the MMAs and commits them to the stage's mbarrier. Two stages overlap
-// the dequantisation of tile k+1 with the MMAs of tile k.
+// the dequantisation of tile k+1 with the MMAs of tile k, and the raw weights of
+// tile k+1 are fetched into registers while tile k is written to shared memory.
+//
+// Split-K: gridDim.z CTAs share a row tile, each over its own run of k-tiles,
+// and store partial sums [split][B][N]; the kernel that consumes the result
+// adds the splits in a fixed order (deterministic, no atomics). This keeps
+// >= 128 CTAs busy on the narrow decode projections (N = 1024..6144).
+//
+// The LM head (f16 embedding table, exact in f16) uses the weights directly as
+// A_hi with no A_lo: two MMAs per k-step. Its epilogue reduces each sequence's
+// 128 logits of the CTA to one (max, lowest index) pair, so only 8 bytes per
+// (sequence, CTA) leave the kernel unless the caller also asks for the logits.
 #pragma once
 
 #include "common.cuh"
@@ -35,28 +46,32 @@ constexpr float kLoScale = 2048.0f;  // lo parts are stored times 2^11
 constexpr unsigned long long kTcWaitNs = 1000ull * 1000 * 1000;
 
 enum TcEpi : int {
-  kTcStore = 0,     // y[b][n] = acc
-  kTcResidual = 1,  // y[b][n] = res[b][n] + acc
-  kTcSiluPair = 2,  // rows 2j, 2j+1 are gate j, up j: act[b][j] = silu(g) * u (also split to hi/lo)
+  kTcStore = 0,   // y[split][b][n] = acc (split-K partials; the consumer sums them)
+  kTcArgmax = 1,  // per (b, CTA) best (value, row) over the CTA's 128 rows; logits to y if set
 };
 
 struct TcArgs {
-  // weights: row n's 16-byte blocks at w + n*w_stride, its f16 scales at s + n*s_stride
+  // q4 weights: row n's 16-byte blocks at w + n*w_stride, its f16 scales at s + n*s_stride
   const char* w;
   const char* s;
   long long w_stride, s_stride;
+  // f16 weights (the LM head): row n at a16 + n*a16_stride (elements)
+  const __half* a16;
+  long long a16_stride;
   int n_rows;                 // weight rows (N of the GEMM)
   int K;                      // columns (multiple of 64)
-  // activations, pre-split: x_hi/x_lo [B rows][K] f16 (row stride K)
+  int kt_split;               // k-tiles per split (gridDim.z splits cover K)
+  // activations, pre-split: x_hi/x_lo [B rows][K] f16, row b at b * ldx
   const __half* x_hi;
   const __half* x_lo;
+  long long ldx;
   int B;                      // activation rows actually present (<= BN * gridDim.y)
   // outputs
-  float* y;                   // [B][ldy]
+  float* y;                   // [split][B][ldy] (kTcStore); optional logits [B][ldy] (kTcArgmax)
   int ldy;
-  const float* res;           // residual [B][ldy] (kTcResidual)
-  __half* y_hi;               // optional hi/lo split of the output (silu pairs), [B][ldy]
-  __half* y_lo;
+  long long y_split;          // floats between two splits' outputs
+  float* part_v;              // kTcArgmax: [B][gridDim.x] best value / row
+  uint32_t* part_i;
   int* err;                   // device status word (bit kTcErrTimeout)
 };
 
@@ -150,22 +165,124 @@ __device__ __forceinline__ void split_f16(float v, __half& hi, __half& lo) {
 }
 
 // ---- the kernel ---------------------------------------------------------------------
-// Grid: (ceil(n_rows / 128), ceil(B / BN)). Shared memory: 2 stages of
-// A_hi, A_lo [128][64] f16 (16 KB each) + B_hi, B_lo [BN][64] f16, 1024-aligned.
-template <int BN, int EPI>
-__global__ void __launch_bounds__(kTcThreads, 1) k_q4_gemm_tc(const TcArgs a) {
+// Transposing (max, lowest row) reduction across a warp of 32 columns: lane l
+// starts with 32 candidates (one per column, all of its own row) and ends with
+// the best of column l over the warp's 32 rows. 31 exchanges instead of 160.
+__device__ __forceinline__ void warp_argmax_columns(float (&v)[32], uint32_t (&id)[32], int lane) {
+#pragma unroll
+  for (int w = 32; w > 1; w >>= 1) {
+    const int o = w >> 1;
+    const bool upper = (lane & o) != 0;
+#pragma unroll
+    for (int j = 0; j < o; ++j) {
+      const float sv = upper ? v[j] : v[j + o];
+      const uint32_t si = upper ? id[j] : id[j + o];
+      const float rv = __shfl_xor_sync(0xffffffffu, sv, o);
+      const uint32_t ri = __shfl_xor_sync(0xffffffffu, si, o);
+      float kv = upper ? v[j + o] : v[j];
+      uint32_t ki = upper ? id[j + o] : id[j];
+      if (am_better(rv, ri, kv, ki)) {
+        kv = rv;
+        ki = ri;
+      }
+      v[j] = kv;
+      id[j] = ki;
+    }
+  }
+}
+
+// Raw weight data of one k-tile held in registers between its load and its
+// dequantisation into shared memory (so the next tile's loads overlap this one's MMAs).
+template <bool AF16>
+struct TcRaw;
+template <>
+struct TcRaw<false> {  // q4: this thread's row, two blocks
+  uint4 q[2];
+  uint32_t sc;  // two f16 scales
+};
+template <>
+struct TcRaw<true> {  // f16: 8 chunks of 16 B (4 rows per warp pass)
+  uint4 c[8];
+};
+
+template <bool AF16>
+__device__ __forceinline__ void tc_load_raw(const TcArgs& a, int n0, int kt, int tid, TcRaw<AF16>& r) {
+  if constexpr (!AF16) {
+    const int n = n0 + tid;
+    if (n < a.n_rows) {
+      const uint4* wb = reinterpret_cast<const uint4*>(a.w + (long long)n * a.w_stride) + kt * 2;
+      r.q[0] = ld_stream(wb);
+      r.q[1] = ld_stream(wb + 1);
+      r.sc = *reinterpret_cast<const uint32_t*>(a.s + (long long)n * a.s_stride + kt * 4);
+    } else {
+      r.q[0] = r.q[1] = make_uint4(0, 0, 0, 0);
+      r.sc = 0;
+    }
+  } else {
+    const int warp = tid >> 5, lane = tid & 31;
+#pragma unroll
+    for (int it = 0; it < 8; ++it) {
+      const int n = n0 + warp * 32 + it * 4 + (lane >> 3);
+      r.c[it] = n < a.n_rows
+                    ? ld_stream(reinterpret_cast<const uint4*>(a.a16 + (long long)n * a.a16_stride + kt * kTcK) + (lane & 7))
+                    : make_uint4(0, 0, 0, 0);
+    }
+  }
+}
+
+template <bool AF16>
+__device__ __forceinline__ void tc_store_raw(const TcRaw<AF16>& r, int tid, unsigned char* A_hi, unsigned char* A_lo) {
+  if constexpr (!AF16) {
+    __half2 s2 = *reinterpret_cast<const __half2*>(&r.sc);
+    const float sc[2] = {__low2float(s2) * (float)(1 << kWShift), __high2float(s2) * (float)(1 << kWShift)};
+#pragma unroll
+    for (int blk = 0; blk < 2; ++blk) {
+      const uint32_t ws[4] = {r.q[blk].x, r.q[blk].y, r.q[blk].z, r.q[blk].w};
+#pragma unroll
+      for (int wi = 0; wi < 4; ++wi) {  // 8 columns per word -> one 16-byte chunk of f16
+        __align__(16) __half hi8[8], lo8[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float v = (float)((int)((ws[wi] >> (4 * i)) & 0xFu) - 8) * sc[blk];
+          split_f16(v, hi8[i], lo8[i]);
+        }
+        const unsigned off = sw128_off(tid, blk * 32 + wi * 8);
+        *reinterpret_cast<uint4*>(A_hi + off) = *reinterpret_cast<const uint4*>(hi8);
+        *reinterpret_cast<uint4*>(A_lo + off) = *reinterpret_cast<const uint4*>(lo8);
+      }
+    }
+  } else {
+    (void)A_lo;
+    const int warp = tid >> 5, lane = tid & 31;
+#pragma unroll
+    for (int it = 0; it < 8; ++it) {
+      const int row = warp * 32 + it * 4 + (lane >> 3);
+      *reinterpret_cast<uint4*>(A_hi + sw128_off(row, (lane & 7) * 8)) = r.c[it];
+    }
+  }
+}
+
+// Grid: (ceil(n_rows / 128), ceil(B / BN), splits). Shared memory: 2 stages of
+// A_hi [128][64] f16 (+ A_lo for q4) + B_hi, B_lo [BN][64] f16, 1024-aligned.
+// Split z covers k-tiles [z * kt_split, min((z + 1) * kt_split, K / 64)).
+template <int BN, bool AF16, int EPI>
+__global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const TcArgs a) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   // 1024-byte alignment of every tile (the swizzle atoms)
   unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   constexpr int kA = kTcM * kTcK * 2;       // 16 KB
   constexpr int kB = BN * kTcK * 2;
-  constexpr int kStage = 2 * kA + 2 * kB;
+  constexpr int kStage = (AF16 ? 1 : 2) * kA + 2 * kB;
   __shared__ unsigned long long mbar[2];
   __shared__ unsigned tmem_base;
+  __shared__ float red_v[EPI == kTcArgmax ? 4 : 1][EPI == kTcArgmax ? BN : 1];
+  __shared__ uint32_t red_i[EPI == kTcArgmax ? 4 : 1][EPI == kTcArgmax ? BN : 1];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int n0 = blockIdx.x * kTcM;
   const int b0 = blockIdx.y * BN;
-  const int kt_count = a.K / kTcK;
+  const int kt_total = a.K / kTcK;
+  const int kt0 = blockIdx.z * a.kt_split;
+  const int nk = min(a.kt_split, kt_total - kt0);
 
   if (warp == 0) {  // TMEM: D_main (BN columns) + D_corr (BN columns)
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(tc_smem(&tmem_base)),
@@ -178,66 +295,37 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_q4_gemm_tc(const TcArgs a) {
     tc_mbar_init(&mbar[1]);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
+  // The weights are constant: the first tile is fetched before waiting for the
+  // kernel that produces the activations.
+  TcRaw<AF16> raw;
+  tc_load_raw<AF16>(a, n0, kt0, tid, raw);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  pdl_wait();
   const unsigned tmem = tmem_base;
   const unsigned idesc = umma_idesc_f16_f32(kTcM, BN);
   bool ok = true;
 
-  // thread -> weight row of the tile
-  const int row = tid;                       // 0..127
-  const int n = n0 + row;
-  const bool row_live = n < a.n_rows;
-  const char* wrow = a.w + (long long)(row_live ? n : 0) * a.w_stride;
-  const __half* srow = reinterpret_cast<const __half*>(a.s + (long long)(row_live ? n : 0) * a.s_stride);
-
-  for (int kt = 0; kt < kt_count; ++kt) {
-    const int st = kt & 1;
+  for (int i = 0; i < nk; ++i) {
+    const int kt = kt0 + i;
+    const int st = i & 1;
     unsigned char* A_hi = smem + st * kStage;
-    unsigned char* A_lo = A_hi + kA;
-    unsigned char* B_hi = A_lo + kA;
+    unsigned char* A_lo = A_hi + kA;  // q4 only
+    unsigned char* B_hi = A_hi + (AF16 ? 1 : 2) * kA;
     unsigned char* B_lo = B_hi + kB;
-    // The MMAs that last read this stage (k-tile kt-2) must be done.
-    if (kt >= 2) ok = tc_mbar_wait(&mbar[st], (unsigned)((kt - 2) >> 1) & 1u) && ok;
-
-    // Dequantise this row's two q4 blocks (64 columns) into A_hi / A_lo.
-    {
-      uint4 q[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
-      float sc[2] = {0.f, 0.f};
-      if (row_live) {
-        const uint4* wb = reinterpret_cast<const uint4*>(wrow) + kt * 2;
-        q[0] = wb[0];
-        q[1] = wb[1];
-        sc[0] = __half2float(srow[kt * 2]) * (float)(1 << kWShift);
-        sc[1] = __half2float(srow[kt * 2 + 1]) * (float)(1 << kWShift);
-      }
-#pragma unroll
-      for (int blk = 0; blk < 2; ++blk) {
-        const uint32_t ws[4] = {q[blk].x, q[blk].y, q[blk].z, q[blk].w};
-#pragma unroll
-        for (int wi = 0; wi < 4; ++wi) {  // 8 columns per word -> one 16-byte chunk of f16
-          __align__(16) __half hi8[8], lo8[8];
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const float v = (float)((int)((ws[wi] >> (4 * i)) & 0xFu) - 8) * sc[blk];
-            split_f16(v, hi8[i], lo8[i]);
-          }
-          const int k = blk * 32 + wi * 8;
-          const unsigned off = sw128_off(row, k);
-          *reinterpret_cast<uint4*>(A_hi + off) = *reinterpret_cast<const uint4*>(hi8);
-          *reinterpret_cast<uint4*>(A_lo + off) = *reinterpret_cast<const uint4*>(lo8);
-        }
-      }
-    }
+    // The MMAs that last read this stage (tile i-2) must be done.
+    if (i >= 2) ok = tc_mbar_wait(&mbar[st], (unsigned)((i - 2) >> 1) & 1u) && ok;
+    tc_store_raw<AF16>(raw, tid, A_hi, A_lo);
+    if (i + 1 < nk) tc_load_raw<AF16>(a, n0, kt + 1, tid, raw);
     // Activation tiles: BN rows x 64 columns of x_hi / x_lo (rows beyond B are zero).
     for (int c = tid; c < BN * 8; c += kTcThreads) {  // 16-byte chunks
       const int r = c >> 3, ch = c & 7;
       const int b = b0 + r;
       uint4 vh = make_uint4(0, 0, 0, 0), vl = make_uint4(0, 0, 0, 0);
       if (b < a.B) {
-        vh = *reinterpret_cast<const uint4*>(a.x_hi + (long long)b * a.K + kt * kTcK + ch * 8);
-        vl = *reinterpret_cast<const uint4*>(a.x_lo + (long long)b * a.K + kt * kTcK + ch * 8);
+        vh = *reinterpret_cast<const uint4*>(a.x_hi + (long long)b * a.ldx + kt * kTcK + ch * 8);
+        vl = *reinterpret_cast<const uint4*>(a.x_lo + (long long)b * a.ldx + kt * kTcK + ch * 8);
       }
       const unsigned off = sw128_off(r, ch * 8);
       *reinterpret_cast<uint4*>(B_hi + off) = vh;
@@ -250,56 +338,75 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_q4_gemm_tc(const TcArgs a) {
 #pragma unroll
       for (int ks = 0; ks < kTcK / 16; ++ks) {
         const unsigned long long dah = umma_desc_k_sw128(tc_smem(A_hi) + ks * 32);
-        const unsigned long long dal = umma_desc_k_sw128(tc_smem(A_lo) + ks * 32);
         const unsigned long long dbh = umma_desc_k_sw128(tc_smem(B_hi) + ks * 32);
         const unsigned long long dbl = umma_desc_k_sw128(tc_smem(B_lo) + ks * 32);
-        const bool acc = kt > 0 || ks > 0;
+        const bool acc = i > 0 || ks > 0;
         umma_f16(tmem, dah, dbh, idesc, acc);
         umma_f16(tmem + BN, dah, dbl, idesc, acc);
-        umma_f16(tmem + BN, dal, dbh, idesc, true);
+        if constexpr (!AF16) {
+          const unsigned long long dal = umma_desc_k_sw128(tc_smem(A_lo) + ks * 32);
+          umma_f16(tmem + BN, dal, dbh, idesc, true);
+        }
       }
       umma_commit(&mbar[st]);
     }
   }
   // Wait for the last MMAs (both stages' final commits).
-  if (kt_count >= 2) ok = tc_mbar_wait(&mbar[(kt_count - 2) & 1], (unsigned)((kt_count - 2) >> 1) & 1u) && ok;
-  ok = tc_mbar_wait(&mbar[(kt_count - 1) & 1], (unsigned)((kt_count - 1) >> 1) & 1u) && ok;
+  if (nk >= 2) ok = tc_mbar_wait(&mbar[(nk - 2) & 1], (unsigned)((nk - 2) >> 1) & 1u) && ok;
+  ok = tc_mbar_wait(&mbar[(nk - 1) & 1], (unsigned)((nk - 1) >> 1) & 1u) && ok;
   tc_fence_after();
+  pdl_trigger();
 
-  if (!ok) {
+  // Epilogue: warp w reads TMEM lanes 32w..32w+31 = weight rows n0 + 32w + lane.
+  const int n = n0 + warp * 32 + lane;
+  const bool row_live = n < a.n_rows;
+  const unsigned lane_base = (unsigned)(warp * 32) << 16;
+  const float unscale = AF16 ? 1.0f : 1.0f / (float)(1 << kWShift);
+  float* y = a.y ? a.y + (long long)blockIdx.z * a.y_split : nullptr;
+  if (!__syncthreads_and(ok)) {
     if (tid == 0 && a.err) atomicOr(a.err, kTcErrTimeout);
   } else {
-    // Epilogue: warp w reads TMEM lanes 32w..32w+31 = weight rows n0 + 32w + lane.
-    const unsigned lane_base = (unsigned)(warp * 32) << 16;
-    const float unscale = 1.0f / (float)(1 << kWShift);
 #pragma unroll 1
     for (int c0 = 0; c0 < BN; c0 += 32) {
       float dm[32], dc[32];
       tmem_ld32(tmem + lane_base + c0, dm);
       tmem_ld32(tmem + lane_base + BN + c0, dc);
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const int b = b0 + c0 + j;
-        const float v = (dm[j] + dc[j] * (1.0f / kLoScale)) * unscale;
-        if constexpr (EPI == kTcSiluPair) {
-          const float other = __shfl_xor_sync(0xffffffffu, v, 1);  // lane pairs: gate (even), up (odd)
-          if ((lane & 1) == 0 && row_live && b < a.B) {
-            const int jrow = n >> 1;
-            const float act = (v / (1.0f + expf(-v))) * other;
-            a.y[(long long)b * a.ldy + jrow] = act;
-            if (a.y_hi) {
-              __half h, l;
-              split_f16(act, h, l);
-              a.y_hi[(long long)b * a.ldy + jrow] = h;
-              a.y_lo[(long long)b * a.ldy + jrow] = l;
-            }
-          }
-        } else {
-          if (row_live && b < a.B) {
-            const long long o = (long long)b * a.ldy + n;
-            a.y[o] = (EPI == kTcResidual) ? a.res[o] + v : v;
-          }
+      for (int j = 0; j < 32; ++j) dm[j] = (dm[j] + dc[j] * (1.0f / kLoScale)) * unscale;
+      if (y) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const int b = b0 + c0 + j;
+          if (row_live && b < a.B) y[(long long)b * a.ldy + n] = dm[j];
         }
+      }
+      if constexpr (EPI == kTcArgmax) {
+        uint32_t id[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          id[j] = (uint32_t)n;
+          if (!row_live) dm[j] = kNegMax;
+        }
+        warp_argmax_columns(dm, id, lane);
+        red_v[warp][c0 + lane] = dm[0];
+        red_i[warp][c0 + lane] = id[0];
+      }
+    }
+    if constexpr (EPI == kTcArgmax) {
+      __syncthreads();
+      for (int j = tid; j < BN; j += kTcThreads) {
+        const int b = b0 + j;
+        if (b >= a.B) continue;
+        float bv = red_v[0][j];
+        uint32_t bi = red_i[0][j];
+#pragma unroll
+        for (int w = 1; w < 4; ++w)
+          if (am_better(red_v[w][j], red_i[w][j], bv, bi)) {
+            bv = red_v[w][j];
+            bi = red_i[w][j];
+          }
+        a.part_v[(long long)b * gridDim.x + blockIdx.x] = bv;
+        a.part_i[(long long)b * gridDim.x + blockIdx.x] = bi;
       }
     }
   }
@@ -311,7 +418,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_q4_gemm_tc(const TcArgs a) {
 
 // Split f32 rows into the hi/lo f16 operands of the GEMM: x_hi[b][k] = f16(x),
 // x_lo[b][k] = f16((x - x_hi) * 2^11). Grid-stride over B*K elements.
-__global__ void k_split_hilo(const float* x, int n, __half* hi, __half* lo) {
+static __global__ void k_split_hilo(const float* x, int n, __half* hi, __half* lo) {
+  pdl_wait();
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
     __half h, l;
     split_f16(x[i], h, l);

@@ -159,6 +159,103 @@ class Engine:
         return out
 
 
+class Batch:
+    """B independent sequences decoded together on an engine's weights (qd_batch_*).
+
+    The batch owns its KV cache ([layer][seq][kv_head][max_seq][128] f16); the
+    engine must outlive it."""
+
+    def __init__(self, engine: Engine, batch: int, max_seq: int):
+        L = _lib.load()
+        h = C.c_void_p()
+        check(L.qd_batch_create(engine._h, int(batch), int(max_seq), C.byref(h)))
+        self._h = h
+        self.engine = engine
+        self.batch = batch
+        self.max_seq = max_seq
+
+    def close(self) -> None:
+        if getattr(self, "_h", None) and _lib is not None and _lib._lib is not None:
+            _lib._lib.qd_batch_destroy(self._h)
+        self._h = None
+
+    def __del__(self):
+        self.close()
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def fill_context(self, ctx: int, seed: int) -> None:
+        check(_lib.load().qd_batch_fill_context(self._h, int(ctx), int(seed) & 0xFFFFFFFF))
+
+    def set_tokens(self, tokens=None, positions=None) -> None:
+        t = None if tokens is None else np.ascontiguousarray(tokens, dtype=np.int32)
+        p = None if positions is None else np.ascontiguousarray(positions, dtype=np.int32)
+        for a in (t, p):
+            if a is not None and a.size != self.batch:
+                raise ValueError(f"expected {self.batch} entries")
+        check(_lib.load().qd_batch_set_tokens(self._h, None if t is None else t.ctypes.data,
+                                              None if p is None else p.ctypes.data))
+
+    def positions(self) -> np.ndarray:
+        out = np.zeros(self.batch, np.int32)
+        check(_lib.load().qd_batch_positions(self._h, out.ctypes.data))
+        return out
+
+    def decode(self, steps: int, want_ids: bool = True) -> Optional[np.ndarray]:
+        """`steps` greedy steps of every sequence; ids [steps][batch]."""
+        out = np.zeros((max(steps, 1), self.batch), np.int32) if want_ids else None
+        check(_lib.load().qd_batch_decode(self._h, int(steps), None if out is None else out.ctypes.data))
+        return None if out is None else out[:steps]
+
+    def prefill(self, ids) -> np.ndarray:
+        """Prompts [batch][n] at positions 0..n-1; returns each sequence's first generated id."""
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        if ids.ndim != 2 or ids.shape[0] != self.batch:
+            raise ValueError(f"ids must be [{self.batch}][n_prompt]")
+        out = np.zeros(self.batch, np.int32)
+        check(_lib.load().qd_batch_prefill(self._h, ids.ctypes.data, int(ids.shape[1]), out.ctypes.data))
+        return out
+
+    def keep_logits(self, keep: bool = True) -> None:
+        check(_lib.load().qd_batch_keep_logits(self._h, int(keep)))
+
+    def logits(self) -> np.ndarray:
+        out = np.zeros((self.batch, self.engine.profile["vocab"]), np.float32)
+        check(_lib.load().qd_batch_logits(self._h, out.ctypes.data))
+        return out
+
+    def read_kv(self, layer: int, seq: int, pos0: int, count: int):
+        kvs = self.engine.profile["kv_heads"] * self.engine.profile["head_dim"]
+        k = np.zeros((count, kvs), np.float32)
+        v = np.zeros((count, kvs), np.float32)
+        check(_lib.load().qd_batch_read_kv(self._h, int(layer), int(seq), int(pos0), int(count),
+                                           k.ctypes.data, v.ctypes.data))
+        return k, v
+
+    def write_kv(self, layer: int, seq: int, pos0: int, k, v) -> None:
+        k = np.ascontiguousarray(k, dtype=np.float32)
+        v = np.ascontiguousarray(v, dtype=np.float32)
+        check(_lib.load().qd_batch_write_kv(self._h, int(layer), int(seq), int(pos0), int(k.shape[0]),
+                                            k.ctypes.data, v.ctypes.data))
+
+    @property
+    def step_kernels(self) -> int:
+        return int(_lib.load().qd_batch_step_kernels(self._h))
+
+
+def generate_batch(engine: Engine, ids, max_new: int) -> np.ndarray:
+    """qd_generate_batch: prompts [batch][n] -> generated ids [batch][max_new]."""
+    ids = np.ascontiguousarray(ids, dtype=np.int32)
+    out = np.zeros((ids.shape[0], max(max_new, 1)), np.int32)
+    check(_lib.load().qd_generate_batch(engine._h, int(ids.shape[0]), ids.ctypes.data, int(ids.shape[1]),
+                                        int(max_new), out.ctypes.data))
+    return out[:, :max_new]
+
+
 # ---- the reference's JavaScript API --------------------------------------------
 
 class CudaDevice:

@@ -446,6 +446,17 @@ void qo_session_free(qo_session* s) {
 }
 
 void qo_session_set_trace(qo_session* s, float* trace) { s->trace = trace; }
+
+/* Cache rows set from outside (a context built elsewhere): rows are stored as
+ * given, in the [pos][kv_head * head_dim] layout cache_write.wgsl:12-18 writes. */
+int qo_session_set_kv(qo_session* s, int layer, int pos0, int count, const float* k, const float* v) {
+  const qo_model* m = s->m;
+  const size_t KV = (size_t)m->kv_heads * m->head_dim;
+  if (layer < 0 || layer >= m->layers || pos0 < 0 || count < 0 || pos0 + count > s->max_seq) return -1;
+  memcpy(s->k_cache[layer] + (size_t)pos0 * KV, k, (size_t)count * KV * sizeof(float));
+  memcpy(s->v_cache[layer] + (size_t)pos0 * KV, v, (size_t)count * KV * sizeof(float));
+  return 0;
+}
 const float* qo_session_final_hidden(const qo_session* s) { return s->final_out; }
 const float* qo_session_hidden(const qo_session* s) { return s->h; }
 

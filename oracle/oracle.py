@@ -56,6 +56,7 @@ def lib():
         L.qo_session_new.argtypes = [vp, i32, i32, i32]; L.qo_session_new.restype = vp
         L.qo_session_free.argtypes = [vp]
         L.qo_session_set_trace.argtypes = [vp, vp]
+        L.qo_session_set_kv.argtypes = [vp, i32, i32, i32, _f32p, _f32p]; L.qo_session_set_kv.restype = i32
         L.qo_forward.argtypes = [vp, i32, i32]; L.qo_forward.restype = i32
         L.qo_session_final_hidden.argtypes = [vp]; L.qo_session_final_hidden.restype = C.POINTER(f32)
         L.qo_session_hidden.argtypes = [vp]; L.qo_session_hidden.restype = C.POINTER(f32)
@@ -201,6 +202,13 @@ class Session:
         if getattr(self, "_h", None):
             lib().qo_session_free(self._h)
             self._h = None
+
+    def set_kv(self, layer: int, pos0: int, k, v) -> None:
+        """Cached K/V rows [pos0, pos0 + len(k)) of `layer` ([n][kv_heads * head_dim] f32)."""
+        k = _c(k, np.float32)
+        v = _c(v, np.float32)
+        if lib().qo_session_set_kv(self._h, layer, pos0, k.shape[0], k.reshape(-1), v.reshape(-1)):
+            raise ValueError("oracle set_kv: rows outside the cache")
 
     def forward(self, token: int, position: int, trace: bool = False):
         tr = None

@@ -19,3 +19,12 @@ def tiny_runtime(tmp_path_factory):
     d = str(tmp_path_factory.mktemp("tiny_runtime"))
     synth.write_runtime(d, synth.TINY, seed=2)
     return d
+
+
+@pytest.fixture(scope="session")
+def qwen_runtime(tmp_path_factory):
+    """Qwen3-0.6B-shape random-init weights (seed 2) in the reference's runtime layout."""
+    from kernel_optimization_webgpu_b200 import synth
+    d = str(tmp_path_factory.mktemp("qwen_seed2"))
+    synth.write_runtime(d, synth.QWEN3_0_6B, seed=2)
+    return d

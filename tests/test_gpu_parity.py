@@ -222,13 +222,6 @@ def test_reference_api_mirror(tiny_runtime):
     ctx["device"].close()
 
 
-@pytest.fixture(scope="module")
-def qwen_runtime(tmp_path_factory):
-    d = str(tmp_path_factory.mktemp("qwen_seed2"))
-    synth.write_runtime(d, synth.QWEN3_0_6B, seed=2)
-    return d
-
-
 @pytest.mark.parametrize("persistent", [True, False])
 def test_engine_qwen_shape_greedy_config2(qwen_runtime, persistent):
     """Config 2: 28 layers, 8 seeded prompt ids, 24 generated tokens, f16 KV."""
