@@ -44,6 +44,7 @@ struct qd_batch {
   std::vector<int> host_pos;
   bool keep_logits = false;
   cudaGraphExec_t g_step[2] = {nullptr, nullptr};  // [keep_logits]
+  CUtensorMap kvmap;         // the whole KV allocation as [rows][128] f16, 64x64 boxes, 128-byte swizzle
   // wide buffers (context fill, prefill), grown on demand
   void* wide = nullptr;
   long long wide_rows = 0;
@@ -60,7 +61,7 @@ int bfail(qd_batch* b, const QdError& err) {
   return err.code;
 }
 
-unsigned long long g_attn_smem_mask = 0;
+unsigned long long g_attn_smem_mask = 0, g_attn_smem_mask2 = 0;
 
 struct Dims {
   int L, H, I, NH, NKV, QS, KVS, R, V, G;
@@ -132,17 +133,21 @@ void launch_attn(qd_batch* b, int l, cudaStream_t s) {
   const Dims d = dims(b->e);
   const dim3 grid(d.NKV, b->splits, b->B);
   const float scale = 1.0f / std::sqrt((float)kHeadDim);
+  const long long layer_rows = (long long)b->B * d.NKV * b->max_seq;
+  const long long k_row0 = (long long)l * layer_rows, v_row0 = (long long)(d.L + l) * layer_rows;
   if (d.G == 1) {
     allow_smem(kb_attn<1>, kBAttnSmem, g_attn_smem_mask);
-    launch_ex(kb_attn<1>, grid, dim3(kBAttnThreads), kBAttnSmem, s, (const float*)b->q, (const __half*)kc_of(b, l),
-              (const __half*)vc_of(b, l), (const int*)b->pos, d.NH, d.NKV, b->max_seq, b->split_len, b->splits, scale,
-              b->part_ml, b->part_o, b->errw);
+    launch_ex(kb_attn<1>, grid, dim3(kBAttnThreads), kBAttnSmem, s, b->kvmap, k_row0, v_row0, (const float*)b->q,
+              (const int*)b->pos, d.NH, d.NKV, b->max_seq, b->split_len, b->splits, scale, b->part_ml, b->part_o,
+              b->errw);
   } else {
-    allow_smem(kb_attn<2>, kBAttnSmem, g_attn_smem_mask);
-    launch_ex(kb_attn<2>, grid, dim3(kBAttnThreads), kBAttnSmem, s, (const float*)b->q, (const __half*)kc_of(b, l),
-              (const __half*)vc_of(b, l), (const int*)b->pos, d.NH, d.NKV, b->max_seq, b->split_len, b->splits, scale,
-              b->part_ml, b->part_o, b->errw);
+    allow_smem(kb_attn<2>, kBAttnSmem, g_attn_smem_mask2);
+    launch_ex(kb_attn<2>, grid, dim3(kBAttnThreads), kBAttnSmem, s, b->kvmap, k_row0, v_row0, (const float*)b->q,
+              (const int*)b->pos, d.NH, d.NKV, b->max_seq, b->split_len, b->splits, scale, b->part_ml, b->part_o,
+              b->errw);
   }
+  launch_ex(kb_attn_combine, dim3(d.NH, b->B), dim3(kHeadDim), 0, s, (const float2*)b->part_ml,
+            (const float*)b->part_o, b->splits, d.NH, b->xh, b->xl);
 }
 
 // One decode step of every sequence (launch order: see batch.cuh).
@@ -155,27 +160,25 @@ void enqueue_step(qd_batch* b, bool keep_logits, cudaStream_t s) {
   for (int l = 0; l < d.L; ++l) {
     const LayerDev& L = e->layers[l];
     if (l == 0)
-      launch(kb_resid_norm, dim3(B), s, b->h, (const float*)nullptr, 0, 0LL, (const __half*)e->embed,
+      launch_ex(kb_resid_norm, dim3(B), dim3(kNormThreads), 0, s, b->h, (const float*)nullptr, 0, 0LL, (const __half*)e->embed,
              (const int*)b->tokens, d.V, L.n_in, d.H, d.eps, b->xh, b->xl, b->errw);
     else
-      launch(kb_resid_norm, dim3(B), s, b->h, (const float*)b->parts, b->sd, sB * d.H, (const __half*)nullptr,
+      launch_ex(kb_resid_norm, dim3(B), dim3(kNormThreads), 0, s, b->h, (const float*)b->parts, b->sd, sB * d.H, (const __half*)nullptr,
              (const int*)nullptr, d.V, L.n_in, d.H, d.eps, b->xh, b->xl, b->errw);
     gemm_q4(L.qkv, d.H, d.R, b->xh, b->xl, B, b->sq, b->ktq, b->parts, s, b->errw);
     launch(kb_rope_cache, dim3(rope_grid), s, (const float*)b->parts, b->sq, sB * d.R, B, d.NH, d.NKV, L.n_q, L.n_k,
            d.eps, (const float*)e->cos_t, (const float*)e->sin_t, e->opt.rope_row_stride, (const int*)b->pos, 1, 0LL,
            b->max_seq, kc_of(b, l), vc_of(b, l), b->q, b->errw);
-    launch_attn(b, l, s);
-    launch(kb_attn_combine, dim3(B), s, (const float2*)b->part_ml, (const float*)b->part_o, b->splits, d.NH, b->xh,
-           b->xl);
+    launch_attn(b, l, s);  // attention + split combine
     gemm_q4(L.o, d.QS, d.H, b->xh, b->xl, B, b->so, b->kto, b->parts, s, b->errw);
-    launch(kb_resid_norm, dim3(B), s, b->h, (const float*)b->parts, b->so, sB * d.H, (const __half*)nullptr,
+    launch_ex(kb_resid_norm, dim3(B), dim3(kNormThreads), 0, s, b->h, (const float*)b->parts, b->so, sB * d.H, (const __half*)nullptr,
            (const int*)nullptr, d.V, L.n_post, d.H, d.eps, b->xh, b->xl, b->errw);
     gemm_q4(L.gu, d.H, 2 * d.I, b->xh, b->xl, B, b->sg, b->ktg, b->parts, s, b->errw);
     const int silu_grid = (int)std::min<long long>((sB * d.I + 255) / 256, 4096);
     launch(kb_silu_split, dim3(silu_grid), s, (const float*)b->parts, b->sg, sB * 2 * d.I, B, d.I, b->xh, b->xl);
     gemm_q4(L.d, d.I, d.H, b->xh, b->xl, B, b->sd, b->ktd, b->parts, s, b->errw);
   }
-  launch(kb_resid_norm, dim3(B), s, b->h, (const float*)b->parts, b->sd, sB * d.H, (const __half*)nullptr,
+  launch_ex(kb_resid_norm, dim3(B), dim3(kNormThreads), 0, s, b->h, (const float*)b->parts, b->sd, sB * d.H, (const __half*)nullptr,
          (const int*)nullptr, d.V, (const float*)e->final_norm, d.H, d.eps, b->xh, b->xl, b->errw);
   lm_head(b, b->xh, b->xl, d.H, B, keep_logits ? b->logits : nullptr, s);
   BatchState st{b->tokens, b->pos, b->out, b->step, b->max_steps};
@@ -184,7 +187,7 @@ void enqueue_step(qd_batch* b, bool keep_logits, cudaStream_t s) {
   launch(kb_step_done, dim3(1), s, b->step);
 }
 
-int step_kernel_count(const qd_batch* b) { return b->e->p.layers * 10 + 4; }
+int step_kernel_count(const qd_batch* b) { return b->e->p.layers * 10 + 4; }  // incl. the split combine
 
 void check_err(qd_batch* b) {
   qd_engine* e = b->e;
@@ -313,9 +316,15 @@ void create_batch(qd_engine* e, int B, int max_seq, qd_batch* b) {
 
   b->kv_layer = (size_t)B * d.NKV * max_seq * kHeadDim;
   const size_t kv_bytes = b->kv_layer * 2 * 2 * d.L;
+  const unsigned long long kv_rows = (unsigned long long)2 * d.L * B * d.NKV * max_seq;
+  if (kv_rows + kBAttnTile >= (1ull << 31)) throw QdError{QD_E_RANGE, "batch KV cache beyond 2^31 rows"};
   if (cudaMalloc(&b->kv, kv_bytes) != cudaSuccess)
     throw QdError{QD_E_NOMEM, "cannot allocate the batch KV cache (" + std::to_string(kv_bytes >> 20) + " MiB)"};
   QD_CK(cudaMemsetAsync(b->kv, 0, kv_bytes, e->stream));
+  std::string terr;
+  if (!make_tmap_2d(&b->kvmap, b->kv, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, kHeadDim, kv_rows, kHeadDim * 2, 64,
+                    kBAttnTile, CU_TENSOR_MAP_SWIZZLE_128B, &terr))
+    throw QdError{QD_E_CUDA, "KV tensor map: " + terr};
 
   const long long maxk = std::max(std::max(d.H, d.QS), d.I);
   const long long parts = std::max(std::max((long long)b->sq * d.R, (long long)b->so * d.H),

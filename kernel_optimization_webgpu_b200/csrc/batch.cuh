@@ -25,14 +25,20 @@
 
 #include "common.cuh"
 #include "gemm_tc.cuh"
+#include "tma.cuh"
 
 namespace qd {
 
 constexpr int kBAttnTile = 64;  // positions per staged K/V tile
 constexpr int kBAttnThreads = 256;
 constexpr int kBErrTimeout = 16;
-// Dynamic shared memory of kb_attn: two stages of K and V tiles.
-constexpr int kBAttnSmem = 2 * 2 * kBAttnTile * kHeadDim * 2;
+constexpr int kMaxParts = 16;   // split-K partials a consumer kernel sums (GEMM split plans stay within)
+// One stage of kb_attn: K and V tiles, each as two 64-position x 64-dim boxes
+// (128-byte rows, 128-byte swizzle), 8 KB per box.
+constexpr int kBAttnBox = kBAttnTile * 64 * 2;
+constexpr int kBAttnStage = 4 * kBAttnBox;
+// Dynamic shared memory of kb_attn: two stages plus alignment slack for the swizzle atoms.
+constexpr int kBAttnSmem = 2 * kBAttnStage + 1024;
 
 struct BatchState {
   int* tokens;    // [B] input token of the step (the previous step's output)
@@ -42,21 +48,39 @@ struct BatchState {
   int max_steps;
 };
 
-// Sum of the split-K partials of element i: parts[s * stride + i], s ascending.
+// Sum of the split-K partials of element i: parts[s * stride + i], s ascending
+// (nparts <= kMaxParts). The loads are unconditional (indices clamped to the
+// last split) so that all of them are in flight before the first add.
+template <int MAXP>
+__device__ __forceinline__ float sum_parts_n(const float* parts, int nparts, long long stride, long long i) {
+  float v[MAXP];
+#pragma unroll
+  for (int s = 0; s < MAXP; ++s) v[s] = parts[(long long)min(s, nparts - 1) * stride + i];
+  float acc = v[0];
+#pragma unroll
+  for (int s = 1; s < MAXP; ++s)
+    if (s < nparts) acc += v[s];
+  return acc;
+}
+
 __device__ __forceinline__ float sum_parts(const float* parts, int nparts, long long stride, long long i) {
-  float v = parts[i];
-  for (int s = 1; s < nparts; ++s) v += parts[(long long)s * stride + i];
-  return v;
+  if (nparts <= 4) return sum_parts_n<4>(parts, nparts, stride, i);
+  if (nparts <= 8) return sum_parts_n<8>(parts, nparts, stride, i);
+  return sum_parts_n<kMaxParts>(parts, nparts, stride, i);
 }
 
 // ---- residual + RMSNorm into the GEMM's hi/lo operands ----------------------------
-// Row b: h[b] = embed row of tokens[b] (embedding mode), or h[b] + sum(parts)
-// (residual mode; parts == nullptr leaves h as is); then
-// x = rms_norm(h[b]) * w -> x_hi[b], x_lo[b]. h is written back in place.
-static __global__ void __launch_bounds__(256) kb_resid_norm(float* h, const float* parts, int nparts, long long part_stride,
-                                                     const __half* embed, const int* tokens, int vocab, const float* w,
-                                                     int K, float eps, __half* x_hi, __half* x_lo, int* err) {
-  __shared__ float red[8];
+// Row b (one CTA of 1024 threads, one element per thread for K <= 1024):
+// h[b] = embed row of tokens[b] (embedding mode), or h[b] + sum(parts) (residual
+// mode; parts == nullptr leaves h as is); then x = rms_norm(h[b]) * w ->
+// x_hi[b], x_lo[b]. h is written back in place.
+constexpr int kNormThreads = 1024;
+static __global__ void __launch_bounds__(kNormThreads) kb_resid_norm(float* h, const float* parts, int nparts,
+                                                                     long long part_stride, const __half* embed,
+                                                                     const int* tokens, int vocab, const float* w,
+                                                                     int K, float eps, __half* x_hi, __half* x_lo,
+                                                                     int* err) {
+  __shared__ float red[kNormThreads / 32];
   pdl_wait();
   const int b = blockIdx.x;
   float* hr = h + (long long)b * K;
@@ -70,7 +94,7 @@ static __global__ void __launch_bounds__(256) kb_resid_norm(float* h, const floa
     er = embed + (long long)tok * K;
   }
   float ss = 0.0f;
-  for (int e = threadIdx.x; e < K; e += 256) {
+  for (int e = threadIdx.x; e < K; e += kNormThreads) {
     float v;
     if (er) v = __half2float(er[e]);
     else if (parts) v = hr[e] + sum_parts(parts, nparts, part_stride, (long long)b * K + e);
@@ -84,9 +108,9 @@ static __global__ void __launch_bounds__(256) kb_resid_norm(float* h, const floa
   pdl_trigger();
   float t = 0.0f;
 #pragma unroll
-  for (int k = 0; k < 8; ++k) t += red[k];
+  for (int k = 0; k < kNormThreads / 32; ++k) t += red[k];
   const float inv = rsqrtf(t / (float)K + eps);
-  for (int e = threadIdx.x; e < K; e += 256) {
+  for (int e = threadIdx.x; e < K; e += kNormThreads) {
     __half hi, lo;
     split_f16(hr[e] * inv * w[e], hi, lo);
     x_hi[(long long)b * K + e] = hi;
@@ -166,33 +190,44 @@ static __global__ void __launch_bounds__(256) kb_rope_cache(const float* parts, 
   pdl_trigger();
 }
 
-// ---- split-KV decode attention with bulk-copy staging ------------------------------
-// Grid (NKV, splits, B); 256 threads serve the G query heads of KV head g.
+// ---- split-KV decode attention with TMA staging ------------------------------------
+// Grid (NKV, splits, B); 256 threads (8 warps) serve the G query heads of KV head g.
 // The CTA covers positions [sp*split_len, min(len, (sp+1)*split_len)) of
 // sequence b, len = pos[b] + 1, in 64-position tiles double-buffered through
-// shared memory (one cp.async.bulk per tile for K and one for V), with an
-// online softmax. Scores: one warp per position (lane = 4 dims). P*V: thread
-// = (position group of 4, dim pair), all G heads at once; groups merged at the end.
-// Partials: ml[b][sp][h] = (running max, sum of exp), o[b][sp][h][128] unnormalised.
+// shared memory by TMA: K and V as two 64x64 boxes each with the 128-byte
+// swizzle (16-byte chunk c of row r sits at chunk c ^ (r & 7)). Thread 0
+// refills a stage once all 8 warps have arrived on its "empty" barrier.
+//
+// Warp w owns positions 8w..8w+7 of every tile and keeps its own online softmax
+// (running max, sum, P*V accumulator): scores with 4 lanes per position (lane =
+// position + 8 * chunk group; the swizzle makes the 8 rows of a load phase hit
+// distinct banks), two shuffles to finish each dot, three for the warp's tile
+// max and sum; P*V with lane = 4 dims. No CTA barrier inside the tile loop; the
+// 8 warps' states are merged once at the end.
+// Partials: ml[b][sp][h] = (max, sum of exp), o[b][sp][h][128] unnormalised.
 template <int G>
-__global__ void __launch_bounds__(kBAttnThreads) kb_attn(const float* q, const __half* kc, const __half* vc,
-                                                          const int* pos, int NH, int NKV, int max_seq, int split_len,
-                                                          int splits, float scale, float2* part_ml, float* part_o,
-                                                          int* err) {
-  extern __shared__ __align__(128) unsigned char attn_smem[];
-  __half* ks = reinterpret_cast<__half*>(attn_smem);                  // [2][64][128]
-  __half* vs = ks + 2 * kBAttnTile * kHeadDim;                        // [2][64][128]
+__global__ void __launch_bounds__(kBAttnThreads) kb_attn(const __grid_constant__ CUtensorMap kvmap, long long k_row0,
+                                                          long long v_row0, const float* q, const int* pos, int NH,
+                                                          int NKV, int max_seq, int split_len, int splits, float scale,
+                                                          float2* part_ml, float* part_o, int* err) {
+  extern __shared__ unsigned char attn_raw[];
+  unsigned char* stages =
+      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(attn_raw) + 1023) & ~uintptr_t(1023));
+  constexpr int kWarps = kBAttnThreads / 32;
   __shared__ __align__(16) float qsm[G][kHeadDim];
-  __shared__ __align__(16) float sc[kBAttnTile][G];
-  __shared__ float run_m[G], run_l[G], tile_f[G];
-  __shared__ __align__(16) float red[3][G][kHeadDim];
-  __shared__ unsigned long long mbar[2];
+  __shared__ float wm[kWarps][G], wl[kWarps][G];
+  __shared__ unsigned long long full[2], empty[2];
+  __shared__ int failed;
   const int g = blockIdx.x, sp = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (tid == 0) {
-    tc_mbar_init(&mbar[0]);
-    tc_mbar_init(&mbar[1]);
+    tc_mbar_init(&full[0]);
+    tc_mbar_init(&full[1]);
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(tc_smem(&empty[0])), "r"(kWarps) : "memory");
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(tc_smem(&empty[1])), "r"(kWarps) : "memory");
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    tma_prefetch_map(&kvmap);
+    failed = 0;
   }
   pdl_wait();
   const int len = min(pos[b], max_seq - 1) + 1;
@@ -204,173 +239,197 @@ __global__ void __launch_bounds__(kBAttnThreads) kb_attn(const float* q, const _
     pdl_trigger();
     return;
   }
-  const __half* kbase = kc + ((long long)b * NKV + g) * max_seq * kHeadDim;
-  const __half* vbase = vc + ((long long)b * NKV + g) * max_seq * kHeadDim;
+  const long long seq_row = ((long long)b * NKV + g) * max_seq;
   const int nt = (hi - lo + kBAttnTile - 1) / kBAttnTile;
-  auto issue = [&](int t) {  // one thread: tile t into buffer t & 1
-    const int p0 = lo + t * kBAttnTile;
-    const int n = min(kBAttnTile, hi - p0);
-    const unsigned bytes = (unsigned)n * kHeadDim * 2;
-    unsigned long long* mb = &mbar[t & 1];
-    __half* kd = ks + (t & 1) * kBAttnTile * kHeadDim;
-    __half* vd = vs + (t & 1) * kBAttnTile * kHeadDim;
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(tc_smem(mb)), "r"(2 * bytes)
+  auto issue = [&](int t) {  // one thread: tile t into stage t & 1
+    const long long row = seq_row + lo + (long long)t * kBAttnTile;
+    unsigned long long* mb = &full[t & 1];
+    unsigned char* st = stages + (t & 1) * kBAttnStage;
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(tc_smem(mb)), "r"(kBAttnStage)
                  : "memory");
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                     tc_smem(kd)),
-                 "l"(kbase + (long long)p0 * kHeadDim), "r"(bytes), "r"(tc_smem(mb))
-                 : "memory");
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                     tc_smem(vd)),
-                 "l"(vbase + (long long)p0 * kHeadDim), "r"(bytes), "r"(tc_smem(mb))
-                 : "memory");
+    tma_load_2d(st, &kvmap, 0, (int)(k_row0 + row), mb);
+    tma_load_2d(st + kBAttnBox, &kvmap, 64, (int)(k_row0 + row), mb);
+    tma_load_2d(st + 2 * kBAttnBox, &kvmap, 0, (int)(v_row0 + row), mb);
+    tma_load_2d(st + 3 * kBAttnBox, &kvmap, 64, (int)(v_row0 + row), mb);
   };
   __syncthreads();  // barrier init visible
+  int issued = 0;   // thread 0 only
   if (tid == 0) {
     issue(0);
-    if (nt > 1) issue(1);
+    issued = 1;
+    if (nt > 1) {
+      issue(1);
+      issued = 2;
+    }
   }
   for (int e = tid; e < G * kHeadDim; e += kBAttnThreads)
     qsm[e / kHeadDim][e % kHeadDim] = q[((long long)b * NH + (long long)g * G) * kHeadDim + e];
-  if (tid < G) {
-    run_m[tid] = -INFINITY;
-    run_l[tid] = 0.0f;
-  }
   __syncthreads();
-  float4 qv[G];
-#pragma unroll
-  for (int h = 0; h < G; ++h) qv[h] = reinterpret_cast<const float4*>(qsm[h])[lane];
-  const int dp = tid & 63, grp = tid >> 6;  // P*V: dims 2dp, 2dp+1; positions j = grp mod 4
-  float acc[G][2];
-#pragma unroll
-  for (int h = 0; h < G; ++h) acc[h][0] = acc[h][1] = 0.0f;
-  int failed_at = -1;
 
-  for (int t = 0; t < nt; ++t) {
+  const int pl = lane & 7, l4 = lane >> 3;  // scores: position 8w + pl, chunk group l4
+  float m_run[G], l_run[G], acc[G][4];
+#pragma unroll
+  for (int h = 0; h < G; ++h) {
+    m_run[h] = -INFINITY;
+    l_run[h] = 0.0f;
+    acc[h][0] = acc[h][1] = acc[h][2] = acc[h][3] = 0.0f;
+  }
+  // P*V: lane holds dims 4*lane .. 4*lane + 3 (half lane >> 4 of the row)
+  const int vcol = (4 * lane) & 63, vcc = vcol >> 3, vhalf = lane >> 4;
+  int consumed = 0;  // tiles this warp has waited for
+  bool ok = true;
+  for (int t = 0; t < nt && ok; ++t) {
     const int buf = t & 1;
+    if (tid == 0 && t >= 1 && t + 1 < nt) {  // refill the stage tile t-1 used with tile t+1
+      ok = tc_mbar_wait(&empty[(t + 1) & 1], (unsigned)((t - 1) >> 1) & 1u);
+      if (ok) {
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        issue(t + 1);
+        issued = t + 2;
+      }
+    }
+    ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+    if (ok) ok = tc_mbar_wait(&full[buf], (unsigned)(t >> 1) & 1u);
+    ok = __all_sync(0xffffffffu, ok);
+    if (!ok) break;
+    consumed = t + 1;
     const int n = min(kBAttnTile, hi - (lo + t * kBAttnTile));
-    const bool ok = tc_mbar_wait(&mbar[buf], (unsigned)(t >> 1) & 1u);
-    if (__syncthreads_or(!ok)) {
-      failed_at = t;
-      break;
-    }
-    const __half* kt = ks + buf * kBAttnTile * kHeadDim;
-    const __half* vt = vs + buf * kBAttnTile * kHeadDim;
-    for (int j = warp; j < n; j += 8) {
-      const uint2 u = *reinterpret_cast<const uint2*>(kt + j * kHeadDim + 4 * lane);
-      const float2 k01 = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
-      const float2 k23 = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+    const unsigned char* st = stages + buf * kBAttnStage;
+    const int j = 8 * warp + pl;
+    // scores
+    float s[G];
+#pragma unroll
+    for (int h = 0; h < G; ++h) s[h] = 0.0f;
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      const int c = l4 + 4 * m;  // 16-byte chunk of the row (dims 8c .. 8c+7)
+      const uint4 u = *reinterpret_cast<const uint4*>(st + (c >> 3) * kBAttnBox + j * 128 + (((c & 7) ^ pl) << 4));
+      const float2 k0 = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+      const float2 k1 = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+      const float2 k2 = __half22float2(*reinterpret_cast<const __half2*>(&u.z));
+      const float2 k3 = __half22float2(*reinterpret_cast<const __half2*>(&u.w));
 #pragma unroll
       for (int h = 0; h < G; ++h) {
-        float d = qv[h].x * k01.x + qv[h].y * k01.y + qv[h].z * k23.x + qv[h].w * k23.y;
-        d = warp_sum(d);
-        if (lane == 0) sc[j][h] = d * scale;
+        const float4 qa = reinterpret_cast<const float4*>(qsm[h])[2 * c];
+        const float4 qb = reinterpret_cast<const float4*>(qsm[h])[2 * c + 1];
+        s[h] += qa.x * k0.x + qa.y * k0.y + qa.z * k1.x + qa.w * k1.y + qb.x * k2.x + qb.y * k2.y + qb.z * k3.x +
+                qb.w * k3.y;
       }
     }
-    __syncthreads();
-    if (warp < G) {  // tile max, probabilities, running max / sum of head `warp`
-      const int h = warp;
-      float tm = -INFINITY;
-      for (int j = lane; j < n; j += 32) tm = fmaxf(tm, sc[j][h]);
-      tm = warp_max(tm);
-      const float mp = run_m[h];
-      const float mn = fmaxf(mp, tm);
-      float ts = 0.0f;
-      for (int j = lane; j < n; j += 32) {
-        const float pj = expf(sc[j][h] - mn);
-        sc[j][h] = pj;
-        ts += pj;
-      }
-      ts = warp_sum(ts);
-      if (lane == 0) {
-        const float f = (mp == -INFINITY) ? 0.0f : expf(mp - mn);
-        tile_f[h] = f;
-        run_m[h] = mn;
-        run_l[h] = run_l[h] * f + ts;
-      }
-    }
-    __syncthreads();
-    {
-      const __half2* vrow = reinterpret_cast<const __half2*>(vt) + dp;
+    float p[G];
 #pragma unroll
-      for (int h = 0; h < G; ++h) {
-        const float f = tile_f[h];
+    for (int h = 0; h < G; ++h) {
+      s[h] += __shfl_xor_sync(0xffffffffu, s[h], 8);
+      s[h] += __shfl_xor_sync(0xffffffffu, s[h], 16);
+      const float sv = j < n ? s[h] * scale : -INFINITY;
+      float tm = fmaxf(sv, __shfl_xor_sync(0xffffffffu, sv, 1));
+      tm = fmaxf(tm, __shfl_xor_sync(0xffffffffu, tm, 2));
+      tm = fmaxf(tm, __shfl_xor_sync(0xffffffffu, tm, 4));
+      const float mn = fmaxf(m_run[h], tm);  // finite: the warp holds at least one valid position or mn = m_run
+      p[h] = (j < n) ? expf(sv - mn) : 0.0f;
+      float ps = p[h] + __shfl_xor_sync(0xffffffffu, p[h], 1);
+      ps += __shfl_xor_sync(0xffffffffu, ps, 2);
+      ps += __shfl_xor_sync(0xffffffffu, ps, 4);
+      const float f = (m_run[h] == -INFINITY) ? 0.0f : expf(m_run[h] - mn);
+      if (mn != -INFINITY) {
+        l_run[h] = l_run[h] * f + ps;
+        m_run[h] = mn;
         acc[h][0] *= f;
         acc[h][1] *= f;
+        acc[h][2] *= f;
+        acc[h][3] *= f;
       }
-      for (int j = grp; j < n; j += 4) {
-        const float2 v = __half22float2(vrow[j * (kHeadDim / 2)]);
+    }
+    // P*V over the warp's 8 positions
+    const unsigned char* vrow = st + (2 + vhalf) * kBAttnBox + (vcol & 7) * 2;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int jj = 8 * warp + k;
+      float pk[G];
+#pragma unroll
+      for (int h = 0; h < G; ++h) pk[h] = __shfl_sync(0xffffffffu, p[h], k);
+      if (jj < n) {
+        const uint2 u = *reinterpret_cast<const uint2*>(vrow + jj * 128 + ((vcc ^ k) << 4));
+        const float2 v01 = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+        const float2 v23 = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
 #pragma unroll
         for (int h = 0; h < G; ++h) {
-          const float pj = sc[j][h];
-          acc[h][0] += pj * v.x;
-          acc[h][1] += pj * v.y;
+          acc[h][0] += pk[h] * v01.x;
+          acc[h][1] += pk[h] * v01.y;
+          acc[h][2] += pk[h] * v23.x;
+          acc[h][3] += pk[h] * v23.y;
         }
       }
     }
-    __syncthreads();  // buffer and scores consumed
-    if (tid == 0 && t + 2 < nt) {
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      issue(t + 2);
-    }
+    __syncwarp();
+    if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tc_smem(&empty[buf])) : "memory");
   }
-  if (failed_at >= 0) {
-    // Copies still in flight (tiles failed_at and failed_at + 1) land in this
-    // CTA's shared memory: give them a bounded chance to finish before exiting.
+  if (!ok && lane == 0) atomicOr(&failed, 1);
+  __syncthreads();
+  if (failed) {
+    // Copies still in flight land in this CTA's shared memory: give each a
+    // bounded chance to finish before exiting.
     if (tid == 0) {
-      for (int t = failed_at; t < min(nt, failed_at + 2); ++t) (void)tc_mbar_wait(&mbar[t & 1], (unsigned)(t >> 1) & 1u);
+      for (int t = consumed; t < issued; ++t) (void)tc_mbar_wait(&full[t & 1], (unsigned)(t >> 1) & 1u);
       atomicOr(err, kBErrTimeout);
     }
     pdl_trigger();
     return;
   }
   pdl_trigger();
-  // Merge the 4 position groups.
-  if (grp > 0) {
+  // Merge the 8 warps' softmax states (the stages are free now: every tile was consumed).
+  float* wo = reinterpret_cast<float*>(stages);  // [kWarps][G][128]
 #pragma unroll
-    for (int h = 0; h < G; ++h) {
-      red[grp - 1][h][2 * dp] = acc[h][0];
-      red[grp - 1][h][2 * dp + 1] = acc[h][1];
+  for (int h = 0; h < G; ++h) {
+    *reinterpret_cast<float4*>(&wo[(warp * G + h) * kHeadDim + 4 * lane]) =
+        make_float4(acc[h][0], acc[h][1], acc[h][2], acc[h][3]);
+    if (lane == 0) {
+      wm[warp][h] = m_run[h];
+      wl[warp][h] = l_run[h];
     }
   }
   __syncthreads();
-  if (grp == 0) {
+  if (tid < G * kHeadDim) {
+    const int h = tid / kHeadDim, d = tid % kHeadDim;
+    float M = -INFINITY;
 #pragma unroll
-    for (int h = 0; h < G; ++h) {
-      float o0 = acc[h][0], o1 = acc[h][1];
+    for (int w = 0; w < kWarps; ++w) M = fmaxf(M, wm[w][h]);
+    float L = 0.0f, O = 0.0f;
 #pragma unroll
-      for (int k = 0; k < 3; ++k) {
-        o0 += red[k][h][2 * dp];
-        o1 += red[k][h][2 * dp + 1];
-      }
-      *reinterpret_cast<float2*>(part_o + (slot + h) * kHeadDim + 2 * dp) = make_float2(o0, o1);
+    for (int w = 0; w < kWarps; ++w) {
+      const float f = wm[w][h] == -INFINITY ? 0.0f : expf(wm[w][h] - M);
+      L += wl[w][h] * f;
+      O += wo[(w * G + h) * kHeadDim + d] * f;
     }
+    part_o[(slot + h) * kHeadDim + d] = O;
+    if (d == 0) part_ml[slot + h] = make_float2(M, L);
   }
-  if (tid < G) part_ml[slot + tid] = make_float2(run_m[tid], run_l[tid]);
 }
 
-// Merge the splits of every head of row b into the o GEMM's operands x_hi/x_lo [B][NH*128].
-static __global__ void __launch_bounds__(256) kb_attn_combine(const float2* part_ml, const float* part_o, int splits, int NH,
-                                                       __half* x_hi, __half* x_lo) {
+// Merge the splits of head h (blockIdx.x) of row b (blockIdx.y) into the o GEMM's
+// operands x_hi/x_lo [B][NH*128]; one thread per dim.
+static __global__ void __launch_bounds__(kHeadDim) kb_attn_combine(const float2* part_ml, const float* part_o,
+                                                                   int splits, int NH, __half* x_hi, __half* x_lo) {
   pdl_wait();
-  const int b = blockIdx.x, QS = NH * kHeadDim;
-  for (int e = threadIdx.x; e < QS; e += 256) {
-    const int h = e / kHeadDim;
-    float M = -INFINITY;
-    for (int s = 0; s < splits; ++s) M = fmaxf(M, part_ml[((long long)b * splits + s) * NH + h].x);
-    float L = 0.0f, O = 0.0f;
-    for (int s = 0; s < splits; ++s) {
-      const float2 ml = part_ml[((long long)b * splits + s) * NH + h];
-      const float f = ml.y > 0.0f ? expf(ml.x - M) : 0.0f;
-      L += ml.y * f;
-      O += part_o[((long long)b * splits + s) * QS + e] * f;
-    }
-    __half hh, ll;
-    split_f16(O / L, hh, ll);
-    x_hi[(long long)b * QS + e] = hh;
-    x_lo[(long long)b * QS + e] = ll;
+  const int h = blockIdx.x, b = blockIdx.y, d = threadIdx.x, QS = NH * kHeadDim;
+  const float2* ml = part_ml + (long long)b * splits * NH + h;
+  const float* po = part_o + (long long)b * splits * QS + (long long)h * kHeadDim + d;
+  float M = -INFINITY;
+#pragma unroll 8
+  for (int s = 0; s < splits; ++s) M = fmaxf(M, ml[(long long)s * NH].x);
+  float L = 0.0f, O = 0.0f;
+#pragma unroll 8
+  for (int s = 0; s < splits; ++s) {
+    const float2 m = ml[(long long)s * NH];
+    const float f = m.y > 0.0f ? expf(m.x - M) : 0.0f;
+    L += m.y * f;
+    O += po[(long long)s * QS] * f;
   }
   pdl_trigger();
+  __half hh, ll;
+  split_f16(O / L, hh, ll);
+  x_hi[(long long)b * QS + h * kHeadDim + d] = hh;
+  x_lo[(long long)b * QS + h * kHeadDim + d] = ll;
 }
 
 // silu(gate) * up from the gate/up GEMM's interleaved partials (column 2j = gate

@@ -670,24 +670,27 @@ double ms_since(std::chrono::steady_clock::time_point t0) {
 
 namespace {
 
-size_t tc_smem_bytes(int bn, bool af16) {
-  return (size_t)2 * ((af16 ? 1 : 2) * kTcM * kTcK * 2 + 2 * bn * kTcK * 2) + 1024;
-}
-
 template <int BN, bool AF16, int EPI>
-void launch_gemm_t(const TcArgs& a, int splits, cudaStream_t s) {
-  const size_t smem = tc_smem_bytes(BN, AF16);
+void launch_gemm_t(TcArgs a, int splits, cudaStream_t s) {
+  const size_t smem = tc_smem_total<BN, AF16>();
   static unsigned long long configured = 0;  // one bit per device ordinal: the attribute is per context
-  int dev = 0;
-  QD_CK(cudaGetDevice(&dev));
-  const unsigned long long bit = 1ull << (dev & 63);
-  if (!(configured & bit)) {
-    QD_CK(cudaFuncSetAttribute(k_gemm_tc<BN, AF16, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    configured |= bit;
-  }
+  allow_smem(k_gemm_tc<BN, AF16, EPI>, smem, configured);
+  std::string err;
+  bool ok;
+  if (AF16)
+    ok = make_tmap_2d(&a.tm_w, a.a16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a.K, a.n_rows, a.a16_stride * 2, kTcK, kTcM,
+                      CU_TENSOR_MAP_SWIZZLE_128B, &err);
+  else
+    ok = make_tmap_2d(&a.tm_w, a.w, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.K / 2, a.n_rows, a.w_stride, 32, kTcM,
+                      CU_TENSOR_MAP_SWIZZLE_NONE, &err);
+  ok = ok && make_tmap_2d(&a.tm_xh, a.x_hi, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a.K, a.B, a.ldx * 2, kTcK, BN,
+                          CU_TENSOR_MAP_SWIZZLE_128B, &err);
+  ok = ok && make_tmap_2d(&a.tm_xl, a.x_lo, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a.K, a.B, a.ldx * 2, kTcK, BN,
+                          CU_TENSOR_MAP_SWIZZLE_128B, &err);
+  if (!ok) throw QdError{QD_E_CUDA, "GEMM tensor maps: " + err};
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((a.n_rows + kTcM - 1) / kTcM, (a.B + BN - 1) / BN, splits);
-  cfg.blockDim = dim3(kTcThreads);
+  cfg.blockDim = dim3(kTcThreads + 32);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
@@ -711,6 +714,11 @@ int gemm_plan_splits(int K, int want, int* kt_split) {
 
 void launch_gemm(TcArgs a, int splits, int mode, cudaStream_t s) {
   if (a.K % kTcK || a.K <= 0 || a.B <= 0 || a.n_rows <= 0) throw QdError{QD_E_INVALID, "GEMM: bad dimensions"};
+  if (mode == kGemmQ4Store && ((reinterpret_cast<uintptr_t>(a.w) & 15) || (a.w_stride & 15) ||
+                               (reinterpret_cast<uintptr_t>(a.s) & 3) || (a.s_stride & 3)))
+    throw QdError{QD_E_INVALID, "GEMM: q4 rows must be 16-byte aligned, scales 4-byte aligned"};
+  if ((reinterpret_cast<uintptr_t>(a.x_hi) & 15) || (reinterpret_cast<uintptr_t>(a.x_lo) & 15))
+    throw QdError{QD_E_INVALID, "GEMM: activations must be 16-byte aligned"};
   if (a.kt_split <= 0) a.kt_split = (a.K / kTcK + splits - 1) / splits;
   if (a.ldx == 0) a.ldx = a.K;
   if (mode == kGemmQ4Store) {

@@ -35,6 +35,7 @@
 #pragma once
 
 #include "common.cuh"
+#include "tma.cuh"
 
 namespace qd {
 
@@ -51,6 +52,11 @@ enum TcEpi : int {
 };
 
 struct TcArgs {
+  // Tensor maps (filled by the host launcher from the pointers below):
+  // tm_w: q4 nibble bytes [n_rows][K/2] (box 32 B x 128 rows) or the f16 table
+  // [n_rows][K] (box 64 x 128, 128-byte swizzle); tm_xh / tm_xl: the
+  // activations [B][K] f16 (box 64 x BN, 128-byte swizzle).
+  CUtensorMap tm_w, tm_xh, tm_xl;
   // q4 weights: row n's 16-byte blocks at w + n*w_stride, its f16 scales at s + n*s_stride
   const char* w;
   const char* s;
@@ -191,92 +197,55 @@ __device__ __forceinline__ void warp_argmax_columns(float (&v)[32], uint32_t (&i
   }
 }
 
-// Raw weight data of one k-tile held in registers between its load and its
-// dequantisation into shared memory (so the next tile's loads overlap this one's MMAs).
-template <bool AF16>
-struct TcRaw;
-template <>
-struct TcRaw<false> {  // q4: this thread's row, two blocks
-  uint4 q[2];
-  uint32_t sc;  // two f16 scales
-};
-template <>
-struct TcRaw<true> {  // f16: 8 chunks of 16 B (4 rows per warp pass)
-  uint4 c[8];
-};
-
-template <bool AF16>
-__device__ __forceinline__ void tc_load_raw(const TcArgs& a, int n0, int kt, int tid, TcRaw<AF16>& r) {
-  if constexpr (!AF16) {
-    const int n = n0 + tid;
-    if (n < a.n_rows) {
-      const uint4* wb = reinterpret_cast<const uint4*>(a.w + (long long)n * a.w_stride) + kt * 2;
-      r.q[0] = ld_stream(wb);
-      r.q[1] = ld_stream(wb + 1);
-      r.sc = *reinterpret_cast<const uint32_t*>(a.s + (long long)n * a.s_stride + kt * 4);
-    } else {
-      r.q[0] = r.q[1] = make_uint4(0, 0, 0, 0);
-      r.sc = 0;
-    }
-  } else {
-    const int warp = tid >> 5, lane = tid & 31;
-#pragma unroll
-    for (int it = 0; it < 8; ++it) {
-      const int n = n0 + warp * 32 + it * 4 + (lane >> 3);
-      r.c[it] = n < a.n_rows
-                    ? ld_stream(reinterpret_cast<const uint4*>(a.a16 + (long long)n * a.a16_stride + kt * kTcK) + (lane & 7))
-                    : make_uint4(0, 0, 0, 0);
-    }
-  }
+// Reduction barrier over the 128 consumer threads (named barrier 1): true if
+// any thread passes `pred`.
+__device__ __forceinline__ bool consumers_any(bool pred) {
+  unsigned r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.or.pred q, 1, %2, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((unsigned)pred), "r"(kTcThreads)
+      : "memory");
+  return r != 0;
 }
 
-template <bool AF16>
-__device__ __forceinline__ void tc_store_raw(const TcRaw<AF16>& r, int tid, unsigned char* A_hi, unsigned char* A_lo) {
-  if constexpr (!AF16) {
-    __half2 s2 = *reinterpret_cast<const __half2*>(&r.sc);
-    const float sc[2] = {__low2float(s2) * (float)(1 << kWShift), __high2float(s2) * (float)(1 << kWShift)};
-#pragma unroll
-    for (int blk = 0; blk < 2; ++blk) {
-      const uint32_t ws[4] = {r.q[blk].x, r.q[blk].y, r.q[blk].z, r.q[blk].w};
-#pragma unroll
-      for (int wi = 0; wi < 4; ++wi) {  // 8 columns per word -> one 16-byte chunk of f16
-        __align__(16) __half hi8[8], lo8[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float v = (float)((int)((ws[wi] >> (4 * i)) & 0xFu) - 8) * sc[blk];
-          split_f16(v, hi8[i], lo8[i]);
-        }
-        const unsigned off = sw128_off(tid, blk * 32 + wi * 8);
-        *reinterpret_cast<uint4*>(A_hi + off) = *reinterpret_cast<const uint4*>(hi8);
-        *reinterpret_cast<uint4*>(A_lo + off) = *reinterpret_cast<const uint4*>(lo8);
-      }
-    }
-  } else {
-    (void)A_lo;
-    const int warp = tid >> 5, lane = tid & 31;
-#pragma unroll
-    for (int it = 0; it < 8; ++it) {
-      const int row = warp * 32 + it * 4 + (lane >> 3);
-      *reinterpret_cast<uint4*>(A_hi + sw128_off(row, (lane & 7) * 8)) = r.c[it];
-    }
-  }
+template <int BN, bool AF16>
+__host__ __device__ constexpr int tc_stages() {
+  return AF16 ? (BN <= 64 ? 4 : 3) : (BN <= 64 ? 4 : (BN <= 128 ? 3 : 2));
+}
+template <int BN, bool AF16>
+__host__ __device__ constexpr int tc_stage_bytes() {
+  return (AF16 ? kTcM * kTcK * 2 : kTcM * 32) + 2 * BN * kTcK * 2;
+}
+template <int BN, bool AF16>
+__host__ __device__ constexpr int tc_smem_total() {
+  return tc_stages<BN, AF16>() * tc_stage_bytes<BN, AF16>() + (AF16 ? 0 : 2 * 2 * kTcM * kTcK * 2) + 1024;
 }
 
-// Grid: (ceil(n_rows / 128), ceil(B / BN), splits). Shared memory: 2 stages of
-// A_hi [128][64] f16 (+ A_lo for q4) + B_hi, B_lo [BN][64] f16, 1024-aligned.
-// Split z covers k-tiles [z * kt_split, min((z + 1) * kt_split, K / 64)).
+// Grid: (ceil(n_rows / 128), ceil(B / BN), splits); 160 threads. Split z covers
+// k-tiles [z * kt_split, min((z + 1) * kt_split, K / 64)).
+// Warp 4 is the producer: one lane streams each k-tile's weights (raw q4
+// nibbles, or the f16 table tile) and the x_hi / x_lo tiles into a ring of S
+// stages by TMA, refilling a stage when the MMAs that read it have committed
+// to its "empty" barrier. Warps 0-3 dequantise the nibbles (thread = weight
+// row) into a double-buffered A_hi / A_lo stage; thread 0 then issues the MMAs.
+// The same four warps run the epilogue from TMEM.
 template <int BN, bool AF16, int EPI>
-__global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const TcArgs a) {
+__global__ void __launch_bounds__(kTcThreads + 32, 1) k_gemm_tc(const __grid_constant__ TcArgs a) {
+  constexpr int S = tc_stages<BN, AF16>();
+  constexpr int kW = AF16 ? kTcM * kTcK * 2 : kTcM * 32;
+  constexpr int kBt = BN * kTcK * 2;
+  constexpr int kStage = tc_stage_bytes<BN, AF16>();
+  constexpr int kA = kTcM * kTcK * 2;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
-  // 1024-byte alignment of every tile (the swizzle atoms)
-  unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  constexpr int kA = kTcM * kTcK * 2;       // 16 KB
-  constexpr int kB = BN * kTcK * 2;
-  constexpr int kStage = (AF16 ? 1 : 2) * kA + 2 * kB;
-  __shared__ unsigned long long mbar[2];
+  unsigned char* ring =
+      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  unsigned char* abuf = ring + S * kStage;  // q4: [2][A_hi | A_lo]
+  __shared__ unsigned long long full[S], empty[S], adone[2];
   __shared__ unsigned tmem_base;
   __shared__ float red_v[EPI == kTcArgmax ? 4 : 1][EPI == kTcArgmax ? BN : 1];
   __shared__ uint32_t red_i[EPI == kTcArgmax ? 4 : 1][EPI == kTcArgmax ? BN : 1];
+  __shared__ int failed;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int n0 = blockIdx.x * kTcM;
   const int b0 = blockIdx.y * BN;
@@ -291,81 +260,172 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const TcArgs a) {
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
   if (tid == 0) {
-    tc_mbar_init(&mbar[0]);
-    tc_mbar_init(&mbar[1]);
+#pragma unroll
+    for (int i = 0; i < S; ++i) {
+      tc_mbar_init(&full[i]);
+      tc_mbar_init(&empty[i]);
+    }
+    tc_mbar_init(&adone[0]);
+    tc_mbar_init(&adone[1]);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    failed = 0;
   }
-  // The weights are constant: the first tile is fetched before waiting for the
-  // kernel that produces the activations.
-  TcRaw<AF16> raw;
-  tc_load_raw<AF16>(a, n0, kt0, tid, raw);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  pdl_wait();
   const unsigned tmem = tmem_base;
-  const unsigned idesc = umma_idesc_f16_f32(kTcM, BN);
-  bool ok = true;
 
-  for (int i = 0; i < nk; ++i) {
-    const int kt = kt0 + i;
-    const int st = i & 1;
-    unsigned char* A_hi = smem + st * kStage;
-    unsigned char* A_lo = A_hi + kA;  // q4 only
-    unsigned char* B_hi = A_hi + (AF16 ? 1 : 2) * kA;
-    unsigned char* B_lo = B_hi + kB;
-    // The MMAs that last read this stage (tile i-2) must be done.
-    if (i >= 2) ok = tc_mbar_wait(&mbar[st], (unsigned)((i - 2) >> 1) & 1u) && ok;
-    tc_store_raw<AF16>(raw, tid, A_hi, A_lo);
-    if (i + 1 < nk) tc_load_raw<AF16>(a, n0, kt + 1, tid, raw);
-    // Activation tiles: BN rows x 64 columns of x_hi / x_lo (rows beyond B are zero).
-    for (int c = tid; c < BN * 8; c += kTcThreads) {  // 16-byte chunks
-      const int r = c >> 3, ch = c & 7;
-      const int b = b0 + r;
-      uint4 vh = make_uint4(0, 0, 0, 0), vl = make_uint4(0, 0, 0, 0);
-      if (b < a.B) {
-        vh = *reinterpret_cast<const uint4*>(a.x_hi + (long long)b * a.ldx + kt * kTcK + ch * 8);
-        vl = *reinterpret_cast<const uint4*>(a.x_lo + (long long)b * a.ldx + kt * kTcK + ch * 8);
-      }
-      const unsigned off = sw128_off(r, ch * 8);
-      *reinterpret_cast<uint4*>(B_hi + off) = vh;
-      *reinterpret_cast<uint4*>(B_lo + off) = vl;
-    }
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    __syncthreads();
-    if (tid == 0) {
-      tc_fence_after();
+  if (warp == kTcThreads / 32) {
+    // ---- producer ----
+    if (lane == 0) {
+      tma_prefetch_map(&a.tm_w);
+      tma_prefetch_map(&a.tm_xh);
+      tma_prefetch_map(&a.tm_xl);
+      bool ok = true;
+      int last[S];
 #pragma unroll
-      for (int ks = 0; ks < kTcK / 16; ++ks) {
-        const unsigned long long dah = umma_desc_k_sw128(tc_smem(A_hi) + ks * 32);
-        const unsigned long long dbh = umma_desc_k_sw128(tc_smem(B_hi) + ks * 32);
-        const unsigned long long dbl = umma_desc_k_sw128(tc_smem(B_lo) + ks * 32);
-        const bool acc = i > 0 || ks > 0;
-        umma_f16(tmem, dah, dbh, idesc, acc);
-        umma_f16(tmem + BN, dah, dbl, idesc, acc);
-        if constexpr (!AF16) {
-          const unsigned long long dal = umma_desc_k_sw128(tc_smem(A_lo) + ks * 32);
-          umma_f16(tmem + BN, dal, dbh, idesc, true);
+      for (int i = 0; i < S; ++i) last[i] = -1;
+      // The weights are constant: the first stages' weight tiles go out before
+      // waiting for the kernel that produces the activations.
+      const int pre = min(S, nk);
+      for (int k = 0; k < pre; ++k) {
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(tc_smem(&full[k])),
+                     "r"(kW + 2 * kBt)
+                     : "memory");
+        tma_load_2d(ring + k * kStage, &a.tm_w, AF16 ? (kt0 + k) * kTcK : (kt0 + k) * 32, n0, &full[k]);
+      }
+      pdl_wait();
+      for (int k = 0; k < nk; ++k) {
+        const int slot = k % S;
+        unsigned char* st = ring + slot * kStage;
+        if (k >= S) {
+          if (!tc_mbar_wait(&empty[slot], (unsigned)((k / S) - 1) & 1u)) {
+            ok = false;
+            break;
+          }
+          asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(tc_smem(&full[slot])),
+                       "r"(kW + 2 * kBt)
+                       : "memory");
+          tma_load_2d(st, &a.tm_w, AF16 ? (kt0 + k) * kTcK : (kt0 + k) * 32, n0, &full[slot]);
+        }
+        tma_load_2d(st + kW, &a.tm_xh, (kt0 + k) * kTcK, b0, &full[slot]);
+        tma_load_2d(st + kW + kBt, &a.tm_xl, (kt0 + k) * kTcK, b0, &full[slot]);
+        last[slot] = k;
+      }
+      if (!ok) atomicOr(&failed, 1);
+      // Nothing may still be landing in shared memory when the CTA exits: the
+      // newest tile of each stage is the only one that can be in flight.
+#pragma unroll
+      for (int i = 0; i < S; ++i)
+        if (last[i] >= 0) (void)tc_mbar_wait(&full[i], (unsigned)(last[i] / S) & 1u);
+    }
+  } else {
+    // ---- consumers: dequantisation, MMA issue, epilogue ----
+    pdl_wait();
+    const unsigned idesc = umma_idesc_f16_f32(kTcM, BN);
+    const int n = n0 + tid;
+    const bool row_live = n < a.n_rows;
+    uint32_t sc_cur = 0, sc_next = 0;
+    if constexpr (!AF16) {
+      const char* srow = a.s + (long long)(row_live ? n : 0) * a.s_stride;
+      if (row_live) {
+        sc_cur = *reinterpret_cast<const uint32_t*>(srow + kt0 * 4);
+        if (nk > 1) sc_next = *reinterpret_cast<const uint32_t*>(srow + (kt0 + 1) * 4);
+      }
+    }
+    bool ok = true;
+    int committed = -1;  // thread 0: last tile whose MMAs were committed
+    for (int i = 0; i < nk; ++i) {
+      const int slot = i % S, st = i & 1;
+      unsigned char* stg = ring + slot * kStage;
+      if constexpr (!AF16) {
+        ok = tc_mbar_wait(&full[slot], (unsigned)(i / S) & 1u) && ok;
+        if (i >= 2) ok = tc_mbar_wait(&adone[st], (unsigned)((i - 2) >> 1) & 1u) && ok;
+        unsigned char* A_hi = abuf + st * 2 * kA;
+        unsigned char* A_lo = A_hi + kA;
+        if (ok) {
+          const uint4* raw = reinterpret_cast<const uint4*>(stg + tid * 32);
+          const uint4 q0 = raw[0], q1 = raw[1];
+          const __half2 s2 = *reinterpret_cast<const __half2*>(&sc_cur);
+          const float sc[2] = {__low2float(s2) * (float)(1 << kWShift), __high2float(s2) * (float)(1 << kWShift)};
+          const uint32_t ws[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+#pragma unroll
+          for (int wi = 0; wi < 8; ++wi) {  // 8 columns per word -> one 16-byte chunk of f16
+            __align__(16) __half hi8[8], lo8[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              const float v = (float)((int)((ws[wi] >> (4 * e)) & 0xFu) - 8) * sc[wi >> 2];
+              split_f16(v, hi8[e], lo8[e]);
+            }
+            const unsigned off = sw128_off(tid, wi * 8);
+            *reinterpret_cast<uint4*>(A_hi + off) = *reinterpret_cast<const uint4*>(hi8);
+            *reinterpret_cast<uint4*>(A_lo + off) = *reinterpret_cast<const uint4*>(lo8);
+          }
+          sc_cur = sc_next;
+          if (row_live && i + 2 < nk)
+            sc_next = *reinterpret_cast<const uint32_t*>(a.s + (long long)n * a.s_stride + (kt0 + i + 2) * 4);
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        if (consumers_any(!ok)) {
+          ok = false;
+          break;
+        }
+        if (tid == 0) {
+          tc_fence_after();
+#pragma unroll
+          for (int ks = 0; ks < kTcK / 16; ++ks) {
+            const unsigned long long dah = umma_desc_k_sw128(tc_smem(A_hi) + ks * 32);
+            const unsigned long long dal = umma_desc_k_sw128(tc_smem(A_lo) + ks * 32);
+            const unsigned long long dbh = umma_desc_k_sw128(tc_smem(stg + kW) + ks * 32);
+            const unsigned long long dbl = umma_desc_k_sw128(tc_smem(stg + kW + kBt) + ks * 32);
+            const bool acc = i > 0 || ks > 0;
+            umma_f16(tmem, dah, dbh, idesc, acc);
+            umma_f16(tmem + BN, dah, dbl, idesc, acc);
+            umma_f16(tmem + BN, dal, dbh, idesc, true);
+          }
+          umma_commit(&empty[slot]);
+          umma_commit(&adone[st]);
+          committed = i;
+        }
+      } else {
+        if (tid == 0) {  // the table tile arrives ready to use: only the MMAs to issue
+          if (!tc_mbar_wait(&full[slot], (unsigned)(i / S) & 1u)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll
+          for (int ks = 0; ks < kTcK / 16; ++ks) {
+            const unsigned long long da = umma_desc_k_sw128(tc_smem(stg) + ks * 32);
+            const unsigned long long dbh = umma_desc_k_sw128(tc_smem(stg + kW) + ks * 32);
+            const unsigned long long dbl = umma_desc_k_sw128(tc_smem(stg + kW + kBt) + ks * 32);
+            const bool acc = i > 0 || ks > 0;
+            umma_f16(tmem, da, dbh, idesc, acc);
+            umma_f16(tmem + BN, da, dbl, idesc, acc);
+          }
+          umma_commit(&empty[slot]);
+          umma_commit(&adone[st]);
+          committed = i;
         }
       }
-      umma_commit(&mbar[st]);
     }
+    // Wait for the last MMAs (they complete in order).
+    if (tid == 0 && committed >= 0)
+      ok = tc_mbar_wait(&adone[committed & 1], (unsigned)(committed >> 1) & 1u) && ok;
+    if (consumers_any(!ok) || (tid == 0 && committed != nk - 1)) ok = false;
+    if (!ok && tid == 0) atomicOr(&failed, 1);
   }
-  // Wait for the last MMAs (both stages' final commits).
-  if (nk >= 2) ok = tc_mbar_wait(&mbar[(nk - 2) & 1], (unsigned)((nk - 2) >> 1) & 1u) && ok;
-  ok = tc_mbar_wait(&mbar[(nk - 1) & 1], (unsigned)((nk - 1) >> 1) & 1u) && ok;
+  __syncthreads();
   tc_fence_after();
   pdl_trigger();
 
-  // Epilogue: warp w reads TMEM lanes 32w..32w+31 = weight rows n0 + 32w + lane.
-  const int n = n0 + warp * 32 + lane;
-  const bool row_live = n < a.n_rows;
-  const unsigned lane_base = (unsigned)(warp * 32) << 16;
-  const float unscale = AF16 ? 1.0f : 1.0f / (float)(1 << kWShift);
-  float* y = a.y ? a.y + (long long)blockIdx.z * a.y_split : nullptr;
-  if (!__syncthreads_and(ok)) {
-    if (tid == 0 && a.err) atomicOr(a.err, kTcErrTimeout);
-  } else {
+  if (tid < kTcThreads && !failed) {
+    // Epilogue: warp w reads TMEM lanes 32w..32w+31 = weight rows n0 + 32w + lane.
+    const int n = n0 + warp * 32 + lane;
+    const bool row_live = n < a.n_rows;
+    const unsigned lane_base = (unsigned)(warp * 32) << 16;
+    const float unscale = AF16 ? 1.0f : 1.0f / (float)(1 << kWShift);
+    float* y = a.y ? a.y + (long long)blockIdx.z * a.y_split : nullptr;
 #pragma unroll 1
     for (int c0 = 0; c0 < BN; c0 += 32) {
       float dm[32], dc[32];
@@ -393,7 +453,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const TcArgs a) {
       }
     }
     if constexpr (EPI == kTcArgmax) {
-      __syncthreads();
+      asm volatile("bar.sync 1, %0;" ::"r"(kTcThreads) : "memory");
       for (int j = tid; j < BN; j += kTcThreads) {
         const int b = b0 + j;
         if (b >= a.B) continue;
@@ -410,6 +470,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_gemm_tc(const TcArgs a) {
       }
     }
   }
+  if (tid == 0 && failed && a.err) atomicOr(a.err, kTcErrTimeout);
   tc_fence_before();
   __syncthreads();
   if (warp == 0)
