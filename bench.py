@@ -41,6 +41,9 @@ WORKLOAD = ("batch-1 greedy decode, Qwen3-0.6B shape (28 layers, hidden 1024, 16
             "8-token prompt + 24 generated, seed 2")
 METRIC, UNIT = "decode tok/s", "tok/s"
 B64, B64_CTX, B64_SEED = 64, 2048, 3
+PF_PROMPTS, PF_LEN, PF_NEW, PF_SEED = 32, 512, 16, 4
+WORKLOAD_PF = ("prefill, Qwen3-0.6B shape: 32 prompts x 512 random ids (seed 4) as tcgen05 dequant-GEMMs over all "
+               "prompt rows with causal GQA attention (mma.sync), then 16 greedy decode tokens per prompt")
 WORKLOAD_B64 = ("batched greedy decode, Qwen3-0.6B shape, 64 independent sequences per GPU, each over a "
                 "2048-position f16 KV context from seeded synthetic hidden states (seed 3), tcgen05 GEMMs")
 
@@ -77,6 +80,16 @@ def batch_step_bytes(shape: synth.Shape, positions) -> int:
     weights = shape.layers * per_layer + H * 2 + shape.vocab * H * 2
     kv = sum(shape.layers * kv_row * (p + 2) for p in positions)
     return weights + kv + len(positions) * H * 2
+
+
+def prefill_flops(shape: synth.Shape, prompts: int, n: int) -> float:
+    """Algorithmic FLOPs of a prefill: 2 * rows * (q4 projection weights) + causal QK^T and P*V."""
+    H, I = shape.hidden, shape.intermediate
+    QS, KV = shape.heads * shape.head_dim, shape.kv_heads * shape.head_dim
+    params = H * (QS + 2 * KV) + QS * H + 2 * H * I + I * H
+    linear = 2.0 * prompts * n * params * shape.layers
+    attn = shape.layers * prompts * shape.heads * 4.0 * shape.head_dim * (n * (n + 1) / 2)
+    return linear + attn
 
 
 def peaks():
@@ -488,6 +501,99 @@ def run_b64(args, world, rank, local):
     return 0
 
 
+def run_prefill(args, world, rank, local):
+    """Config 4: 32 prompts x 512 ids prefilled together (split over the ranks), then 16 tokens."""
+    import torch
+
+    from kernel_optimization_webgpu_b200 import runtime as R
+    torch.cuda.set_device(local)
+    rt = prepare_runtime(world, rank)
+    _, peak_kind = peaks()
+    tflops_peak = _bf16_peak()
+    shape = synth.QWEN3_0_6B
+    if PF_PROMPTS % world:
+        raise SystemExit("32 prompts must split evenly over the ranks")
+    mine = PF_PROMPTS // world
+    rng = np.random.Generator(np.random.PCG64(PF_SEED))
+    all_ids = rng.integers(0, shape.vocab, size=(PF_PROMPTS, PF_LEN)).astype(np.int32)
+    ids = np.ascontiguousarray(all_ids[rank * mine:(rank + 1) * mine])
+    eng = R.Engine(rt, device=local, max_seq=64)
+    stream = torch.cuda.Stream()
+    eng.set_stream(stream)
+    bt = R.Batch(eng, mine, PF_LEN + PF_NEW)
+    warm = max(args.warmup, 3)
+    for _ in range(warm):
+        bt.prefill(ids)
+    barrier(world)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        with torch.cuda.stream(stream):
+            torch.cuda._sleep(20_000_000)
+        e0.record(stream)
+        for _ in range(args.steps):
+            first = bt.prefill(ids)
+        e1.record(stream)
+        e1.synchronize()
+    barrier(world)
+    t_local = e0.elapsed_time(e1) / 1000.0 / args.steps
+    t_max = max_over_ranks(t_local, world)
+    value = PF_PROMPTS * PF_LEN / t_max
+    flops_local = prefill_flops(shape, mine, PF_LEN)
+    achieved = flops_local / t_local / 1e12
+    # decode tail: 15 more greedy tokens after the prefilled first one
+    d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    d0.record(stream)
+    more = bt.decode(PF_NEW - 1)
+    d1.record(stream)
+    d1.synchronize()
+    tail_s = max_over_ranks(d0.elapsed_time(d1) / 1000.0, world)
+    # e2e: host prompt ids in, first ids out, through qd_batch_prefill
+    barrier(world)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        bt.prefill(ids)
+    t_e2e = max_over_ranks((time.perf_counter() - t0) / args.steps, world)
+    bt.close()
+    eng.close()
+    if rank == 0:
+        line = {
+            "metric": "prefill tok/s", "value": round(value, 1), "unit": "tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": warm, "ms_per_step": round(t_max * 1000.0, 4), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32 (f16 hi/lo tensor-core operands)",
+            "data": "synthetic (seeded random-init weights and prompt ids, reference runtime layout)",
+            "config": {"workload": WORKLOAD_PF, "global_batch": PF_PROMPTS, "seq_len": PF_LEN,
+                       "parallelism": f"prompts sharded: {mine} per GPU x {world} (no collective)",
+                       "l2": "inputs larger than L2 (16384 prompt rows, 248 MB of q4 weights per pass)",
+                       "decode_tail": {"tokens_per_prompt": PF_NEW, "ms": round(tail_s * 1000, 3),
+                                       "tok_s": round(PF_PROMPTS * (PF_NEW - 1) / tail_s, 1)}},
+            "roofline": {"bound": "tensor", "kernel": "prefill pass (28 layers: 4 q4 GEMMs, causal attention, "
+                                                      "fused norms) + LM head",
+                         "achieved": round(achieved, 1), "peak": tflops_peak, "unit": "TFLOP/s",
+                         "frac": round(achieved / tflops_peak, 4), "traffic": None,
+                         "flops_per_step": flops_local, "peak_source": peak_kind,
+                         "note": "algorithmic FLOPs; the GEMMs run 3 f16 MMAs per k-step (hi/lo splits) to keep "
+                                 "f32 accuracy, so tensor-pipe work is about 1.5x this"},
+            "e2e": {"value": round(PF_PROMPTS * PF_LEN / t_e2e, 1), "unit": "tok/s",
+                    "h2d_bytes_per_step": mine * PF_LEN * 4, "d2h_bytes_per_step": mine * 4,
+                    "step": "one qd_batch_prefill call: the prompts' ids in, each prompt's first id out"},
+            "gpu_launches": args.steps * (shape.layers * 9 + 3),
+            "clocks": clk.summary(),
+            "generated_ids_sample": [int(first[0])] + more[:3, 0].tolist(),
+        }
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+def _bf16_peak() -> float:
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            return float(json.load(f)["bf16_tflops"])
+    return 1590.0
+
+
 def time_cpu_batched(rt, bt, steps=3):
     """Oracle decode of one sequence of the batched workload (its 2048 cached rows
     copied from the GPU context) on the host cores."""
@@ -517,21 +623,23 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-steps", type=int, default=24)
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--workload", default="b1", choices=["b1", "b64"])
+    ap.add_argument("--workload", default="b1", choices=["b1", "b64", "prefill"])
     ap.add_argument("--batch", type=int, default=B64, help="b64 workload: sequences per GPU (profiling cases)")
     ap.add_argument("--decode-only", action="store_true",
                     help="prefill + warm-up + timed decode steps only (for profiler launch lists)")
     args = ap.parse_args()
     if args.steps is None:
-        args.steps = 128 if args.workload == "b64" else 480
+        args.steps = {"b64": 128, "prefill": 10}.get(args.workload, 480)
     if args.warmup is None:
-        args.warmup = 3 if args.workload == "b64" else 24
+        args.warmup = 24 if args.workload == "b1" else 3
     world, rank, local = dist_setup()
     try:
         if args.impl == "reference":
             rc = run_reference(args, world, rank)
         elif args.workload == "b64":
             rc = run_b64(args, world, rank, local)
+        elif args.workload == "prefill":
+            rc = run_prefill(args, world, rank, local)
         else:
             rc = run_ours(args, world, rank, local)
     finally:

@@ -61,7 +61,10 @@ int bfail(qd_batch* b, const QdError& err) {
   return err.code;
 }
 
-unsigned long long g_attn_smem_mask = 0, g_attn_smem_mask2 = 0;
+unsigned long long g_attn_smem_mask = 0, g_attn_smem_mask2 = 0, g_pf_smem_mask = 0, g_pf_smem_mask2 = 0;
+
+// Dynamic shared memory of kb_prefill_attn<G>: two K/V stages + the Q tile (hi/lo) + alignment.
+size_t pf_smem(int G) { return (size_t)2 * kBAttnStage + (size_t)G * 4 * kPfQBytes + 1024; }
 
 struct Dims {
   int L, H, I, NH, NKV, QS, KVS, R, V, G;
@@ -436,6 +439,74 @@ void decode(qd_batch* b, int steps, int32_t* out_ids) {
   for (int i = 0; i < B; ++i) b->host_pos[i] += steps;
 }
 
+// ---- prefill ------------------------------------------------------------------------
+// All prompts at once: B * n rows through every layer (GEMMs over the rows,
+// causal attention inside each prompt), then the LM head on each prompt's last
+// row; each sequence's first generated id becomes its next input at position n.
+void prefill(qd_batch* b, const int32_t* ids, int n, int32_t* first_ids) {
+  qd_engine* e = b->e;
+  const Dims d = dims(e);
+  cudaStream_t s = e->stream;
+  const int B = b->B;
+  const long long T = (long long)B * n;
+  if (T > (1ll << 31) / std::max(d.R, 2 * d.I)) throw QdError{QD_E_RANGE, "prefill: batch * n_prompt too large"};
+  ensure_wide(b, T);
+  QD_CK(cudaMemcpyAsync(b->w_tok, ids, (size_t)T * 4, cudaMemcpyHostToDevice, s));
+  const float scale = 1.0f / std::sqrt((float)kHeadDim);
+  const long long layer_rows = (long long)B * d.NKV * b->max_seq;
+  const int qtiles = (n + kPfTile - 1) / kPfTile;
+  const int rope_grid = (int)std::min<long long>((T * (d.NH + 2 * d.NKV) + 7) / 8, 1 << 20);
+  const int silu_grid = (int)std::min<long long>((T * d.I + 255) / 256, 1 << 20);
+  for (int l = 0; l < d.L; ++l) {
+    const LayerDev& L = e->layers[l];
+    if (l == 0)
+      launch_ex(kb_resid_norm, dim3((unsigned)T), dim3(kNormThreads), 0, s, b->w_h, (const float*)nullptr, 0, 0LL,
+                (const __half*)e->embed, (const int*)b->w_tok, d.V, L.n_in, d.H, d.eps, b->w_xh, b->w_xl, b->errw);
+    else
+      launch_ex(kb_resid_norm, dim3((unsigned)T), dim3(kNormThreads), 0, s, b->w_h, (const float*)b->w_y, 1, 0LL,
+                (const __half*)nullptr, (const int*)nullptr, d.V, L.n_in, d.H, d.eps, b->w_xh, b->w_xl, b->errw);
+    gemm_q4(L.qkv, d.H, d.R, b->w_xh, b->w_xl, (int)T, 1, d.H / kTcK, b->w_y, s, b->errw);
+    launch(kb_rope_cache, dim3(rope_grid), s, (const float*)b->w_y, 1, 0LL, (int)T, d.NH, d.NKV, L.n_q, L.n_k, d.eps,
+           (const float*)e->cos_t, (const float*)e->sin_t, e->opt.rope_row_stride, (const int*)nullptr, n, 0LL,
+           b->max_seq, kc_of(b, l), vc_of(b, l), b->w_q, b->errw);
+    const long long k_row0 = (long long)l * layer_rows, v_row0 = (long long)(d.L + l) * layer_rows;
+    const dim3 agrid(d.NKV, qtiles, B);
+    if (d.G == 1) {
+      allow_smem(kb_prefill_attn<1>, pf_smem(1), g_pf_smem_mask);
+      launch_ex(kb_prefill_attn<1>, agrid, dim3(128), pf_smem(1), s, b->kvmap, k_row0, v_row0, (const float*)b->w_q, n,
+                d.NH, d.NKV, b->max_seq, scale, b->w_xh, b->w_xl, b->errw);
+    } else {
+      allow_smem(kb_prefill_attn<2>, pf_smem(2), g_pf_smem_mask2);
+      launch_ex(kb_prefill_attn<2>, agrid, dim3(256), pf_smem(2), s, b->kvmap, k_row0, v_row0, (const float*)b->w_q, n,
+                d.NH, d.NKV, b->max_seq, scale, b->w_xh, b->w_xl, b->errw);
+    }
+    gemm_q4(L.o, d.QS, d.H, b->w_xh, b->w_xl, (int)T, 1, d.QS / kTcK, b->w_y, s, b->errw);
+    launch_ex(kb_resid_norm, dim3((unsigned)T), dim3(kNormThreads), 0, s, b->w_h, (const float*)b->w_y, 1, 0LL,
+              (const __half*)nullptr, (const int*)nullptr, d.V, L.n_post, d.H, d.eps, b->w_xh, b->w_xl, b->errw);
+    gemm_q4(L.gu, d.H, 2 * d.I, b->w_xh, b->w_xl, (int)T, 1, d.H / kTcK, b->w_y, s, b->errw);
+    launch(kb_silu_split, dim3(silu_grid), s, (const float*)b->w_y, 1, 0LL, (int)T, d.I, b->w_xh, b->w_xl);
+    gemm_q4(L.d, d.I, d.H, b->w_xh, b->w_xl, (int)T, 1, d.I / kTcK, b->w_y, s, b->errw);
+  }
+  launch_ex(kb_resid_norm, dim3((unsigned)T), dim3(kNormThreads), 0, s, b->w_h, (const float*)b->w_y, 1, 0LL,
+            (const __half*)nullptr, (const int*)nullptr, d.V, (const float*)e->final_norm, d.H, d.eps, b->w_xh,
+            b->w_xl, b->errw);
+  // LM head on each prompt's last row; the merge feeds the id back and moves the position to n.
+  lm_head(b, b->w_xh + (size_t)(n - 1) * d.H, b->w_xl + (size_t)(n - 1) * d.H, (long long)n * d.H, B,
+          b->keep_logits ? b->logits : nullptr, s);
+  std::vector<int32_t> p(B, n - 1);
+  std::memcpy(b->pinned_io + 16 + B, p.data(), (size_t)B * 4);
+  QD_CK(cudaMemcpyAsync(b->pos, b->pinned_io + 16 + B, (size_t)B * 4, cudaMemcpyHostToDevice, s));
+  QD_CK(cudaMemsetAsync(b->step, 0, 4, s));
+  BatchState st{b->tokens, b->pos, b->out, b->step, b->max_steps};
+  launch(kb_argmax_merge, dim3((B + 7) / 8), s, (const float*)b->lm_pv, (const uint32_t*)b->lm_pi, b->lm_tiles, B, st,
+         b->result);
+  if (first_ids) QD_CK(cudaMemcpyAsync(b->pinned, b->out, (size_t)B * 4, cudaMemcpyDeviceToHost, s));
+  QD_CK(cudaStreamSynchronize(s));
+  check_err(b);
+  if (first_ids) std::memcpy(first_ids, b->pinned, (size_t)B * 4);
+  b->host_pos.assign(B, n);
+}
+
 }  // namespace
 
 extern "C" {
@@ -607,21 +678,38 @@ int qd_batch_write_kv(qd_batch* b, int layer, int seq, int pos0, int count, cons
 int qd_batch_step_kernels(const qd_batch* b) { return b ? step_kernel_count(b) : 0; }
 
 int qd_batch_prefill(qd_batch* b, const int32_t* ids, int n_prompt, int32_t* first_ids) {
-  (void)ids;
-  (void)n_prompt;
-  (void)first_ids;
-  return bfail(b, QdError{QD_E_INVALID, "batched prefill is not available in this build"});
+  if (!b || !ids) return bfail(b, QdError{QD_E_INVALID, "NULL argument"});
+  try {
+    if (n_prompt < 1 || n_prompt > b->max_seq) throw QdError{QD_E_RANGE, "n_prompt must be 1..max_seq"};
+    const long long T = (long long)b->B * n_prompt;
+    for (long long i = 0; i < T; ++i)
+      if (ids[i] < 0 || ids[i] >= b->e->p.vocab) throw QdError{QD_E_RANGE, "token id outside the vocabulary"};
+    QD_CK(cudaSetDevice(b->e->dev));
+    prefill(b, ids, n_prompt, first_ids);
+  } catch (const QdError& err) {
+    return bfail(b, err);
+  }
+  return QD_OK;
 }
 
 int qd_generate_batch(qd_engine* e, int batch, const int32_t* ids, int n_prompt, int max_new_tokens,
                       int32_t* out_ids) {
-  (void)e;
-  (void)batch;
-  (void)ids;
-  (void)n_prompt;
-  (void)max_new_tokens;
-  (void)out_ids;
-  return bfail(nullptr, QdError{QD_E_INVALID, "batched prefill is not available in this build"});
+  if (!e || !ids || !out_ids) return bfail(nullptr, QdError{QD_E_INVALID, "NULL argument"});
+  if (max_new_tokens < 1 || n_prompt < 1) return bfail(nullptr, QdError{QD_E_INVALID, "n_prompt and max_new_tokens must be >= 1"});
+  qd_batch* b = nullptr;
+  int rc = qd_batch_create(e, batch, n_prompt + max_new_tokens, &b);
+  if (rc) return rc;
+  std::vector<int32_t> first(batch), rest((size_t)batch * (max_new_tokens - 1));
+  rc = qd_batch_prefill(b, ids, n_prompt, first.data());
+  if (!rc && max_new_tokens > 1) rc = qd_batch_decode(b, max_new_tokens - 1, rest.data());
+  if (!rc)
+    for (int i = 0; i < batch; ++i) {
+      out_ids[(size_t)i * max_new_tokens] = first[i];
+      for (int t = 1; t < max_new_tokens; ++t)
+        out_ids[(size_t)i * max_new_tokens + t] = rest[(size_t)(t - 1) * batch + i];
+    }
+  qd_batch_destroy(b);
+  return rc;
 }
 
 }  // extern "C"

@@ -558,4 +558,264 @@ static __global__ void __launch_bounds__(256) kb_ctx_hidden(uint32_t seed, uint3
   }
 }
 
+// ---- causal prefill attention (tensor cores) ------------------------------------------
+// Grid (NKV, ceil(n / 64), B); 128 * G threads. CTA = one 64-position query tile
+// of prompt b and the G query heads of KV head g; warp w takes head w / 4 and
+// positions 16 (w % 4) .. + 15 of the tile. Key/value tiles (64 positions) come
+// from the cache by TMA (same tensor map and 128-byte swizzle as decode),
+// double-buffered; tiles 0 .. qt are visited, the diagonal one masked.
+//
+// Math on mma.sync m16n8k16 (f16 in, f32 accumulate): S = Q K^T with Q split
+// into f16 hi + lo parts (K is exact in f16), online softmax per row in
+// registers, O += P V with P split the same way (V exact). ldmatrix reads the
+// swizzled tiles conflict-free. The output rows (O / l) are written as the hi/lo
+// operands of the o GEMM: x_hi/x_lo [T][NH*128], T = B * n.
+constexpr int kPfTile = 64;
+constexpr int kPfQBytes = kPfTile * 64 * 2;  // one 64-position x 64-dim f16 half of a head's Q tile
+
+__device__ __forceinline__ void ldsm_x4(unsigned addr, unsigned& r0, unsigned& r1, unsigned& r2, unsigned& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(unsigned addr, unsigned& r0, unsigned& r1, unsigned& r2, unsigned& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void mma16816(float (&d)[4], unsigned a0, unsigned a1, unsigned a2, unsigned a3, unsigned b0,
+                                         unsigned b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ unsigned pack_h2(float lo_elem, float hi_elem) {
+  const __half2 h = __floats2half2_rn(lo_elem, hi_elem);
+  return *reinterpret_cast<const unsigned*>(&h);
+}
+// f16 hi/lo split of a pair: hi = f16(x), lo = f16(x - hi) (unscaled).
+__device__ __forceinline__ void split_pair(float x0, float x1, unsigned& hi, unsigned& lo) {
+  const __half2 h = __floats2half2_rn(x0, x1);
+  const float2 hf = __half22float2(h);
+  hi = *reinterpret_cast<const unsigned*>(&h);
+  lo = pack_h2(x0 - hf.x, x1 - hf.y);
+}
+// Byte offset of (row r, 16-byte chunk c of the 64-dim half) in a 128-byte-swizzled box.
+__device__ __forceinline__ unsigned swz(int r, int c) { return (unsigned)(r * 128 + (((c ^ r) & 7) << 4)); }
+
+template <int G>
+__global__ void __launch_bounds__(128 * G) kb_prefill_attn(const __grid_constant__ CUtensorMap kvmap, long long k_row0,
+                                                           long long v_row0, const float* q, int n, int NH, int NKV,
+                                                           int max_seq, float scale, __half* x_hi, __half* x_lo,
+                                                           int* err) {
+  extern __shared__ unsigned char pf_raw[];
+  unsigned char* base =
+      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(pf_raw) + 1023) & ~uintptr_t(1023));
+  unsigned char* kv = base;                          // [2 stages][K0 K1 V0 V1] boxes of 8 KB
+  unsigned char* qs = base + 2 * kBAttnStage;        // [G][hi|lo][2 halves] boxes of 8 KB
+  __shared__ unsigned long long full[2];
+  const int g = blockIdx.x, b = blockIdx.z;
+  const int qt = (int)gridDim.y - 1 - (int)blockIdx.y;  // longest tiles first
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int h = warp >> 2, wq = warp & 3;  // head within the group, 16-row slice of the tile
+  const int QS = NH * kHeadDim;
+  if (tid == 0) {
+    tc_mbar_init(&full[0]);
+    tc_mbar_init(&full[1]);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    tma_prefetch_map(&kvmap);
+  }
+  pdl_wait();
+  const long long seq_row = ((long long)b * NKV + g) * max_seq;
+  const int nkt = qt + 1;
+  auto issue = [&](int t) {
+    const long long row = seq_row + (long long)t * kPfTile;
+    unsigned char* st = kv + (t & 1) * kBAttnStage;
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(tc_smem(&full[t & 1])),
+                 "r"(kBAttnStage)
+                 : "memory");
+    tma_load_2d(st, &kvmap, 0, (int)(k_row0 + row), &full[t & 1]);
+    tma_load_2d(st + kBAttnBox, &kvmap, 64, (int)(k_row0 + row), &full[t & 1]);
+    tma_load_2d(st + 2 * kBAttnBox, &kvmap, 0, (int)(v_row0 + row), &full[t & 1]);
+    tma_load_2d(st + 3 * kBAttnBox, &kvmap, 64, (int)(v_row0 + row), &full[t & 1]);
+  };
+  __syncthreads();
+  if (tid == 0) {
+    issue(0);
+    if (nkt > 1) issue(1);
+  }
+  // Q tile -> f16 hi/lo, swizzled like the K boxes. Rows beyond n are zero.
+  for (int e = tid; e < G * kPfTile * 32; e += 128 * G) {  // 4 dims per item
+    const int hh = e / (kPfTile * 32), r = (e / 32) % kPfTile, d4 = e % 32;
+    const int p = qt * kPfTile + r;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (p < n)
+      v = *reinterpret_cast<const float4*>(q + ((long long)b * n + p) * QS + ((long long)g * G + hh) * kHeadDim + 4 * d4);
+    unsigned h01, l01, h23, l23;
+    split_pair(v.x, v.y, h01, l01);
+    split_pair(v.z, v.w, h23, l23);
+    const int dim = 4 * d4, half = dim >> 6, c = (dim & 63) >> 3;
+    const unsigned off = swz(r, c) + (dim & 7) * 2;
+    unsigned char* qh = qs + ((hh * 2 + 0) * 2 + half) * kPfQBytes;
+    unsigned char* ql = qs + ((hh * 2 + 1) * 2 + half) * kPfQBytes;
+    *reinterpret_cast<uint2*>(qh + off) = make_uint2(h01, h23);
+    *reinterpret_cast<uint2*>(ql + off) = make_uint2(l01, l23);
+  }
+  __syncthreads();
+
+  const int r0 = wq * 16;           // first tile row of this warp
+  const int ra = r0 + (lane >> 2);  // accumulator rows ra and ra + 8
+  const int qa = qt * kPfTile + ra, qb = qa + 8;
+  float o[16][4];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.0f;
+  float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.0f, l_b = 0.0f;
+  const unsigned qh_base = tc_smem(qs + (h * 2 + 0) * 2 * kPfQBytes);
+  const unsigned ql_base = tc_smem(qs + (h * 2 + 1) * 2 * kPfQBytes);
+  bool ok = true;
+  int consumed = 0;
+  for (int t = 0; t < nkt; ++t) {
+    const int buf = t & 1;
+    ok = tc_mbar_wait(&full[buf], (unsigned)(t >> 1) & 1u);
+    if (__syncthreads_or(!ok)) {
+      ok = false;
+      break;
+    }
+    consumed = t + 1;
+    const unsigned kb = tc_smem(kv + buf * kBAttnStage);
+    const unsigned vb = kb + 2 * kBAttnBox;
+    // S = Q K^T for 16 rows x 64 keys
+    float s[8][4];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.0f;
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk) {  // 16 dims per step
+      // A: rows r0.., matrices (rows +0/+8) x (dims +0/+8)
+      const int mi = lane >> 3, rr = r0 + (lane & 7) + 8 * (mi & 1), ch = 2 * kk + (mi >> 1);
+      const unsigned aoff = (unsigned)((ch >> 3) * kPfQBytes) + swz(rr, ch & 7);
+      unsigned ah0, ah1, ah2, ah3, al0, al1, al2, al3;
+      ldsm_x4(qh_base + aoff, ah0, ah1, ah2, ah3);
+      ldsm_x4(ql_base + aoff, al0, al1, al2, al3);
+#pragma unroll
+      for (int j = 0; j < 8; j += 2) {  // two n-tiles of 8 keys per ldmatrix.x4
+        const int key = 8 * (j + (mi >> 1)) + (lane & 7), kc = 2 * kk + (mi & 1);
+        unsigned b0, b1, b2, b3;
+        ldsm_x4(kb + (unsigned)((kc >> 3) * kBAttnBox) + swz(key, kc & 7), b0, b1, b2, b3);
+        mma16816(s[j], ah0, ah1, ah2, ah3, b0, b1);
+        mma16816(s[j], al0, al1, al2, al3, b0, b1);
+        mma16816(s[j + 1], ah0, ah1, ah2, ah3, b2, b3);
+        mma16816(s[j + 1], al0, al1, al2, al3, b2, b3);
+      }
+    }
+    // scale, causal mask, online softmax (rows qa, qb; each quad holds one row pair)
+    float mt_a = -INFINITY, mt_b = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int key = t * kPfTile + 8 * j + 2 * (lane & 3) + e;
+        s[j][e] = (key <= qa && key < n) ? s[j][e] * scale : -INFINITY;
+        s[j][2 + e] = (key <= qb && key < n) ? s[j][2 + e] * scale : -INFINITY;
+        mt_a = fmaxf(mt_a, s[j][e]);
+        mt_b = fmaxf(mt_b, s[j][2 + e]);
+      }
+    }
+    mt_a = fmaxf(mt_a, __shfl_xor_sync(0xffffffffu, mt_a, 1));
+    mt_a = fmaxf(mt_a, __shfl_xor_sync(0xffffffffu, mt_a, 2));
+    mt_b = fmaxf(mt_b, __shfl_xor_sync(0xffffffffu, mt_b, 1));
+    mt_b = fmaxf(mt_b, __shfl_xor_sync(0xffffffffu, mt_b, 2));
+    const float mn_a = fmaxf(m_a, mt_a), mn_b = fmaxf(m_b, mt_b);
+    const float fa = (m_a == -INFINITY || mn_a == -INFINITY) ? (mn_a == -INFINITY ? 1.0f : 0.0f) : expf(m_a - mn_a);
+    const float fb = (m_b == -INFINITY || mn_b == -INFINITY) ? (mn_b == -INFINITY ? 1.0f : 0.0f) : expf(m_b - mn_b);
+    float ps_a = 0.0f, ps_b = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        s[j][e] = s[j][e] == -INFINITY ? 0.0f : expf(s[j][e] - mn_a);
+        s[j][2 + e] = s[j][2 + e] == -INFINITY ? 0.0f : expf(s[j][2 + e] - mn_b);
+        ps_a += s[j][e];
+        ps_b += s[j][2 + e];
+      }
+    }
+    ps_a += __shfl_xor_sync(0xffffffffu, ps_a, 1);
+    ps_a += __shfl_xor_sync(0xffffffffu, ps_a, 2);
+    ps_b += __shfl_xor_sync(0xffffffffu, ps_b, 1);
+    ps_b += __shfl_xor_sync(0xffffffffu, ps_b, 2);
+    l_a = l_a * fa + ps_a;
+    l_b = l_b * fb + ps_b;
+    m_a = mn_a;
+    m_b = mn_b;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      o[i][0] *= fa;
+      o[i][1] *= fa;
+      o[i][2] *= fb;
+      o[i][3] *= fb;
+    }
+    // O += P V: P from the S accumulators (hi + lo f16), V by transposed ldmatrix
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) {  // 16 keys per step
+      unsigned ph[4], plo[4];
+      split_pair(s[2 * ks][0], s[2 * ks][1], ph[0], plo[0]);
+      split_pair(s[2 * ks][2], s[2 * ks][3], ph[1], plo[1]);
+      split_pair(s[2 * ks + 1][0], s[2 * ks + 1][1], ph[2], plo[2]);
+      split_pair(s[2 * ks + 1][2], s[2 * ks + 1][3], ph[3], plo[3]);
+      const int mi = lane >> 3;
+      const int key = 16 * ks + (lane & 7) + 8 * (mi & 1);
+#pragma unroll
+      for (int dn = 0; dn < 16; dn += 2) {  // two 8-dim n-tiles per ldmatrix.x4
+        const int vc = dn + (mi >> 1);       // 8-dim chunk of the row (0..15)
+        unsigned b0, b1, b2, b3;
+        ldsm_x4_t(vb + (unsigned)((vc >> 3) * kBAttnBox) + swz(key, vc & 7), b0, b1, b2, b3);
+        mma16816(o[dn], ph[0], ph[1], ph[2], ph[3], b0, b1);
+        mma16816(o[dn], plo[0], plo[1], plo[2], plo[3], b0, b1);
+        mma16816(o[dn + 1], ph[0], ph[1], ph[2], ph[3], b2, b3);
+        mma16816(o[dn + 1], plo[0], plo[1], plo[2], plo[3], b2, b3);
+      }
+    }
+    __syncthreads();  // stage consumed
+    if (tid == 0 && t + 2 < nkt) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      issue(t + 2);
+    }
+  }
+  if (!ok) {
+    if (tid == 0) {
+      for (int t = consumed; t < min(nkt, consumed + 2); ++t) (void)tc_mbar_wait(&full[t & 1], (unsigned)(t >> 1) & 1u);
+      atomicOr(err, kBErrTimeout);
+    }
+    pdl_trigger();
+    return;
+  }
+  pdl_trigger();
+  const float ia = 1.0f / l_a, ib = 1.0f / l_b;
+  const int col0 = (g * G + h) * kHeadDim + 2 * (lane & 3);
+#pragma unroll
+  for (int dn = 0; dn < 16; ++dn) {
+    const int col = col0 + 8 * dn;
+    if (qa < n) {
+      unsigned hi, lo;
+      const float x0 = o[dn][0] * ia, x1 = o[dn][1] * ia;
+      const __half2 hh = __floats2half2_rn(x0, x1);
+      const float2 hf = __half22float2(hh);
+      hi = *reinterpret_cast<const unsigned*>(&hh);
+      lo = pack_h2((x0 - hf.x) * kLoScale, (x1 - hf.y) * kLoScale);
+      *reinterpret_cast<unsigned*>(x_hi + ((long long)b * n + qa) * QS + col) = hi;
+      *reinterpret_cast<unsigned*>(x_lo + ((long long)b * n + qa) * QS + col) = lo;
+    }
+    if (qb < n) {
+      unsigned hi, lo;
+      const float x0 = o[dn][2] * ib, x1 = o[dn][3] * ib;
+      const __half2 hh = __floats2half2_rn(x0, x1);
+      const float2 hf = __half22float2(hh);
+      hi = *reinterpret_cast<const unsigned*>(&hh);
+      lo = pack_h2((x0 - hf.x) * kLoScale, (x1 - hf.y) * kLoScale);
+      *reinterpret_cast<unsigned*>(x_hi + ((long long)b * n + qb) * QS + col) = hi;
+      *reinterpret_cast<unsigned*>(x_lo + ((long long)b * n + qb) * QS + col) = lo;
+    }
+  }
+}
+
 }  // namespace qd

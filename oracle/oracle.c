@@ -447,6 +447,12 @@ void qo_session_free(qo_session* s) {
 
 void qo_session_set_trace(qo_session* s, float* trace) { s->trace = trace; }
 
+/* The session's K (which = 0) or V (which = 1) cache of a layer: [max_seq][kv_heads * head_dim]. */
+const float* qo_session_kv(const qo_session* s, int layer, int which) {
+  if (layer < 0 || layer >= s->m->layers) return 0;
+  return which ? s->v_cache[layer] : s->k_cache[layer];
+}
+
 /* Cache rows set from outside (a context built elsewhere): rows are stored as
  * given, in the [pos][kv_head * head_dim] layout cache_write.wgsl:12-18 writes. */
 int qo_session_set_kv(qo_session* s, int layer, int pos0, int count, const float* k, const float* v) {

@@ -67,6 +67,8 @@ qo_session* qo_session_new(const qo_model* m, int max_seq, int kv_f16, int rope_
 void qo_session_free(qo_session* s);
 /* Optional per-layer dump of the hidden state after each layer: [layers][hidden]. */
 void qo_session_set_trace(qo_session* s, float* trace);
+/* The session's K (which = 0) or V (which = 1) cache of a layer: [max_seq][kv_heads * head_dim]. */
+const float* qo_session_kv(const qo_session* s, int layer, int which);
 /* Overwrite cached K/V rows [pos0, pos0 + count) of a layer: [count][kv_heads * head_dim]. */
 int qo_session_set_kv(qo_session* s, int layer, int pos0, int count, const float* k, const float* v);
 /* One token through all layers plus the final norm (enqueueAutoregressiveToken). */

@@ -56,6 +56,7 @@ def lib():
         L.qo_session_new.argtypes = [vp, i32, i32, i32]; L.qo_session_new.restype = vp
         L.qo_session_free.argtypes = [vp]
         L.qo_session_set_trace.argtypes = [vp, vp]
+        L.qo_session_kv.argtypes = [vp, i32, i32]; L.qo_session_kv.restype = C.POINTER(f32)
         L.qo_session_set_kv.argtypes = [vp, i32, i32, i32, _f32p, _f32p]; L.qo_session_set_kv.restype = i32
         L.qo_forward.argtypes = [vp, i32, i32]; L.qo_forward.restype = i32
         L.qo_session_final_hidden.argtypes = [vp]; L.qo_session_final_hidden.restype = C.POINTER(f32)
@@ -196,12 +197,23 @@ class Model:
 class Session:
     def __init__(self, model: Model, max_seq: int, kv_f16: bool, rope_row_stride: int):
         self.model = model
+        self.max_seq = max_seq
         self._h = lib().qo_session_new(model._h, max_seq, int(kv_f16), rope_row_stride)
 
     def __del__(self):
         if getattr(self, "_h", None):
             lib().qo_session_free(self._h)
             self._h = None
+
+    def kv(self, layer: int, pos0: int, count: int):
+        """Cached K and V rows [pos0, pos0 + count) of `layer` (copies)."""
+        kvs = self.model.kv_heads * self.model.head_dim
+        out = []
+        for which in (0, 1):
+            p = lib().qo_session_kv(self._h, layer, which)
+            a = np.ctypeslib.as_array(p, shape=(self.max_seq, kvs))
+            out.append(a[pos0:pos0 + count].copy())
+        return out[0], out[1]
 
     def set_kv(self, layer: int, pos0: int, k, v) -> None:
         """Cached K/V rows [pos0, pos0 + len(k)) of `layer` ([n][kv_heads * head_dim] f32)."""

@@ -195,3 +195,80 @@ def test_batch_qwen_shape_config3(qwen_runtime):
             wk, wv = oracle_kv_row(model, 3, layer, 17 * ctx + pos, pos)
             assert np.allclose(gk[0], wk, rtol=2.0 ** -10, atol=1e-4)
             assert np.allclose(gv[0], wv, rtol=2.0 ** -10, atol=1e-4)
+
+
+# ---- prefill (config 4 flow) -------------------------------------------------------
+
+def _oracle_greedy(model, prompt, max_new, max_seq):
+    sess = model.session(max_seq=max_seq, kv_f16=True)
+    ids, margins = sess.greedy(prompt, max_new)
+    return ids, margins, sess
+
+
+@pytest.mark.parametrize("n", [1, 64, 70, 130])
+def test_prefill_then_decode_matches_oracle(tiny, n):
+    """Prompts of n ids (a single id, exactly one tile, ragged tiles) prefilled as one
+    GEMM pass with causal attention, then 4 decode steps."""
+    eng, model = tiny
+    B, steps = 3, 4
+    rng = np.random.Generator(np.random.PCG64(4))
+    ids = rng.integers(0, model.vocab, size=(B, n)).astype(np.int32)
+    with R.Batch(eng, B, n + steps + 2) as bt:
+        first = bt.prefill(ids)
+        assert bt.positions().tolist() == [n] * B
+        more = bt.decode(steps)
+        for s in range(B):
+            want, margins, sess = _oracle_greedy(model, ids[s].tolist(), steps + 1, n + steps + 2)
+            got = [int(first[s])] + more[:, s].tolist()
+            assert got == want, (s, got, want, margins)
+        # the prompt's cached rows against the oracle's (f16 rounding of nearby values)
+        sess = model.session(max_seq=n + 1, kv_f16=True)
+        for i, t in enumerate(ids[1].tolist()):
+            sess.forward(t, i)
+        for layer in range(len(model.layers)):
+            gk, gv = bt.read_kv(layer, 1, 0, n)
+            wk, wv = sess.kv(layer, 0, n)
+            assert np.allclose(gk, wk, rtol=2.0 ** -9, atol=1e-3), layer
+            assert np.allclose(gv, wv, rtol=2.0 ** -9, atol=1e-3), layer
+
+
+def test_generate_batch_wrapper(tiny):
+    eng, model = tiny
+    rng = np.random.Generator(np.random.PCG64(5))
+    ids = rng.integers(0, model.vocab, size=(2, 9)).astype(np.int32)
+    out = R.generate_batch(eng, ids, 5)
+    assert out.shape == (2, 5)
+    for s in range(2):
+        want, _, _ = _oracle_greedy(model, ids[s].tolist(), 5, 16)
+        assert out[s].tolist() == want
+
+
+def test_prefill_rejects_bad_requests(tiny):
+    eng, model = tiny
+    with R.Batch(eng, 2, 16) as bt:
+        with pytest.raises(R.QdError) as ex:
+            bt.prefill(np.zeros((2, 17), np.int32))        # longer than max_seq
+        assert ex.value.code == -5
+        bad = np.zeros((2, 4), np.int32)
+        bad[1, 2] = model.vocab
+        with pytest.raises(R.QdError) as ex:
+            bt.prefill(bad)                                # id outside the vocabulary
+        assert ex.value.code == -5
+        with pytest.raises(ValueError):
+            bt.prefill(np.zeros((3, 4), np.int32))         # wrong batch
+
+
+def test_prefill_qwen_shape_config4(qwen_runtime):
+    """Config 4 shape: 32 prompts of 512 ids (seed 4), prefill then 16 decode tokens;
+    the last prompt checked end to end against the oracle's sequential greedy."""
+    model = O.Model(qwen_runtime)
+    B, n, steps = 32, 512, 16
+    rng = np.random.Generator(np.random.PCG64(4))
+    ids = rng.integers(0, model.vocab, size=(B, n)).astype(np.int32)
+    with R.Engine(qwen_runtime, max_seq=64) as eng, R.Batch(eng, B, n + steps) as bt:
+        first = bt.prefill(ids)
+        more = bt.decode(steps - 1)
+        for s in (B - 1,):
+            want, margins, _ = _oracle_greedy(model, ids[s].tolist(), steps, n + steps)
+            got = [int(first[s])] + more[:, s].tolist()
+            assert got == want, (s, got, want, margins)
