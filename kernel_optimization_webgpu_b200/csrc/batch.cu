@@ -50,6 +50,7 @@ struct qd_batch {
   long long wide_rows = 0;
   float *w_h = nullptr, *w_y = nullptr, *w_q = nullptr;
   __half *w_xh = nullptr, *w_xl = nullptr;
+  __half *w_ah = nullptr, *w_al = nullptr;  // prefill: silu(gate)*up operands of the down GEMM
   int* w_tok = nullptr;
 };
 
@@ -110,6 +111,22 @@ void gemm_q4(const char* base, int K, int n_rows, const __half* xh, const __half
   a.y_split = (long long)rows * n_rows;
   a.err = err;
   launch_gemm(a, splits, kGemmQ4Store, s);
+}
+
+// gate/up GEMM with silu(gate) * up fused into the epilogue (one split): writes
+// the down GEMM's hi/lo operands [rows][I] directly.
+void gemm_q4_silu(const char* base, int K, int I, const __half* xh, const __half* xl, int rows, __half* out_hi,
+                  __half* out_lo, cudaStream_t s, int* err) {
+  TcArgs a = q4_args(base, K, 2 * I);
+  a.x_hi = xh;
+  a.x_lo = xl;
+  a.B = rows;
+  a.kt_split = K / kTcK;
+  a.ldy = I;
+  a.y_hi = out_hi;
+  a.y_lo = out_lo;
+  a.err = err;
+  launch_gemm(a, 1, kGemmQ4Silu, s);
 }
 
 void lm_head(qd_batch* b, const __half* xh, const __half* xl, long long ldx, int rows, float* logits, cudaStream_t s) {
@@ -236,6 +253,7 @@ void ensure_wide(qd_batch* b, long long rows) {
   };
   const size_t o_h = take(rows * d.H * 4), o_y = take(rows * maxn * 4), o_q = take(rows * d.QS * 4);
   const size_t o_xh = take(rows * maxk * 2), o_xl = take(rows * maxk * 2), o_tok = take(rows * 4);
+  const size_t o_ah = take(rows * d.I * 2), o_al = take(rows * d.I * 2);
   if (cudaMalloc(&b->wide, off) != cudaSuccess) throw QdError{QD_E_NOMEM, "cannot allocate prefill buffers"};
   char* base = static_cast<char*>(b->wide);
   b->w_h = reinterpret_cast<float*>(base + o_h);
@@ -244,6 +262,8 @@ void ensure_wide(qd_batch* b, long long rows) {
   b->w_xh = reinterpret_cast<__half*>(base + o_xh);
   b->w_xl = reinterpret_cast<__half*>(base + o_xl);
   b->w_tok = reinterpret_cast<int*>(base + o_tok);
+  b->w_ah = reinterpret_cast<__half*>(base + o_ah);
+  b->w_al = reinterpret_cast<__half*>(base + o_al);
   b->wide_rows = rows;
 }
 
@@ -456,7 +476,6 @@ void prefill(qd_batch* b, const int32_t* ids, int n, int32_t* first_ids) {
   const long long layer_rows = (long long)B * d.NKV * b->max_seq;
   const int qtiles = (n + kPfTile - 1) / kPfTile;
   const int rope_grid = (int)std::min<long long>((T * (d.NH + 2 * d.NKV) + 7) / 8, 1 << 20);
-  const int silu_grid = (int)std::min<long long>((T * d.I + 255) / 256, 1 << 20);
   for (int l = 0; l < d.L; ++l) {
     const LayerDev& L = e->layers[l];
     if (l == 0)
@@ -483,9 +502,9 @@ void prefill(qd_batch* b, const int32_t* ids, int n, int32_t* first_ids) {
     gemm_q4(L.o, d.QS, d.H, b->w_xh, b->w_xl, (int)T, 1, d.QS / kTcK, b->w_y, s, b->errw);
     launch_ex(kb_resid_norm, dim3((unsigned)T), dim3(kNormThreads), 0, s, b->w_h, (const float*)b->w_y, 1, 0LL,
               (const __half*)nullptr, (const int*)nullptr, d.V, L.n_post, d.H, d.eps, b->w_xh, b->w_xl, b->errw);
-    gemm_q4(L.gu, d.H, 2 * d.I, b->w_xh, b->w_xl, (int)T, 1, d.H / kTcK, b->w_y, s, b->errw);
-    launch(kb_silu_split, dim3(silu_grid), s, (const float*)b->w_y, 1, 0LL, (int)T, d.I, b->w_xh, b->w_xl);
-    gemm_q4(L.d, d.I, d.H, b->w_xh, b->w_xl, (int)T, 1, d.I / kTcK, b->w_y, s, b->errw);
+    // gate/up: silu(gate) * up goes straight into the down GEMM's operands
+    gemm_q4_silu(L.gu, d.H, d.I, b->w_xh, b->w_xl, (int)T, b->w_ah, b->w_al, s, b->errw);
+    gemm_q4(L.d, d.I, d.H, b->w_ah, b->w_al, (int)T, 1, d.I / kTcK, b->w_y, s, b->errw);
   }
   launch_ex(kb_resid_norm, dim3((unsigned)T), dim3(kNormThreads), 0, s, b->w_h, (const float*)b->w_y, 1, 0LL,
             (const __half*)nullptr, (const int*)nullptr, d.V, (const float*)e->final_norm, d.H, d.eps, b->w_xh,

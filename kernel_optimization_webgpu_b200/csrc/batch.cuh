@@ -70,20 +70,21 @@ __device__ __forceinline__ float sum_parts(const float* parts, int nparts, long 
 }
 
 // ---- residual + RMSNorm into the GEMM's hi/lo operands ----------------------------
-// Row b (one CTA of 1024 threads, one element per thread for K <= 1024):
+// Row b (one CTA of 256 threads, 4 consecutive elements per thread and pass):
 // h[b] = embed row of tokens[b] (embedding mode), or h[b] + sum(parts) (residual
 // mode; parts == nullptr leaves h as is); then x = rms_norm(h[b]) * w ->
-// x_hi[b], x_lo[b]. h is written back in place.
-constexpr int kNormThreads = 1024;
+// x_hi[b], x_lo[b]. h is written back in place. K is a multiple of 4, <= 4096.
+constexpr int kNormThreads = 256;
 static __global__ void __launch_bounds__(kNormThreads) kb_resid_norm(float* h, const float* parts, int nparts,
                                                                      long long part_stride, const __half* embed,
                                                                      const int* tokens, int vocab, const float* w,
                                                                      int K, float eps, __half* x_hi, __half* x_lo,
                                                                      int* err) {
+  constexpr int kMaxPer = 4;  // float4 items per thread (K <= 4096)
   __shared__ float red[kNormThreads / 32];
   pdl_wait();
   const int b = blockIdx.x;
-  float* hr = h + (long long)b * K;
+  float4* hr = reinterpret_cast<float4*>(h + (long long)b * K);
   const __half* er = nullptr;
   if (embed) {
     int tok = tokens[b];
@@ -93,14 +94,48 @@ static __global__ void __launch_bounds__(kNormThreads) kb_resid_norm(float* h, c
     }
     er = embed + (long long)tok * K;
   }
+  const int K4 = K >> 2;
+  float4 v[kMaxPer];
   float ss = 0.0f;
-  for (int e = threadIdx.x; e < K; e += kNormThreads) {
-    float v;
-    if (er) v = __half2float(er[e]);
-    else if (parts) v = hr[e] + sum_parts(parts, nparts, part_stride, (long long)b * K + e);
-    else v = hr[e];
-    if (er || parts) hr[e] = v;
-    ss += v * v;
+#pragma unroll
+  for (int k = 0; k < kMaxPer; ++k) {
+    const int e4 = threadIdx.x + k * kNormThreads;
+    if (e4 >= K4) break;
+    float4 x;
+    if (er) {
+      const uint2 u = *reinterpret_cast<const uint2*>(er + 4 * e4);
+      const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+      const float2 c = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+      x = make_float4(a.x, a.y, c.x, c.y);
+    } else {
+      x = hr[e4];
+      if (parts) {
+        const long long i4 = (long long)b * K4 + e4;
+        const float4* p4 = reinterpret_cast<const float4*>(parts);
+        const long long s4 = part_stride >> 2;
+        float4 acc = p4[i4];
+        if (nparts > 1) {
+          float4 pv[kMaxParts - 1];
+#pragma unroll
+          for (int s = 1; s < kMaxParts; ++s) pv[s - 1] = p4[(long long)min(s, nparts - 1) * s4 + i4];
+#pragma unroll
+          for (int s = 1; s < kMaxParts; ++s)
+            if (s < nparts) {
+              acc.x += pv[s - 1].x;
+              acc.y += pv[s - 1].y;
+              acc.z += pv[s - 1].z;
+              acc.w += pv[s - 1].w;
+            }
+        }
+        x.x += acc.x;
+        x.y += acc.y;
+        x.z += acc.z;
+        x.w += acc.w;
+      }
+    }
+    if (er || parts) hr[e4] = x;
+    v[k] = x;
+    ss += x.x * x.x + x.y * x.y + x.z * x.z + x.w * x.w;
   }
   ss = warp_sum(ss);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
@@ -110,11 +145,21 @@ static __global__ void __launch_bounds__(kNormThreads) kb_resid_norm(float* h, c
 #pragma unroll
   for (int k = 0; k < kNormThreads / 32; ++k) t += red[k];
   const float inv = rsqrtf(t / (float)K + eps);
-  for (int e = threadIdx.x; e < K; e += kNormThreads) {
-    __half hi, lo;
-    split_f16(hr[e] * inv * w[e], hi, lo);
-    x_hi[(long long)b * K + e] = hi;
-    x_lo[(long long)b * K + e] = lo;
+  const float4* w4 = reinterpret_cast<const float4*>(w);
+#pragma unroll
+  for (int k = 0; k < kMaxPer; ++k) {
+    const int e4 = threadIdx.x + k * kNormThreads;
+    if (e4 >= K4) break;
+    const float4 ww = w4[e4];
+    __half h0, l0, h1, l1, h2, l2, h3, l3;
+    split_f16(v[k].x * inv * ww.x, h0, l0);
+    split_f16(v[k].y * inv * ww.y, h1, l1);
+    split_f16(v[k].z * inv * ww.z, h2, l2);
+    split_f16(v[k].w * inv * ww.w, h3, l3);
+    __half2 hh[2] = {__halves2half2(h0, h1), __halves2half2(h2, h3)};
+    __half2 ll[2] = {__halves2half2(l0, l1), __halves2half2(l2, l3)};
+    *reinterpret_cast<uint2*>(x_hi + (long long)b * K + 4 * e4) = *reinterpret_cast<const uint2*>(hh);
+    *reinterpret_cast<uint2*>(x_lo + (long long)b * K + 4 * e4) = *reinterpret_cast<const uint2*>(ll);
   }
 }
 
@@ -136,22 +181,26 @@ static __global__ void __launch_bounds__(256) kb_rope_cache(const float* parts, 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tasks = q_heads + 2 * NKV;
   const int ld = tasks * kHeadDim;
-  const long long nt = (long long)R * tasks;
-  for (long long task = (long long)blockIdx.x * 8 + warp; task < nt; task += (long long)gridDim.x * 8) {
-    const int r = (int)(task / tasks), t = (int)(task % tasks);
-    const long long grow = row0 + r;
-    const int seq = (int)(grow / rows_per_seq);
-    const int p = (pos ? pos[seq] : 0) + (int)(grow % rows_per_seq);
+  const int nt = R * tasks;  // the host keeps R * tasks and row0 + R below 2^31
+  const int r0 = (int)row0;
+  for (int task = blockIdx.x * 8 + warp; task < nt; task += gridDim.x * 8) {
+    const int r = task / tasks, t = task - r * tasks;
+    const int grow = r0 + r;
+    const int seq = grow / rows_per_seq;
+    const int p = (pos ? pos[seq] : 0) + (grow - seq * rows_per_seq);
     if (p < 0 || p >= max_seq) {
       if (lane == 0) atomicOr(err, kErrPosition);
       continue;
     }
     const long long base = (long long)r * ld + (long long)t * kHeadDim + 4 * lane;
-    float4 x;
-    x.x = sum_parts(parts, nparts, part_stride, base);
-    x.y = sum_parts(parts, nparts, part_stride, base + 1);
-    x.z = sum_parts(parts, nparts, part_stride, base + 2);
-    x.w = sum_parts(parts, nparts, part_stride, base + 3);
+    float4 x = *reinterpret_cast<const float4*>(parts + base);
+    for (int s = 1; s < nparts; ++s) {  // split-K partials in order (decode only: at most a few)
+      const float4 y = *reinterpret_cast<const float4*>(parts + (long long)s * part_stride + base);
+      x.x += y.x;
+      x.y += y.y;
+      x.z += y.z;
+      x.w += y.w;
+    }
     if (t >= q_heads + NKV) {  // v: cached as projected
       const int g = t - q_heads - NKV;
       __half* dst = vc + (((long long)seq * NKV + g) * max_seq + p) * kHeadDim + 4 * lane;

@@ -725,6 +725,11 @@ void launch_gemm(TcArgs a, int splits, int mode, cudaStream_t s) {
     if (a.B <= 64) launch_gemm_t<64, false, kTcStore>(a, splits, s);
     else if (a.B <= 128) launch_gemm_t<128, false, kTcStore>(a, splits, s);
     else launch_gemm_t<256, false, kTcStore>(a, splits, s);
+  } else if (mode == kGemmQ4Silu) {
+    if (splits != 1 || (a.n_rows & 1) || !a.y_hi || !a.y_lo)
+      throw QdError{QD_E_INVALID, "GEMM: the silu epilogue needs one split, paired rows and hi/lo outputs"};
+    if (a.B <= 128) launch_gemm_t<128, false, kTcSilu>(a, splits, s);
+    else launch_gemm_t<256, false, kTcSilu>(a, splits, s);
   } else {
     if (a.B <= 64) launch_gemm_t<64, true, kTcArgmax>(a, splits, s);
     else launch_gemm_t<128, true, kTcArgmax>(a, splits, s);

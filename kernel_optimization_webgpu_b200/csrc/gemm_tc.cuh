@@ -49,6 +49,7 @@ constexpr unsigned long long kTcWaitNs = 1000ull * 1000 * 1000;
 enum TcEpi : int {
   kTcStore = 0,   // y[split][b][n] = acc (split-K partials; the consumer sums them)
   kTcArgmax = 1,  // per (b, CTA) best (value, row) over the CTA's 128 rows; logits to y if set
+  kTcSilu = 2,    // rows 2j, 2j+1 = gate j, up j (no split-K): y_hi/y_lo[b][j] = split(silu(gate) * up)
 };
 
 struct TcArgs {
@@ -78,6 +79,8 @@ struct TcArgs {
   long long y_split;          // floats between two splits' outputs
   float* part_v;              // kTcArgmax: [B][gridDim.x] best value / row
   uint32_t* part_i;
+  __half* y_hi;               // kTcSilu: the next GEMM's operands [B][ldy]
+  __half* y_lo;
   int* err;                   // device status word (bit kTcErrTimeout)
 };
 
@@ -433,7 +436,20 @@ __global__ void __launch_bounds__(kTcThreads + 32, 1) k_gemm_tc(const __grid_con
       tmem_ld32(tmem + lane_base + BN + c0, dc);
 #pragma unroll
       for (int j = 0; j < 32; ++j) dm[j] = (dm[j] + dc[j] * (1.0f / kLoScale)) * unscale;
-      if (y) {
+      if constexpr (EPI == kTcSilu) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const float up = __shfl_xor_sync(0xffffffffu, dm[j], 1);  // lane pairs: gate (even), up (odd)
+          const int b = b0 + c0 + j;
+          if ((lane & 1) == 0 && row_live && b < a.B) {
+            const float act = dm[j] / (1.0f + expf(-dm[j])) * up;
+            __half hh, ll;
+            split_f16(act, hh, ll);
+            a.y_hi[(long long)b * a.ldy + (n >> 1)] = hh;
+            a.y_lo[(long long)b * a.ldy + (n >> 1)] = ll;
+          }
+        }
+      } else if (y) {
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
           const int b = b0 + c0 + j;

@@ -85,7 +85,7 @@ void set_thread_error(const std::string& msg);
 
 // tcgen05 GEMM launch (gemm_tc.cuh): q4 weights with split-K partial outputs,
 // or the f16 LM head with the per-CTA (max, index) epilogue.
-enum GemmMode : int { kGemmQ4Store = 0, kGemmF16Argmax = 1 };
+enum GemmMode : int { kGemmQ4Store = 0, kGemmF16Argmax = 1, kGemmQ4Silu = 2 };
 struct TcArgs;
 void launch_gemm(TcArgs a, int splits, int mode, cudaStream_t s);
 // Splits actually used for K columns when `want` are asked for (no empty split).
