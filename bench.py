@@ -173,6 +173,14 @@ def barrier(world):
         dist.barrier()
 
 
+def shard_range(total: int, world: int, rank: int):
+    """Contiguous share [lo, hi) of `total` independent units for `rank` (no remainder allowed)."""
+    if total % world:
+        raise ValueError(f"{total} units do not split evenly over {world} ranks")
+    per = total // world
+    return rank * per, (rank + 1) * per
+
+
 def max_over_ranks(x: float, world: int) -> float:
     if world == 1:
         return x
@@ -511,12 +519,11 @@ def run_prefill(args, world, rank, local):
     _, peak_kind = peaks()
     tflops_peak = _bf16_peak()
     shape = synth.QWEN3_0_6B
-    if PF_PROMPTS % world:
-        raise SystemExit("32 prompts must split evenly over the ranks")
-    mine = PF_PROMPTS // world
+    lo, hi = shard_range(PF_PROMPTS, world, rank)
+    mine = hi - lo
     rng = np.random.Generator(np.random.PCG64(PF_SEED))
     all_ids = rng.integers(0, shape.vocab, size=(PF_PROMPTS, PF_LEN)).astype(np.int32)
-    ids = np.ascontiguousarray(all_ids[rank * mine:(rank + 1) * mine])
+    ids = np.ascontiguousarray(all_ids[lo:hi])
     eng = R.Engine(rt, device=local, max_seq=64)
     stream = torch.cuda.Stream()
     eng.set_stream(stream)
