@@ -244,7 +244,8 @@ __global__ void __launch_bounds__(kTcThreads + 32, 1) k_gemm_tc(const __grid_con
   unsigned char* ring =
       reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   unsigned char* abuf = ring + S * kStage;  // q4: [2][A_hi | A_lo]
-  __shared__ unsigned long long full[S], empty[S], adone[2];
+  // full_w: the stage's weight tile landed; full_b: its x_hi / x_lo tiles landed
+  __shared__ unsigned long long full_w[S], full_b[S], empty[S], adone[2];
   __shared__ unsigned tmem_base;
   __shared__ float red_v[EPI == kTcArgmax ? 4 : 1][EPI == kTcArgmax ? BN : 1];
   __shared__ uint32_t red_i[EPI == kTcArgmax ? 4 : 1][EPI == kTcArgmax ? BN : 1];
@@ -265,7 +266,8 @@ __global__ void __launch_bounds__(kTcThreads + 32, 1) k_gemm_tc(const __grid_con
   if (tid == 0) {
 #pragma unroll
     for (int i = 0; i < S; ++i) {
-      tc_mbar_init(&full[i]);
+      tc_mbar_init(&full_w[i]);
+      tc_mbar_init(&full_b[i]);
       tc_mbar_init(&empty[i]);
     }
     tc_mbar_init(&adone[0]);
@@ -292,10 +294,9 @@ __global__ void __launch_bounds__(kTcThreads + 32, 1) k_gemm_tc(const __grid_con
       // waiting for the kernel that produces the activations.
       const int pre = min(S, nk);
       for (int k = 0; k < pre; ++k) {
-        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(tc_smem(&full[k])),
-                     "r"(kW + 2 * kBt)
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(tc_smem(&full_w[k])), "r"(kW)
                      : "memory");
-        tma_load_2d(ring + k * kStage, &a.tm_w, AF16 ? (kt0 + k) * kTcK : (kt0 + k) * 32, n0, &full[k]);
+        tma_load_2d(ring + k * kStage, &a.tm_w, AF16 ? (kt0 + k) * kTcK : (kt0 + k) * 32, n0, &full_w[k]);
       }
       pdl_wait();
       for (int k = 0; k < nk; ++k) {
@@ -306,13 +307,15 @@ __global__ void __launch_bounds__(kTcThreads + 32, 1) k_gemm_tc(const __grid_con
             ok = false;
             break;
           }
-          asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(tc_smem(&full[slot])),
-                       "r"(kW + 2 * kBt)
+          asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(tc_smem(&full_w[slot])), "r"(kW)
                        : "memory");
-          tma_load_2d(st, &a.tm_w, AF16 ? (kt0 + k) * kTcK : (kt0 + k) * 32, n0, &full[slot]);
+          tma_load_2d(st, &a.tm_w, AF16 ? (kt0 + k) * kTcK : (kt0 + k) * 32, n0, &full_w[slot]);
         }
-        tma_load_2d(st + kW, &a.tm_xh, (kt0 + k) * kTcK, b0, &full[slot]);
-        tma_load_2d(st + kW + kBt, &a.tm_xl, (kt0 + k) * kTcK, b0, &full[slot]);
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(tc_smem(&full_b[slot])),
+                     "r"(2 * kBt)
+                     : "memory");
+        tma_load_2d(st + kW, &a.tm_xh, (kt0 + k) * kTcK, b0, &full_b[slot]);
+        tma_load_2d(st + kW + kBt, &a.tm_xl, (kt0 + k) * kTcK, b0, &full_b[slot]);
         last[slot] = k;
       }
       if (!ok) atomicOr(&failed, 1);
@@ -320,7 +323,10 @@ __global__ void __launch_bounds__(kTcThreads + 32, 1) k_gemm_tc(const __grid_con
       // newest tile of each stage is the only one that can be in flight.
 #pragma unroll
       for (int i = 0; i < S; ++i)
-        if (last[i] >= 0) (void)tc_mbar_wait(&full[i], (unsigned)(last[i] / S) & 1u);
+        if (last[i] >= 0) {
+          (void)tc_mbar_wait(&full_w[i], (unsigned)(last[i] / S) & 1u);
+          (void)tc_mbar_wait(&full_b[i], (unsigned)(last[i] / S) & 1u);
+        }
     }
   } else {
     // ---- consumers: dequantisation, MMA issue, epilogue ----
@@ -342,7 +348,7 @@ __global__ void __launch_bounds__(kTcThreads + 32, 1) k_gemm_tc(const __grid_con
       const int slot = i % S, st = i & 1;
       unsigned char* stg = ring + slot * kStage;
       if constexpr (!AF16) {
-        ok = tc_mbar_wait(&full[slot], (unsigned)(i / S) & 1u) && ok;
+        ok = tc_mbar_wait(&full_w[slot], (unsigned)(i / S) & 1u) && ok;
         if (i >= 2) ok = tc_mbar_wait(&adone[st], (unsigned)((i - 2) >> 1) & 1u) && ok;
         unsigned char* A_hi = abuf + st * 2 * kA;
         unsigned char* A_lo = A_hi + kA;
@@ -373,7 +379,7 @@ __global__ void __launch_bounds__(kTcThreads + 32, 1) k_gemm_tc(const __grid_con
           ok = false;
           break;
         }
-        if (tid == 0) {
+        if (tid == 0 && (ok = tc_mbar_wait(&full_b[slot], (unsigned)(i / S) & 1u))) {
           tc_fence_after();
 #pragma unroll
           for (int ks = 0; ks < kTcK / 16; ++ks) {
@@ -392,7 +398,7 @@ __global__ void __launch_bounds__(kTcThreads + 32, 1) k_gemm_tc(const __grid_con
         }
       } else {
         if (tid == 0) {  // the table tile arrives ready to use: only the MMAs to issue
-          if (!tc_mbar_wait(&full[slot], (unsigned)(i / S) & 1u)) {
+          if (!tc_mbar_wait(&full_w[slot], (unsigned)(i / S) & 1u) || !tc_mbar_wait(&full_b[slot], (unsigned)(i / S) & 1u)) {
             ok = false;
             break;
           }
