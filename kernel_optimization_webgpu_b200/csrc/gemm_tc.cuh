@@ -214,7 +214,8 @@ __device__ __forceinline__ bool consumers_any(bool pred) {
 
 template <int BN, bool AF16>
 __host__ __device__ constexpr int tc_stages() {
-  return AF16 ? (BN <= 64 ? 4 : 3) : (BN <= 64 ? 4 : (BN <= 128 ? 3 : 2));
+  // q4 at BN = 64 (decode): two stages keep the CTA at ~105 KB so two fit per SM
+  return AF16 ? (BN <= 64 ? 4 : 3) : (BN <= 64 ? 2 : (BN <= 128 ? 3 : 2));
 }
 template <int BN, bool AF16>
 __host__ __device__ constexpr int tc_stage_bytes() {
@@ -355,20 +356,36 @@ __global__ void __launch_bounds__(kTcThreads + 32, 1) k_gemm_tc(const __grid_con
         if (ok) {
           const uint4* raw = reinterpret_cast<const uint4*>(stg + tid * 32);
           const uint4 q0 = raw[0], q1 = raw[1];
-          const __half2 s2 = *reinterpret_cast<const __half2*>(&sc_cur);
-          const float sc[2] = {__low2float(s2) * (float)(1 << kWShift), __high2float(s2) * (float)(1 << kWShift)};
           const uint32_t ws[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+          // f16x2 arithmetic, exact: q = n - 8 from the biased pattern 0x6400 | n (1024 + n);
+          // hi = q * s' (s' = scale * 2^10, exact in f16) rounded once, as f32 math then a
+          // round to f16 would; lo = (q * s' - hi) * 2^11 with the residual from one fma.
+          const __half2 s2 = *reinterpret_cast<const __half2*>(&sc_cur);
+          const __half2 k1024 = __float2half2_rn(1024.0f), bias = __float2half2_rn(1032.0f);
+          const __half2 k2048 = __float2half2_rn(kLoScale);
+          const __half2 sa = __hmul2(__low2half2(s2), k1024), sb = __hmul2(__high2half2(s2), k1024);
 #pragma unroll
           for (int wi = 0; wi < 8; ++wi) {  // 8 columns per word -> one 16-byte chunk of f16
-            __align__(16) __half hi8[8], lo8[8];
+            const uint32_t w = ws[wi];
+            const __half2 scl = wi < 4 ? sa : sb;
+            uint32_t hi_p[4], lo_p[4];
 #pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              const float v = (float)((int)((ws[wi] >> (4 * e)) & 0xFu) - 8) * sc[wi >> 2];
-              split_f16(v, hi8[e], lo8[e]);
+            for (int i = 0; i < 4; ++i) {  // pair i = columns (i, i + 4) of the word
+              const uint32_t bits = ((w >> (4 * i)) & 0x000F000Fu) | 0x64006400u;
+              const __half2 q = __hsub2(*reinterpret_cast<const __half2*>(&bits), bias);
+              const __half2 h = __hmul2(q, scl);
+              const __half2 l = __hmul2(__hfma2(q, scl, __hneg2(h)), k2048);
+              hi_p[i] = *reinterpret_cast<const uint32_t*>(&h);
+              lo_p[i] = *reinterpret_cast<const uint32_t*>(&l);
             }
+            // back to column order: (c0,c1) (c2,c3) (c4,c5) (c6,c7)
+            const uint4 H = make_uint4(__byte_perm(hi_p[0], hi_p[1], 0x5410), __byte_perm(hi_p[2], hi_p[3], 0x5410),
+                                       __byte_perm(hi_p[0], hi_p[1], 0x7632), __byte_perm(hi_p[2], hi_p[3], 0x7632));
+            const uint4 Lo = make_uint4(__byte_perm(lo_p[0], lo_p[1], 0x5410), __byte_perm(lo_p[2], lo_p[3], 0x5410),
+                                        __byte_perm(lo_p[0], lo_p[1], 0x7632), __byte_perm(lo_p[2], lo_p[3], 0x7632));
             const unsigned off = sw128_off(tid, wi * 8);
-            *reinterpret_cast<uint4*>(A_hi + off) = *reinterpret_cast<const uint4*>(hi8);
-            *reinterpret_cast<uint4*>(A_lo + off) = *reinterpret_cast<const uint4*>(lo8);
+            *reinterpret_cast<uint4*>(A_hi + off) = H;
+            *reinterpret_cast<uint4*>(A_lo + off) = Lo;
           }
           sc_cur = sc_next;
           if (row_live && i + 2 < nk)
