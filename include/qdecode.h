@@ -54,7 +54,11 @@ typedef struct qd_options {
   int rope_row_stride;   /* cos/sin offset = position * stride + pair; 0 = head_dim (reference) */
   const char* variant;   /* "optimized" | "mixed" | "original": accepted, one B200 path */
   int use_graph;         /* 1 (default): each token is one CUDA graph launch */
-  int persistent;        /* 1 (default): one persistent kernel per token where the shape allows;
+  int persistent;        /* 1 (default): one persistent kernel per token, one CTA per SM, where
+                            the shape allows;
+                            2: one launch per token on thread-block clusters of 8 CTAs (the
+                            q/k/v -> attention and gate/up -> down exchanges stay inside a
+                            cluster) where the shape and device allow, else as 1;
                             0: one kernel per fused stage */
   int timeline;          /* 1: record per-CTA stage timestamps of each persistent launch */
 } qd_options;
@@ -93,14 +97,25 @@ int qd_generate_greedy(qd_engine* e, const int32_t* input_ids, int n_prompt, int
 /* Parity and inspection helpers. */
 int qd_engine_logits(qd_engine* e, float* host_logits);       /* logits of the last generated step */
 int qd_engine_hidden(qd_engine* e, float* host_hidden);       /* residual stream after the last layer */
-int qd_engine_uses_persistent(const qd_engine* e);            /* 1 if tokens run as one persistent kernel */
+/* Token kernel in use: 2 = cluster kernel, 1 = single-CTA-ring persistent kernel,
+ * 0 = one kernel per stage. */
+int qd_engine_uses_persistent(const qd_engine* e);
 /* Stage timestamps (ns, globaltimer) of the last persistent launch: host_out[cta][event]
- * (needs qd_options.timeline = 1). Event order per CTA: start; per layer 14 events (QKV
- * input ready, QKV weights ready, QKV stored, attention done, O input ready, O stored,
- * gate/up input ready, gate/up stored, down input ready, down stored, QKV norm done, O
- * weights ready, gate/up norm done, down weights ready); LM-head input ready, LM head
- * done, merged (last CTA only). Pass host_out NULL to query the sizes. */
+ * (needs qd_options.timeline = 1). Pass host_out NULL to query the sizes.
+ * Cluster kernel, per CTA: start; per layer 11 events (layer input ready, q/k/v weights
+ * ready, q/k/v rows done, group rows exchanged, attention partial done, partials
+ * exchanged, O partial added, O sums ready, gate/up done, activations exchanged, down
+ * partial added; attention-only events stay 0 in the other clusters); LM-head input
+ * ready, LM head done, merged (last CTA only).
+ * Single-CTA-ring kernel, per CTA: start; per layer 14 events (QKV input ready, QKV
+ * weights ready, QKV stored, attention done, O input ready, O stored, gate/up input
+ * ready, gate/up stored, down input ready, down stored, QKV norm done, O weights ready,
+ * gate/up norm done, down weights ready); LM-head input ready, LM head done, merged. */
 int qd_engine_timeline(qd_engine* e, uint64_t* host_out, int* ctas, int* events_per_cta);
+/* SM clock (clock64) stamps inside every layer of the last cluster-kernel launch:
+ * host_out[cta][layer][event], events_per_layer per layer (needs qd_options.timeline = 1
+ * and the cluster kernel). For stage-by-stage cycle counts within one CTA. */
+int qd_engine_timeline_fine(qd_engine* e, uint64_t* host_out, int* ctas, int* events_per_layer);
 /* One token through the layers at `position` (no LM head), with the residual
  * stream after every layer copied to host_trace[layers][hidden]. */
 int qd_engine_forward_trace(qd_engine* e, int32_t token, int position, float* host_trace);

@@ -9,6 +9,7 @@
 
 #include "../../include/qdecode.h"
 #include "common.cuh"
+#include "cluster.cuh"
 #include "persist.cuh"
 
 namespace qd {
@@ -145,4 +146,17 @@ struct qd_engine {
   size_t persist_smem = 0;
   int lm_rows = 0;
   unsigned long long* timeline = nullptr;  // stage stamps of the last persistent launch (opt-in)
+  // cluster decode kernel (cluster.cuh)
+  bool clus = false;
+  int ncl = 0;                       // clusters of kCC CTAs
+  int c_slot = 0, c_nslots = 0, c_lmrows = 0;
+  size_t c_smem = 0;
+  long long c_layer_bytes = 0;
+  std::vector<long long> c_cta_off;  // host copy of each CTA's slice offset inside a layer
+  void* cblob = nullptr;             // packed per-CTA layer slices
+  long long* c_d_cta_off = nullptr;
+  float* c_norms = nullptr;           // [L][input | post | q | k] norm weights
+  unsigned long long* c_fine = nullptr;  // [grid][L][kCFine] SM clock stamps (timeline option)
+  long long* c_acc = nullptr;        // [2][L][2][H] fixed-point sums
+  unsigned* c_cnt = nullptr;         // [2][L][2][32] counters
 };

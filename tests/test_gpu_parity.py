@@ -158,12 +158,13 @@ def test_engine_layer_trace_matches_oracle(tiny_runtime, tiny_model, kv):
                 assert rel(got[layer], want[layer]) < TOL, (pos, layer)
 
 
-@pytest.mark.parametrize("use_graph,persistent", [(True, True), (False, True), (True, False), (False, False)])
+# persistent: 2 = cluster kernel, 1 = single-CTA-ring kernel, 0 = one kernel per stage
+@pytest.mark.parametrize("use_graph,persistent", [(True, 2), (False, 2), (True, 1), (False, 1), (True, 0), (False, 0)])
 def test_engine_greedy_tiny_matches_oracle_f16_kv(tiny_runtime, tiny_model, use_graph, persistent):
     with open(os.path.join(GOLDEN, "tiny_seed2_greedy.json")) as f:
         g = json.load(f)
     with R.Engine(tiny_runtime, max_seq=64, use_graph=use_graph, persistent=persistent) as eng:
-        assert eng.persistent == persistent
+        assert eng.token_kernel == persistent
         ids, st = eng.generate_greedy(g["prompt"], g["max_new"])
         sess = tiny_model.session(max_seq=64, kv_f16=True)
         want, margins = sess.greedy(g["prompt"], g["max_new"])
@@ -175,11 +176,12 @@ def test_engine_greedy_tiny_matches_oracle_f16_kv(tiny_runtime, tiny_model, use_
         assert rel(eng.hidden(), sess.hidden()) < TOL
 
 
-@pytest.mark.parametrize("persistent", [True, False])
+@pytest.mark.parametrize("persistent", [2, 1, 0])
 def test_engine_greedy_tiny_f32_kv_matches_js_port_golden(tiny_runtime, persistent):
     with open(os.path.join(GOLDEN, "tiny_seed2_greedy.json")) as f:
         g = json.load(f)
     with R.Engine(tiny_runtime, max_seq=64, kv_dtype="f32", persistent=persistent) as eng:
+        assert eng.token_kernel == persistent
         ids, _ = eng.generate_greedy(g["prompt"], 1)
         first = np.load(os.path.join(GOLDEN, "tiny_seed2_first_logits.npy"))
         assert rel(eng.logits(), first) < TOL
@@ -222,7 +224,7 @@ def test_reference_api_mirror(tiny_runtime):
     ctx["device"].close()
 
 
-@pytest.mark.parametrize("persistent", [True, False])
+@pytest.mark.parametrize("persistent", [2, 1, 0])
 def test_engine_qwen_shape_greedy_config2(qwen_runtime, persistent):
     """Config 2: 28 layers, 8 seeded prompt ids, 24 generated tokens, f16 KV."""
     rng = np.random.Generator(np.random.PCG64(2))
@@ -230,7 +232,7 @@ def test_engine_qwen_shape_greedy_config2(qwen_runtime, persistent):
     model = O.Model(qwen_runtime)
     want, margins = model.session(max_seq=64, kv_f16=True).greedy(prompt, 24)
     with R.Engine(qwen_runtime, max_seq=64, persistent=persistent) as eng:
-        assert eng.persistent == persistent
+        assert eng.token_kernel == persistent
         ids, _ = eng.generate_greedy(prompt, 24)
         assert ids == want, (ids, want, margins.tolist())
         got_h = eng.forward_trace(want[-1], 8 + 23)[-1]
