@@ -296,10 +296,12 @@ __global__ void __launch_bounds__(kBAttnThreads) kb_attn(const __grid_constant__
     unsigned char* st = stages + (t & 1) * kBAttnStage;
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(tc_smem(mb)), "r"(kBAttnStage)
                  : "memory");
-    tma_load_2d(st, &kvmap, 0, (int)(k_row0 + row), mb);
-    tma_load_2d(st + kBAttnBox, &kvmap, 64, (int)(k_row0 + row), mb);
-    tma_load_2d(st + 2 * kBAttnBox, &kvmap, 0, (int)(v_row0 + row), mb);
-    tma_load_2d(st + 3 * kBAttnBox, &kvmap, 64, (int)(v_row0 + row), mb);
+    // KV rows are read once per step: evict-first keeps the step's small tensors in L2
+    const unsigned long long pol = l2_evict_first();
+    tma_load_2d_hint(st, &kvmap, 0, (int)(k_row0 + row), mb, pol);
+    tma_load_2d_hint(st + kBAttnBox, &kvmap, 64, (int)(k_row0 + row), mb, pol);
+    tma_load_2d_hint(st + 2 * kBAttnBox, &kvmap, 0, (int)(v_row0 + row), mb, pol);
+    tma_load_2d_hint(st + 3 * kBAttnBox, &kvmap, 64, (int)(v_row0 + row), mb, pol);
   };
   __syncthreads();  // barrier init visible
   int issued = 0;   // thread 0 only

@@ -211,7 +211,7 @@ __device__ __forceinline__ void c_issue(const CArgs& a, const CShared& S, const 
   // barrier that precedes this call, so no proxy fence is needed.
   const int slot = i % a.n_slots;
   mbar_arrive_tx(&S.mbar[slot], bytes);
-  if (bytes) bulk_load(S.ring + (size_t)slot * a.slot_bytes, src, bytes, &S.mbar[slot]);
+  if (bytes) bulk_load_hint(S.ring + (size_t)slot * a.slot_bytes, src, bytes, &S.mbar[slot], policy_evict_first());
   R.issued = i + 1;
 }
 

@@ -291,13 +291,23 @@ __global__ void __launch_bounds__(kTcThreads + 32, 1) k_gemm_tc(const __grid_con
       int last[S];
 #pragma unroll
       for (int i = 0; i < S; ++i) last[i] = -1;
+      // With one column tile (decode) every weight tile is read exactly once per
+      // launch: evict-first. With several (prefill) the other column tiles reread
+      // it from L2, so it keeps the normal policy.
+      const bool once = gridDim.y == 1;
+      const unsigned long long pol = l2_evict_first();
+      auto load_w = [&](unsigned char* dst, int k, unsigned long long* mb) {
+        const int x = AF16 ? (kt0 + k) * kTcK : (kt0 + k) * 32;
+        if (once) tma_load_2d_hint(dst, &a.tm_w, x, n0, mb, pol);
+        else tma_load_2d(dst, &a.tm_w, x, n0, mb);
+      };
       // The weights are constant: the first stages' weight tiles go out before
       // waiting for the kernel that produces the activations.
       const int pre = min(S, nk);
       for (int k = 0; k < pre; ++k) {
         asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(tc_smem(&full_w[k])), "r"(kW)
                      : "memory");
-        tma_load_2d(ring + k * kStage, &a.tm_w, AF16 ? (kt0 + k) * kTcK : (kt0 + k) * 32, n0, &full_w[k]);
+        load_w(ring + k * kStage, k, &full_w[k]);
       }
       pdl_wait();
       for (int k = 0; k < nk; ++k) {
@@ -310,7 +320,7 @@ __global__ void __launch_bounds__(kTcThreads + 32, 1) k_gemm_tc(const __grid_con
           }
           asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(tc_smem(&full_w[slot])), "r"(kW)
                        : "memory");
-          tma_load_2d(st, &a.tm_w, AF16 ? (kt0 + k) * kTcK : (kt0 + k) * 32, n0, &full_w[slot]);
+          load_w(st, k, &full_w[slot]);
         }
         asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(tc_smem(&full_b[slot])),
                      "r"(2 * kBt)
