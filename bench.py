@@ -36,6 +36,9 @@ import numpy as np  # noqa: E402
 from kernel_optimization_webgpu_b200 import synth  # noqa: E402
 
 PROMPT_LEN, NEW_TOKENS = 8, 24
+# DRAM bytes (read + write) of one k_decode_persistent token launch, measured by ncu
+# on the default workload (561.50 MB read + 4.77 MB written).
+B1_TRAFFIC = 566265856
 WORKLOAD = ("batch-1 greedy decode, Qwen3-0.6B shape (28 layers, hidden 1024, 16q/8kv heads x 128, "
             "SwiGLU 3072, q4 MatMulNBits block 32 with f16 scales, tied f16 LM head 151936x1024, f16 KV), "
             "8-token prompt + 24 generated, seed 2")
@@ -313,6 +316,11 @@ def run_ours(args, world, rank, local):
     ids = prompt_ids()
     eng = R.Engine(rt, device=local, max_seq=64)
     step_kernels = eng.step_kernels
+    eng_kernel = eng.token_kernel
+    token_kernel_desc = {
+        2: "decode token: k_decode_cluster, one launch per token (28 layers + LM head/argmax)",
+        1: "decode token: k_decode_persistent, one launch per token (28 layers + LM head/argmax)",
+    }.get(eng.token_kernel, f"decode token: one CUDA graph of {step_kernels} kernels (28 layers + LM head/argmax)")
     stream = torch.cuda.Stream()
     eng.set_stream(stream)
     shape = synth.QWEN3_0_6B
@@ -400,10 +408,12 @@ def run_ours(args, world, rank, local):
             "config": {"workload": WORKLOAD, "global_batch": world, "seq_len": PROMPT_LEN + NEW_TOKENS,
                        "parallelism": f"replicas x{world} (batch-1 decode does not shard)",
                        "l2": "inputs larger than L2 (559 MB of weights streamed per token, L2 126 MB)"},
-            "roofline": {"bound": "hbm", "kernel": "decode token (one CUDA graph: 28 layers x 5 kernels + "
-                                                   "LM head/argmax)",
+            "roofline": {"bound": "hbm", "kernel": token_kernel_desc,
                          "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(achieved / peak, 4), "traffic": None,
+                         "frac": round(achieved / peak, 4),
+                         "traffic": B1_TRAFFIC if eng_kernel == 1 else None,
+                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch "
+                                           "(profiles/persistent_decode_b1_warp_states.md)" if eng_kernel == 1 else None,
                          "bytes_per_step": int(bytes_avg), "peak_source": peak_kind},
             "e2e": {"value": round(e2e, 2), "unit": UNIT, "h2d_bytes_per_step": PROMPT_LEN * 4,
                     "d2h_bytes_per_step": NEW_TOKENS * 4,
