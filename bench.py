@@ -451,7 +451,22 @@ def run_b64(args, world, rank, local):
     bt.fill_context(B64_CTX, B64_SEED + rank)
     fill_s = time.perf_counter() - t0
     bt.set_tokens(tokens, [B64_CTX] * nb)
-    bt.decode(warm, want_ids=False)
+    gather = None
+    if args.vocab_shard:
+        import torch.distributed as dist
+
+        bt.set_vocab_shard(rank, world)
+
+        def gather(out, inp):
+            if world > 1:
+                dist.all_gather_into_tensor(out, inp)
+            elif out.data_ptr() != inp.data_ptr():
+                out.view(inp.shape).copy_(inp)
+
+        with torch.cuda.stream(stream):
+            bt.decode_sharded(warm, gather)
+    else:
+        bt.decode(warm, want_ids=False)
     step_kernels = bt.step_kernels
 
     # timed: exactly K steps, device time with events on the engine's stream (synchronised around)
@@ -463,7 +478,11 @@ def run_b64(args, world, rank, local):
         with torch.cuda.stream(stream):
             torch.cuda._sleep(20_000_000)  # hold the stream while the host enqueues
         e0.record(stream)
-        bt.decode(args.steps, want_ids=False)
+        if args.vocab_shard:
+            with torch.cuda.stream(stream):
+                bt.decode_sharded(args.steps, gather)
+        else:
+            bt.decode(args.steps, want_ids=False)
         e1.record(stream)
         e1.synchronize()
     torch.cuda.synchronize()
@@ -480,7 +499,11 @@ def run_b64(args, world, rank, local):
     torch.cuda.synchronize()
     t0 = time.perf_counter()
     bt.set_tokens(tokens, [B64_CTX] * nb)
-    ids = bt.decode(args.steps)
+    if args.vocab_shard:
+        with torch.cuda.stream(stream):
+            ids = bt.decode_sharded(args.steps, gather)
+    else:
+        ids = bt.decode(args.steps)
     t_e2e = max_over_ranks(time.perf_counter() - t0, world)
     e2e = world * nb * args.steps / t_e2e
 
@@ -497,7 +520,10 @@ def run_b64(args, world, rank, local):
             "data": "synthetic (seeded random-init weights and context, reference runtime layout)",
             "config": {"workload": WORKLOAD_B64 if nb == B64 else WORKLOAD_B64.replace("64 independent", f"{nb} independent"),
                        "global_batch": nb * world, "seq_len": max_seq,
-                       "parallelism": f"sequences sharded: {nb} per GPU x {world} (no collective)",
+                       "parallelism": (f"sequences sharded: {nb} per GPU x {world}; LM head split by vocabulary "
+                                       f"over the {world} ranks (NCCL all-gathers of the final-norm rows and of the "
+                                       f"(index, max) pairs)") if args.vocab_shard else
+                                      f"sequences sharded: {nb} per GPU x {world} (no collective)",
                        "l2": "inputs larger than L2 (about 15.5 GB of KV plus 559 MB of weights per step)",
                        "context_fill_s": round(fill_s, 3)},
             "roofline": {"bound": "hbm", "kernel": "decode step of 64 sequences (one CUDA graph: 28 layers x "
@@ -642,6 +668,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--workload", default="b1", choices=["b1", "b64", "prefill"])
     ap.add_argument("--batch", type=int, default=B64, help="b64 workload: sequences per GPU (profiling cases)")
+    ap.add_argument("--vocab-shard", action="store_true",
+                    help="b64 workload: split the LM head by vocabulary over the ranks (NCCL all-gathers)")
     ap.add_argument("--decode-only", action="store_true",
                     help="prefill + warm-up + timed decode steps only (for profiler launch lists)")
     args = ap.parse_args()

@@ -180,6 +180,29 @@ int qd_batch_write_kv(qd_batch* b, int layer, int seq, int pos0, int count, cons
 /* Kernels one qd_batch_decode step launches (for launch accounting). */
 int qd_batch_step_kernels(const qd_batch* b);
 
+/* Vocabulary-sharded LM head of a batched step across `world` ranks (config 3 with the LM head
+ * split by vocabulary over GPUs; one batch per rank, every rank the same batch size). Per step:
+ * each rank runs its layers (qd_batch_step_layers), the ranks all-gather their final-norm rows,
+ * each rank scores its vocabulary slice [V*rank/world, V*(rank+1)/world) for every rank's rows
+ * and reduces each row to one (index, value) pair (qd_batch_step_lm_slice), the ranks all-gather
+ * the pairs, and each rank keeps the best candidate of its own rows, ties to the lowest index
+ * (qd_batch_step_merge). The collectives are the caller's (NCCL all-gather on the engine's
+ * stream, for instance); the buffers are the caller's device memory:
+ *   gather_hi, gather_lo  f16 [world * batch][hidden], 16-byte aligned; this rank's rows start at
+ *                         rank * batch (qd_batch_step_layers writes them): the all-gather's buffers
+ *   pairs_local           u32 [world * batch][2] = {index, f32 bits of the max} of this rank's slice
+ *   pairs_all             u32 [world][world * batch][2]: the all-gather of every rank's pairs_local
+ * The three step calls only enqueue on the engine's stream; qd_batch_shard_sync waits and returns
+ * the ids [steps][batch] of the steps merged since the previous sync (at most 256).
+ * Replaces, for the batch, the replicated LM head + argmax of greedyNextTokenResident
+ * (webgpu-runtime.js:580-604). */
+int qd_batch_set_vocab_shard(qd_batch* b, int rank, int world, void* gather_hi, void* gather_lo,
+                             void* pairs_local, void* pairs_all);
+int qd_batch_step_layers(qd_batch* b);
+int qd_batch_step_lm_slice(qd_batch* b);
+int qd_batch_step_merge(qd_batch* b);
+int qd_batch_shard_sync(qd_batch* b, int steps, int32_t* out_ids);
+
 /* runCustomQwenGreedyPrompt over `batch` prompts of n_prompt ids each: prefill,
  * then max_new_tokens greedy tokens per prompt. ids [batch][n_prompt], out_ids
  * [batch][max_new_tokens] (host). Uses a temporary batch of max_seq

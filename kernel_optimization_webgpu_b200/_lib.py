@@ -34,6 +34,8 @@ EXPORTS = (
     "qd_batch_create", "qd_batch_destroy", "qd_batch_size", "qd_batch_fill_context", "qd_batch_set_tokens",
     "qd_batch_positions", "qd_batch_decode", "qd_batch_prefill", "qd_batch_keep_logits", "qd_batch_logits",
     "qd_batch_read_kv", "qd_batch_write_kv", "qd_batch_step_kernels", "qd_generate_batch",
+    "qd_batch_set_vocab_shard", "qd_batch_step_layers", "qd_batch_step_lm_slice", "qd_batch_step_merge",
+    "qd_batch_shard_sync",
 )
 
 
@@ -163,6 +165,13 @@ def load(build_if_stale: bool = True):
     L.qd_batch_step_kernels.restype = i32
     L.qd_generate_batch.argtypes = [vp, i32, vp, i32, i32, vp]
     L.qd_generate_batch.restype = i32
+    L.qd_batch_set_vocab_shard.argtypes = [vp, i32, i32, vp, vp, vp, vp]
+    L.qd_batch_set_vocab_shard.restype = i32
+    for name in ("qd_batch_step_layers", "qd_batch_step_lm_slice", "qd_batch_step_merge"):
+        getattr(L, name).argtypes = [vp]
+        getattr(L, name).restype = i32
+    L.qd_batch_shard_sync.argtypes = [vp, i32, vp]
+    L.qd_batch_shard_sync.restype = i32
     _lib = L
     return L
 

@@ -52,6 +52,15 @@ struct qd_batch {
   __half *w_xh = nullptr, *w_xl = nullptr;
   __half *w_ah = nullptr, *w_al = nullptr;  // prefill: silu(gate)*up operands of the down GEMM
   int* w_tok = nullptr;
+  // vocabulary-sharded LM head (qd_batch_set_vocab_shard); gather/pair buffers are the caller's
+  int shard_rank = 0, shard_world = 0, shard_v0 = 0, shard_v1 = 0, shard_tiles = 0;
+  __half *gx_hi = nullptr, *gx_lo = nullptr;
+  uint32_t *pairs_local = nullptr, *pairs_all = nullptr;
+  void* shard_buf = nullptr;            // [world*B][tiles] (max, index) per vocabulary tile of the slice
+  float* shard_pv = nullptr;
+  uint32_t* shard_pi = nullptr;
+  cudaGraphExec_t g_layers = nullptr;   // layers + final norm + copy into the gather buffer
+  int shard_steps = 0;                  // merged steps since the last qd_batch_shard_sync
 };
 
 namespace {
@@ -170,8 +179,9 @@ void launch_attn(qd_batch* b, int l, cudaStream_t s) {
             (const float*)b->part_o, b->splits, d.NH, b->xh, b->xl);
 }
 
-// One decode step of every sequence (launch order: see batch.cuh).
-void enqueue_step(qd_batch* b, bool keep_logits, cudaStream_t s) {
+// Every layer of one decode step, then the final norm into x_hi / x_lo (launch
+// order: see batch.cuh).
+void enqueue_layers(qd_batch* b, cudaStream_t s) {
   qd_engine* e = b->e;
   const Dims d = dims(e);
   const int B = b->B;
@@ -200,6 +210,13 @@ void enqueue_step(qd_batch* b, bool keep_logits, cudaStream_t s) {
   }
   launch_ex(kb_resid_norm, dim3(B), dim3(kNormThreads), 0, s, b->h, (const float*)b->parts, b->sd, sB * d.H, (const __half*)nullptr,
          (const int*)nullptr, d.V, (const float*)e->final_norm, d.H, d.eps, b->xh, b->xl, b->errw);
+}
+
+// One decode step of every sequence: the layers, the LM head + argmax, the ids fed back.
+void enqueue_step(qd_batch* b, bool keep_logits, cudaStream_t s) {
+  const Dims d = dims(b->e);
+  const int B = b->B;
+  enqueue_layers(b, s);
   lm_head(b, b->xh, b->xl, d.H, B, keep_logits ? b->logits : nullptr, s);
   BatchState st{b->tokens, b->pos, b->out, b->step, b->max_steps};
   launch(kb_argmax_merge, dim3((B + 7) / 8), s, (const float*)b->lm_pv, (const uint32_t*)b->lm_pi, b->lm_tiles, B, st,
@@ -273,6 +290,10 @@ void drop_graphs(qd_batch* b) {
       cudaGraphExecDestroy(g);
       g = nullptr;
     }
+  if (b->g_layers) {
+    cudaGraphExecDestroy(b->g_layers);
+    b->g_layers = nullptr;
+  }
 }
 
 cudaGraphExec_t capture_step(qd_batch* b, bool keep_logits) {
@@ -305,6 +326,7 @@ void free_batch(qd_batch* b) {
   if (b->dec) cudaFree(b->dec);
   if (b->logits) cudaFree(b->logits);
   if (b->wide) cudaFree(b->wide);
+  if (b->shard_buf) cudaFree(b->shard_buf);
   if (b->pinned) cudaFreeHost(b->pinned);
   if (b->pinned_io) cudaFreeHost(b->pinned_io);
   delete b;
@@ -527,9 +549,166 @@ void prefill(qd_batch* b, const int32_t* ids, int n, int32_t* first_ids) {
   b->host_pos.assign(B, n);
 }
 
+// ---- vocabulary-sharded LM head ------------------------------------------------------
+cudaGraphExec_t capture_layers_to_gather(qd_batch* b) {
+  cudaStream_t s = b->e->stream;
+  const Dims d = dims(b->e);
+  const size_t rows_bytes = (size_t)b->B * d.H * 2;
+  const size_t off = (size_t)b->shard_rank * b->B * d.H;
+  cudaGraph_t g = nullptr;
+  QD_CK(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+  try {
+    enqueue_layers(b, s);
+    QD_CK(cudaMemcpyAsync(b->gx_hi + off, b->xh, rows_bytes, cudaMemcpyDeviceToDevice, s));
+    QD_CK(cudaMemcpyAsync(b->gx_lo + off, b->xl, rows_bytes, cudaMemcpyDeviceToDevice, s));
+  } catch (...) {
+    cudaStreamEndCapture(s, &g);
+    if (g) cudaGraphDestroy(g);
+    throw;
+  }
+  QD_CK(cudaStreamEndCapture(s, &g));
+  cudaGraphExec_t x = nullptr;
+  const cudaError_t rc = cudaGraphInstantiate(&x, g, 0);
+  cudaGraphDestroy(g);
+  QD_CK(rc);
+  return x;
+}
+
+void require_shard(const qd_batch* b) {
+  if (!b->shard_world) throw QdError{QD_E_INVALID, "no vocabulary shard set (qd_batch_set_vocab_shard)"};
+}
+
 }  // namespace
 
 extern "C" {
+
+int qd_batch_set_vocab_shard(qd_batch* b, int rank, int world, void* gather_hi, void* gather_lo, void* pairs_local,
+                             void* pairs_all) {
+  if (!b) return bfail(nullptr, QdError{QD_E_INVALID, "NULL batch"});
+  try {
+    if (world < 1 || rank < 0 || rank >= world) throw QdError{QD_E_INVALID, "rank must be 0..world-1"};
+    if (!gather_hi || !gather_lo || !pairs_local || !pairs_all) throw QdError{QD_E_INVALID, "NULL buffer"};
+    if ((reinterpret_cast<uintptr_t>(gather_hi) | reinterpret_cast<uintptr_t>(gather_lo)) & 15)
+      throw QdError{QD_E_INVALID, "gather buffers must be 16-byte aligned"};
+    const Dims d = dims(b->e);
+    if ((long long)world * b->B > 65535) throw QdError{QD_E_RANGE, "world * batch above 65535 rows"};
+    QD_CK(cudaSetDevice(b->e->dev));
+    QD_CK(cudaStreamSynchronize(b->e->stream));
+    drop_graphs(b);
+    if (b->shard_buf) {
+      cudaFree(b->shard_buf);
+      b->shard_buf = nullptr;
+    }
+    b->shard_rank = rank;
+    b->shard_world = world;
+    b->shard_v0 = (int)((long long)d.V * rank / world);
+    b->shard_v1 = (int)((long long)d.V * (rank + 1) / world);
+    b->shard_tiles = (b->shard_v1 - b->shard_v0 + kTcM - 1) / kTcM;
+    const size_t n = (size_t)world * b->B * b->shard_tiles;
+    if (cudaMalloc(&b->shard_buf, n * 8) != cudaSuccess) throw QdError{QD_E_NOMEM, "cannot allocate LM-slice partials"};
+    b->shard_pv = static_cast<float*>(b->shard_buf);
+    b->shard_pi = reinterpret_cast<uint32_t*>(b->shard_pv + n);
+    b->gx_hi = static_cast<__half*>(gather_hi);
+    b->gx_lo = static_cast<__half*>(gather_lo);
+    b->pairs_local = static_cast<uint32_t*>(pairs_local);
+    b->pairs_all = static_cast<uint32_t*>(pairs_all);
+    b->shard_steps = 0;
+    QD_CK(cudaMemsetAsync(b->step, 0, 4, b->e->stream));
+    QD_CK(cudaStreamSynchronize(b->e->stream));
+  } catch (const QdError& err) {
+    return bfail(b, err);
+  }
+  return QD_OK;
+}
+
+int qd_batch_step_layers(qd_batch* b) {
+  if (!b) return bfail(nullptr, QdError{QD_E_INVALID, "NULL batch"});
+  try {
+    require_shard(b);
+    if (b->shard_steps >= b->max_steps) throw QdError{QD_E_RANGE, "too many steps since the last qd_batch_shard_sync"};
+    for (int i = 0; i < b->B; ++i)
+      if (b->host_pos[i] < 0 || (long long)b->host_pos[i] + b->shard_steps + 1 > b->max_seq)
+        throw QdError{QD_E_RANGE, "sequence " + std::to_string(i) + ": position beyond max_seq"};
+    QD_CK(cudaSetDevice(b->e->dev));
+    if (!b->g_layers) b->g_layers = capture_layers_to_gather(b);
+    QD_CK(cudaGraphLaunch(b->g_layers, b->e->stream));
+  } catch (const QdError& err) {
+    return bfail(b, err);
+  }
+  return QD_OK;
+}
+
+int qd_batch_step_lm_slice(qd_batch* b) {
+  if (!b) return bfail(nullptr, QdError{QD_E_INVALID, "NULL batch"});
+  try {
+    require_shard(b);
+    QD_CK(cudaSetDevice(b->e->dev));
+    const Dims d = dims(b->e);
+    cudaStream_t s = b->e->stream;
+    const int rows = b->shard_world * b->B;
+    TcArgs a{};
+    a.a16 = b->e->embed + (size_t)b->shard_v0 * d.H;
+    a.a16_stride = d.H;
+    a.n_rows = b->shard_v1 - b->shard_v0;
+    a.row0 = b->shard_v0;
+    a.K = d.H;
+    a.kt_split = d.H / kTcK;
+    a.x_hi = b->gx_hi;
+    a.x_lo = b->gx_lo;
+    a.ldx = d.H;
+    a.B = rows;
+    a.part_v = b->shard_pv;
+    a.part_i = b->shard_pi;
+    a.err = b->errw;
+    launch_gemm(a, 1, kGemmF16Argmax, s);
+    BatchState none{nullptr, nullptr, nullptr, nullptr, 0};
+    launch(kb_argmax_merge, dim3((rows + 7) / 8), s, (const float*)b->shard_pv, (const uint32_t*)b->shard_pi,
+           b->shard_tiles, rows, none, b->pairs_local);
+  } catch (const QdError& err) {
+    return bfail(b, err);
+  }
+  return QD_OK;
+}
+
+int qd_batch_step_merge(qd_batch* b) {
+  if (!b) return bfail(nullptr, QdError{QD_E_INVALID, "NULL batch"});
+  try {
+    require_shard(b);
+    QD_CK(cudaSetDevice(b->e->dev));
+    cudaStream_t s = b->e->stream;
+    BatchState st{b->tokens, b->pos, b->out, b->step, b->max_steps};
+    launch(kb_shard_merge, dim3((b->B + 255) / 256), s, (const uint32_t*)b->pairs_all, b->shard_world, b->shard_rank,
+           b->B, st);
+    launch(kb_step_done, dim3(1), s, b->step);
+    b->shard_steps += 1;
+  } catch (const QdError& err) {
+    return bfail(b, err);
+  }
+  return QD_OK;
+}
+
+int qd_batch_shard_sync(qd_batch* b, int steps, int32_t* out_ids) {
+  if (!b) return bfail(nullptr, QdError{QD_E_INVALID, "NULL batch"});
+  try {
+    require_shard(b);
+    if (steps != b->shard_steps) throw QdError{QD_E_INVALID, "steps must equal the merged steps since the last sync"};
+    QD_CK(cudaSetDevice(b->e->dev));
+    cudaStream_t s = b->e->stream;
+    if (out_ids && steps) {
+      ensure_pinned(b, (size_t)steps * b->B);
+      QD_CK(cudaMemcpyAsync(b->pinned, b->out, (size_t)steps * b->B * 4, cudaMemcpyDeviceToHost, s));
+    }
+    QD_CK(cudaMemsetAsync(b->step, 0, 4, s));
+    QD_CK(cudaStreamSynchronize(s));
+    check_err(b);
+    if (out_ids && steps) std::memcpy(out_ids, b->pinned, (size_t)steps * b->B * 4);
+    for (int i = 0; i < b->B; ++i) b->host_pos[i] += steps;
+    b->shard_steps = 0;
+  } catch (const QdError& err) {
+    return bfail(b, err);
+  }
+  return QD_OK;
+}
 
 int qd_batch_create(qd_engine* e, int batch, int max_seq, qd_batch** out) {
   if (!out) return bfail(nullptr, QdError{QD_E_INVALID, "NULL out"});

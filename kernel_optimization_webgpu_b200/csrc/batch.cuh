@@ -547,6 +547,35 @@ static __global__ void __launch_bounds__(256) kb_argmax_merge(const float* part_
   pdl_trigger();
 }
 
+// Vocabulary-sharded LM head, last step: ranks r < world each hold (index, value
+// bits) pairs of every rank's rows over their vocabulary slice, all[w][row][2]
+// with row = rank * B + b. Row b of this rank takes the best of the world
+// candidates (larger value, then lower index: slices are in vocabulary order)
+// and feeds it back like kb_argmax_merge.
+static __global__ void __launch_bounds__(256) kb_shard_merge(const uint32_t* all, int world, int rank, int B,
+                                                             BatchState st) {
+  pdl_wait();
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b < B) {
+    float bv = kNegMax;
+    uint32_t bi = 0;
+    for (int w = 0; w < world; ++w) {
+      const long long o = ((long long)w * world * B + (long long)rank * B + b) * 2;
+      const uint32_t i = all[o];
+      const float v = __uint_as_float(all[o + 1]);
+      if (am_better(v, i, bv, bi)) {
+        bv = v;
+        bi = i;
+      }
+    }
+    const int s = *st.step;
+    st.tokens[b] = (int)bi;
+    st.pos[b] += 1;
+    if (s < st.max_steps) st.out[(long long)s * B + b] = (int)bi;
+  }
+  pdl_trigger();
+}
+
 static __global__ void kb_step_done(int* step) {
   pdl_wait();
   if (threadIdx.x == 0 && blockIdx.x == 0) *step += 1;

@@ -79,6 +79,7 @@ struct TcArgs {
   long long y_split;          // floats between two splits' outputs
   float* part_v;              // kTcArgmax: [B][gridDim.x] best value / row
   uint32_t* part_i;
+  int row0;                   // kTcArgmax: index of the matrix's first row (a vocabulary slice starts at row0)
   __half* y_hi;               // kTcSilu: the next GEMM's operands [B][ldy]
   __half* y_lo;
   int* err;                   // device status word (bit kTcErrTimeout)
@@ -493,7 +494,7 @@ __global__ void __launch_bounds__(kTcThreads + 32, 1) k_gemm_tc(const __grid_con
         uint32_t id[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
-          id[j] = (uint32_t)n;
+          id[j] = (uint32_t)(n + a.row0);
           if (!row_live) dm[j] = kNegMax;
         }
         warp_argmax_columns(dm, id, lane);

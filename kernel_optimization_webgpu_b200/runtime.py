@@ -109,7 +109,11 @@ class Engine:
 
     # stepping interface (enqueue only)
     def set_stream(self, stream=None) -> None:
-        """Enqueue on a torch.cuda.Stream (None: the engine's own stream)."""
+        """Enqueue on a torch.cuda.Stream (None: the engine's own stream). The legacy
+        default stream (handle 0) is refused: the C ABI reads a NULL stream as the
+        engine's own stream, which would not be ordered with work on the default one."""
+        if stream is not None and stream.cuda_stream == 0:
+            raise ValueError("pass a created torch.cuda.Stream(), not the legacy default stream")
         ptr = C.c_void_p(stream.cuda_stream) if stream is not None else None
         check(_lib.load().qd_engine_set_stream(self._h, ptr), self._h)
 
@@ -261,6 +265,72 @@ class Batch:
     @property
     def step_kernels(self) -> int:
         return int(_lib.load().qd_batch_step_kernels(self._h))
+
+    # ---- vocabulary-sharded LM head (qd_batch_set_vocab_shard) ----------------------------
+    def set_vocab_shard(self, rank: int, world: int, device=None) -> dict:
+        """Split the LM head by vocabulary over `world` ranks (this batch is rank `rank`).
+        Allocates the exchange buffers as torch CUDA tensors and returns them:
+        gather_hi / gather_lo f16 [world*batch][hidden] (this rank's rows at rank*batch),
+        pairs_local int32 [world*batch][2], pairs_all int32 [world][world*batch][2]."""
+        import torch
+
+        dev = torch.device("cuda", torch.cuda.current_device() if device is None else device)
+        rows, H = world * self.batch, self.engine.profile["hidden"]
+        bufs = {
+            "gather_hi": torch.zeros((rows, H), dtype=torch.float16, device=dev),
+            "gather_lo": torch.zeros((rows, H), dtype=torch.float16, device=dev),
+            "pairs_local": torch.zeros((rows, 2), dtype=torch.int32, device=dev),
+            "pairs_all": torch.zeros((world, rows, 2), dtype=torch.int32, device=dev),
+        }
+        check(_lib.load().qd_batch_set_vocab_shard(self._h, int(rank), int(world),
+                                                   *(C.c_void_p(bufs[k].data_ptr()) for k in
+                                                     ("gather_hi", "gather_lo", "pairs_local", "pairs_all"))))
+        self._shard = (int(rank), int(world), bufs)
+        return bufs
+
+    def step_layers(self) -> None:
+        check(_lib.load().qd_batch_step_layers(self._h))
+
+    def step_lm_slice(self) -> None:
+        check(_lib.load().qd_batch_step_lm_slice(self._h))
+
+    def step_merge(self) -> None:
+        check(_lib.load().qd_batch_step_merge(self._h))
+
+    def shard_sync(self, steps: int) -> np.ndarray:
+        out = np.zeros((max(steps, 1), self.batch), np.int32)
+        check(_lib.load().qd_batch_shard_sync(self._h, int(steps), out.ctypes.data))
+        return out[:steps]
+
+    def decode_sharded(self, steps: int, all_gather) -> np.ndarray:
+        """`steps` greedy steps with the vocabulary-sharded LM head; ids [steps][batch]
+        (see sharded_decode)."""
+        return sharded_decode(self, steps, all_gather)
+
+
+def sharded_decode(batch, steps: int, all_gather) -> np.ndarray:
+    """The per-step flow of the vocabulary-sharded LM head on one rank: layers, all-gather
+    of the final-norm rows, this rank's vocabulary slice for every row, all-gather of the
+    (index, value) pairs, merge of this rank's rows. all_gather(out, inp) gathers every
+    rank's `inp` into `out` in rank order and must be ordered on the engine's stream
+    (torch.distributed.all_gather_into_tensor on an NCCL group, called with the engine's
+    stream as torch's current stream, for instance). Returns ids [steps][batch]."""
+    rank, world, bufs = batch._shard
+    B = batch.batch
+    parts = []
+    done = 0
+    while done < steps:
+        n = min(steps - done, 256)
+        for _ in range(n):
+            batch.step_layers()
+            for key in ("gather_hi", "gather_lo"):
+                all_gather(bufs[key], bufs[key][rank * B:(rank + 1) * B])
+            batch.step_lm_slice()
+            all_gather(bufs["pairs_all"], bufs["pairs_local"])
+            batch.step_merge()
+        parts.append(batch.shard_sync(n))
+        done += n
+    return np.concatenate(parts) if parts else np.zeros((0, B), np.int32)
 
 
 def generate_batch(engine: Engine, ids, max_new: int) -> np.ndarray:

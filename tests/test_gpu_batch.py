@@ -272,3 +272,76 @@ def test_prefill_qwen_shape_config4(qwen_runtime):
             want, margins, _ = _oracle_greedy(model, ids[s].tolist(), steps, n + steps)
             got = [int(first[s])] + more[:, s].tolist()
             assert got == want, (s, got, want, margins)
+
+
+# ---- vocabulary-sharded LM head (config 3 across GPUs), ranks emulated on one GPU ---------
+
+def _emulated_shard_decode(eng, model, world, B, steps, ctx=40, max_seq=64):
+    """`world` batches on one GPU play the ranks: the all-gathers are copies between their
+    buffers, in rank order, on the engine's stream. Returns each rank's ids and the ids the
+    same batches give with the replicated LM head."""
+    stream = torch.cuda.Stream()  # the library and the copies below share this stream
+    eng.set_stream(stream)
+    rng = np.random.Generator(np.random.PCG64(11))
+    tokens = [rng.integers(0, model.vocab, size=B).astype(np.int32) for _ in range(world)]
+    want = []
+    for r in range(world):
+        with R.Batch(eng, B, max_seq) as bt:
+            bt.fill_context(ctx, 20 + r)
+            bt.set_tokens(tokens[r], [ctx] * B)
+            want.append(bt.decode(steps))
+    batches = [R.Batch(eng, B, max_seq) for _ in range(world)]
+    try:
+        bufs = []
+        for r, bt in enumerate(batches):
+            bt.fill_context(ctx, 20 + r)
+            bt.set_tokens(tokens[r], [ctx] * B)
+            bufs.append(bt.set_vocab_shard(r, world))
+        with torch.cuda.stream(stream):
+            for _ in range(steps):
+                for bt in batches:
+                    bt.step_layers()
+                for key in ("gather_hi", "gather_lo"):
+                    for dst in bufs:
+                        for r, src in enumerate(bufs):
+                            dst[key][r * B:(r + 1) * B].copy_(src[key][r * B:(r + 1) * B])
+                for bt in batches:
+                    bt.step_lm_slice()
+                for dst in bufs:
+                    for r, src in enumerate(bufs):
+                        dst["pairs_all"][r].copy_(src["pairs_local"])
+                for bt in batches:
+                    bt.step_merge()
+        got = [bt.shard_sync(steps) for bt in batches]
+        pos = [bt.positions().tolist() for bt in batches]
+    finally:
+        for bt in batches:
+            bt.close()
+        eng.set_stream(None)
+    return got, want, pos
+
+
+@pytest.mark.parametrize("world", [1, 3])
+def test_vocab_sharded_lm_head_matches_replicated(tiny, world):
+    """Each rank scores a vocabulary slice (uneven for 3 ranks: 4099 rows) for every rank's
+    rows; the merged ids equal the replicated LM head's, bit for bit."""
+    eng, model = tiny
+    B, steps, ctx = 2, 5, 40
+    got, want, pos = _emulated_shard_decode(eng, model, world, B, steps, ctx)
+    for r in range(world):
+        assert got[r].tolist() == want[r].tolist(), r
+        assert pos[r] == [ctx + steps] * B
+
+
+def test_vocab_shard_rejects_bad_requests(tiny):
+    eng, model = tiny
+    with R.Batch(eng, 2, 32) as bt:
+        with pytest.raises(R.QdError):
+            bt.step_layers()                      # no shard set
+        with pytest.raises(R.QdError):
+            bt.set_vocab_shard(2, 2)              # rank outside 0..world-1
+        bt.fill_context(4, 1)
+        bt.set_tokens([1, 2], [4, 4])
+        bt.set_vocab_shard(0, 1)
+        with pytest.raises(R.QdError):
+            bt.shard_sync(1)                      # no merged step to sync
