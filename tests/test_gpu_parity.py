@@ -189,6 +189,22 @@ def test_engine_greedy_tiny_f32_kv_matches_js_port_golden(tiny_runtime, persiste
         assert ids == g["generated"]
 
 
+@pytest.mark.parametrize("persistent", [2, 1])
+def test_engine_long_prompt_matches_oracle(tiny_runtime, tiny_model, persistent):
+    """A 300-token prompt: each attention warp walks ~19 cached positions (the K/V
+    prefetch pipeline refills in the loop), the cluster kernel splits them over its 8 CTAs."""
+    rng = np.random.Generator(np.random.PCG64(8))
+    prompt = rng.integers(0, tiny_model.vocab, size=300).tolist()
+    with R.Engine(tiny_runtime, max_seq=320, persistent=persistent) as eng:
+        assert eng.token_kernel == persistent
+        ids, _ = eng.generate_greedy(prompt, 6)
+        sess = tiny_model.session(max_seq=320, kv_f16=True)
+        want, margins = sess.greedy(prompt, 6)
+        assert ids == want, (ids, want, margins.tolist())
+        _, logits, _ = sess.next_token()
+        assert rel(eng.logits(), logits) < TOL
+
+
 def test_engine_callback_order_and_early_stop(tiny_runtime):
     seen = []
     with R.Engine(tiny_runtime, max_seq=64) as eng:
