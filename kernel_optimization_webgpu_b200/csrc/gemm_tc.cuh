@@ -471,12 +471,20 @@ __global__ void __launch_bounds__(kTcThreads + 32, 1) k_gemm_tc(const __grid_con
 #pragma unroll
       for (int j = 0; j < 32; ++j) dm[j] = (dm[j] + dc[j] * (1.0f / kLoScale)) * unscale;
       if constexpr (EPI == kTcSilu) {
+        // Lane pairs hold the gate (even lane) and up (odd lane) rows of pair n / 2.
+        // Each step finishes two activation rows: the even lane row j, the odd lane
+        // row j + 1, so that every lane computes (fast exp and divide: the result is
+        // within a few ulp of silu(g) * u).
+        const bool odd = lane & 1;
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const float up = __shfl_xor_sync(0xffffffffu, dm[j], 1);  // lane pairs: gate (even), up (odd)
-          const int b = b0 + c0 + j;
-          if ((lane & 1) == 0 && row_live && b < a.B) {
-            const float act = dm[j] / (1.0f + expf(-dm[j])) * up;
+        for (int j = 0; j < 32; j += 2) {
+          const float o0 = __shfl_xor_sync(0xffffffffu, dm[j], 1);
+          const float o1 = __shfl_xor_sync(0xffffffffu, dm[j + 1], 1);
+          const float g = odd ? o1 : dm[j];
+          const float u = odd ? dm[j + 1] : o0;
+          const int b = b0 + c0 + j + (odd ? 1 : 0);
+          if (row_live && b < a.B) {
+            const float act = __fdividef(g, 1.0f + __expf(-g)) * u;
             __half hh, ll;
             split_f16(act, hh, ll);
             a.y_hi[(long long)b * a.ldy + (n >> 1)] = hh;
