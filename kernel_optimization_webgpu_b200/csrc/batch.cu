@@ -186,7 +186,7 @@ void enqueue_layers(qd_batch* b, cudaStream_t s) {
   const Dims d = dims(e);
   const int B = b->B;
   const long long sB = B;
-  const int rope_grid = (int)std::min<long long>((sB * (d.NH + 2 * d.NKV) + 7) / 8, 4096);
+  const int rope_grid = rope_grid_for(sB * (d.NH + 2 * d.NKV), 4096);
   for (int l = 0; l < d.L; ++l) {
     const LayerDev& L = e->layers[l];
     if (l == 0)
@@ -447,7 +447,7 @@ void fill_context(qd_batch* b, int ctx, uint32_t seed) {
       // k and v rows of the fused qkv matrix
       gemm_q4(L.qkv + (size_t)d.QS * rec_bytes(d.H), d.H, 2 * d.KVS, b->w_xh, b->w_xl, R, 1, d.H / kTcK, b->w_y, s,
               b->errw);
-      const int grid = (int)std::min<long long>(((long long)R * 2 * d.NKV + 7) / 8, 8192);
+      const int grid = rope_grid_for((long long)R * 2 * d.NKV, 8192);
       launch(kb_rope_cache, dim3(grid), s, (const float*)b->w_y, 1, 0LL, R, 0, d.NKV, L.n_q, L.n_k, d.eps,
              (const float*)e->cos_t, (const float*)e->sin_t, e->opt.rope_row_stride, (const int*)nullptr, ctx, r0,
              b->max_seq, kc_of(b, l), vc_of(b, l), (float*)nullptr, b->errw);
@@ -498,7 +498,7 @@ void prefill(qd_batch* b, const int32_t* ids, int n, int32_t* first_ids) {
   const float scale = 1.0f / std::sqrt((float)kHeadDim);
   const long long layer_rows = (long long)B * d.NKV * b->max_seq;
   const int qtiles = (n + kPfTile - 1) / kPfTile;
-  const int rope_grid = (int)std::min<long long>((T * (d.NH + 2 * d.NKV) + 7) / 8, 1 << 20);
+  const int rope_grid = rope_grid_for(T * (d.NH + 2 * d.NKV), 1 << 20);
   for (int l = 0; l < d.L; ++l) {
     const LayerDev& L = e->layers[l];
     if (l == 0)

@@ -168,11 +168,15 @@ static __global__ void __launch_bounds__(kNormThreads) kb_resid_norm(float* h, c
 // (split-K partials, summed here). Row r belongs to sequence
 // seq = (row0 + r) / rows_per_seq at position
 // (pos ? pos[seq] : 0) + (row0 + r) % rows_per_seq.
-// One warp per head task: q heads are normalised, rotated and stored to q_out
-// [r][q_heads*128]; k heads normalised, rotated (rope.wgsl:14-31, table offset
-// position * row_stride + pair) and appended to the cache; v heads appended as
-// projected. Cache row (seq, g, p) sits at ((seq*NKV + g)*max_seq + p)*128.
-static __global__ void __launch_bounds__(256) kb_rope_cache(const float* parts, int nparts, long long part_stride, int R,
+// One warp per kRopeTasks consecutive head tasks: q heads are normalised,
+// rotated and stored to q_out [r][q_heads*128]; k heads normalised, rotated
+// (rope.wgsl:14-31, table offset position * row_stride + pair) and appended to
+// the cache; v heads appended as projected. Cache row (seq, g, p) sits at
+// ((seq*NKV + g)*max_seq + p)*128. The warp issues the partial loads of all
+// its tasks before the first reduction, so that kRopeTasks * 512 bytes of
+// partials per warp are in flight at once.
+constexpr int kRopeTasks = 4;
+static __global__ void __launch_bounds__(256, 3) kb_rope_cache(const float* parts, int nparts, long long part_stride, int R,
                                                      int q_heads, int NKV, const float* norm_q, const float* norm_k,
                                                      float eps, const float* cos_t, const float* sin_t, int row_stride,
                                                      const int* pos, int rows_per_seq, long long row0, int max_seq,
@@ -183,60 +187,83 @@ static __global__ void __launch_bounds__(256) kb_rope_cache(const float* parts, 
   const int ld = tasks * kHeadDim;
   const int nt = R * tasks;  // the host keeps R * tasks and row0 + R below 2^31
   const int r0 = (int)row0;
-  for (int task = blockIdx.x * 8 + warp; task < nt; task += gridDim.x * 8) {
-    const int r = task / tasks, t = task - r * tasks;
-    const int grow = r0 + r;
-    const int seq = grow / rows_per_seq;
-    const int p = (pos ? pos[seq] : 0) + (grow - seq * rows_per_seq);
-    if (p < 0 || p >= max_seq) {
-      if (lane == 0) atomicOr(err, kErrPosition);
-      continue;
+  const int pair0 = (4 * lane) & (kHeadDim / 2 - 1);
+  for (int t0 = (blockIdx.x * 8 + warp) * kRopeTasks; t0 < nt; t0 += gridDim.x * 8 * kRopeTasks) {
+    // the partials of every task first (several loads in flight), in split order
+    float4 x[kRopeTasks];
+#pragma unroll
+    for (int i = 0; i < kRopeTasks; ++i) {
+      const int task = min(t0 + i, nt - 1);
+      const int r = task / tasks, t = task - r * tasks;
+      x[i] = __ldg(reinterpret_cast<const float4*>(parts + (long long)r * ld + (long long)t * kHeadDim) + lane);
     }
-    const long long base = (long long)r * ld + (long long)t * kHeadDim + 4 * lane;
-    float4 x = *reinterpret_cast<const float4*>(parts + base);
-    for (int s = 1; s < nparts; ++s) {  // split-K partials in order (decode only: at most a few)
-      const float4 y = *reinterpret_cast<const float4*>(parts + (long long)s * part_stride + base);
-      x.x += y.x;
-      x.y += y.y;
-      x.z += y.z;
-      x.w += y.w;
+    for (int s = 1; s < nparts; ++s) {  // split-K partials (decode only: at most a few)
+#pragma unroll
+      for (int i = 0; i < kRopeTasks; ++i) {
+        const int task = min(t0 + i, nt - 1);
+        const int r = task / tasks, t = task - r * tasks;
+        const float4 y = __ldg(reinterpret_cast<const float4*>(parts + (long long)s * part_stride + (long long)r * ld +
+                                                               (long long)t * kHeadDim) + lane);
+        x[i].x += y.x;
+        x[i].y += y.y;
+        x[i].z += y.z;
+        x[i].w += y.w;
+      }
     }
-    if (t >= q_heads + NKV) {  // v: cached as projected
-      const int g = t - q_heads - NKV;
-      __half* dst = vc + (((long long)seq * NKV + g) * max_seq + p) * kHeadDim + 4 * lane;
-      reinterpret_cast<__half2*>(dst)[0] = __floats2half2_rn(x.x, x.y);
-      reinterpret_cast<__half2*>(dst)[1] = __floats2half2_rn(x.z, x.w);
-      continue;
-    }
-    const float* nw = t < q_heads ? norm_q : norm_k;
-    float ss = x.x * x.x + x.y * x.y + x.z * x.z + x.w * x.w;
-    ss = warp_sum(ss);
-    const float inv = rsqrtf(ss / (float)kHeadDim + eps);
-    const float4 w4 = reinterpret_cast<const float4*>(nw)[lane];
-    const float4 y = make_float4(x.x * inv * w4.x, x.y * inv * w4.y, x.z * inv * w4.z, x.w * inv * w4.w);
-    // rotate-half: dims d and d +- 64 sit 16 lanes apart
-    float4 pr;
-    pr.x = __shfl_xor_sync(0xffffffffu, y.x, 16);
-    pr.y = __shfl_xor_sync(0xffffffffu, y.y, 16);
-    pr.z = __shfl_xor_sync(0xffffffffu, y.z, 16);
-    pr.w = __shfl_xor_sync(0xffffffffu, y.w, 16);
-    const int pair0 = (4 * lane) & (kHeadDim / 2 - 1);
-    const long long toff = (long long)p * row_stride + pair0;
-    const float4 c = *reinterpret_cast<const float4*>(cos_t + toff);
-    const float4 s = *reinterpret_cast<const float4*>(sin_t + toff);
-    const float sg = lane < 16 ? -1.0f : 1.0f;  // first half: x*cos - x[d+64]*sin
-    const float4 o = make_float4(y.x * c.x + sg * pr.x * s.x, y.y * c.y + sg * pr.y * s.y,
-                                 y.z * c.z + sg * pr.z * s.z, y.w * c.w + sg * pr.w * s.w);
-    if (t < q_heads) {
-      reinterpret_cast<float4*>(q_out + (long long)r * q_heads * kHeadDim + (long long)t * kHeadDim)[lane] = o;
-    } else {
-      const int g = t - q_heads;
-      __half* dst = kc + (((long long)seq * NKV + g) * max_seq + p) * kHeadDim + 4 * lane;
-      reinterpret_cast<__half2*>(dst)[0] = __floats2half2_rn(o.x, o.y);
-      reinterpret_cast<__half2*>(dst)[1] = __floats2half2_rn(o.z, o.w);
+#pragma unroll
+    for (int i = 0; i < kRopeTasks; ++i) {
+      const int task = t0 + i;
+      if (task >= nt) break;
+      const int r = task / tasks, t = task - r * tasks;
+      const int grow = r0 + r;
+      const int seq = grow / rows_per_seq;
+      const int p = (pos ? pos[seq] : 0) + (grow - seq * rows_per_seq);
+      if (p < 0 || p >= max_seq) {
+        if (lane == 0) atomicOr(err, kErrPosition);
+        continue;
+      }
+      if (t >= q_heads + NKV) {  // v: cached as projected
+        const int g = t - q_heads - NKV;
+        __half* dst = vc + (((long long)seq * NKV + g) * max_seq + p) * kHeadDim + 4 * lane;
+        reinterpret_cast<__half2*>(dst)[0] = __floats2half2_rn(x[i].x, x[i].y);
+        reinterpret_cast<__half2*>(dst)[1] = __floats2half2_rn(x[i].z, x[i].w);
+        continue;
+      }
+      const long long toff = (long long)p * row_stride + pair0;
+      const float4 c = __ldg(reinterpret_cast<const float4*>(cos_t + toff));
+      const float4 sn = __ldg(reinterpret_cast<const float4*>(sin_t + toff));
+      const float4 w4 = __ldg(reinterpret_cast<const float4*>(t < q_heads ? norm_q : norm_k) + lane);
+      float ss = x[i].x * x[i].x + x[i].y * x[i].y + x[i].z * x[i].z + x[i].w * x[i].w;
+      ss = warp_sum(ss);
+      const float inv = rsqrtf(ss / (float)kHeadDim + eps);
+      const float4 y = make_float4(x[i].x * inv * w4.x, x[i].y * inv * w4.y, x[i].z * inv * w4.z, x[i].w * inv * w4.w);
+      // rotate-half: dims d and d +- 64 sit 16 lanes apart
+      float4 pr;
+      pr.x = __shfl_xor_sync(0xffffffffu, y.x, 16);
+      pr.y = __shfl_xor_sync(0xffffffffu, y.y, 16);
+      pr.z = __shfl_xor_sync(0xffffffffu, y.z, 16);
+      pr.w = __shfl_xor_sync(0xffffffffu, y.w, 16);
+      const float sg = lane < 16 ? -1.0f : 1.0f;  // first half: x*cos - x[d+64]*sin
+      const float4 o = make_float4(y.x * c.x + sg * pr.x * sn.x, y.y * c.y + sg * pr.y * sn.y,
+                                   y.z * c.z + sg * pr.z * sn.z, y.w * c.w + sg * pr.w * sn.w);
+      if (t < q_heads) {
+        reinterpret_cast<float4*>(q_out + (long long)r * q_heads * kHeadDim + (long long)t * kHeadDim)[lane] = o;
+      } else {
+        const int g = t - q_heads;
+        __half* dst = kc + (((long long)seq * NKV + g) * max_seq + p) * kHeadDim + 4 * lane;
+        reinterpret_cast<__half2*>(dst)[0] = __floats2half2_rn(o.x, o.y);
+        reinterpret_cast<__half2*>(dst)[1] = __floats2half2_rn(o.z, o.w);
+      }
     }
   }
   pdl_trigger();
+}
+
+// Grid of kb_rope_cache for nt head tasks: one warp per kRopeTasks tasks, capped
+// (the kernel strides over the rest).
+inline int rope_grid_for(long long nt, long long cap) {
+  const long long per_cta = 8LL * kRopeTasks;
+  return (int)std::max<long long>(1, std::min<long long>((nt + per_cta - 1) / per_cta, cap));
 }
 
 // ---- split-KV decode attention with TMA staging ------------------------------------
