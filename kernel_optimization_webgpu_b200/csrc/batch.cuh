@@ -37,8 +37,13 @@ constexpr int kMaxParts = 16;   // split-K partials a consumer kernel sums (GEMM
 // (128-byte rows, 128-byte swizzle), 8 KB per box.
 constexpr int kBAttnBox = kBAttnTile * 64 * 2;
 constexpr int kBAttnStage = 4 * kBAttnBox;
-// Dynamic shared memory of kb_attn: two stages plus alignment slack for the swizzle atoms.
-constexpr int kBAttnSmem = 2 * kBAttnStage + 1024;
+// K/V stages of kb_attn's ring and its dynamic shared memory (plus alignment slack
+// for the swizzle atoms). Two stages (65 KB, three CTAs per SM) measured best at
+// 64 sequences x 2048 positions: three stages (two CTAs per SM) ran 7% slower and
+// four (one CTA per SM) 30% slower; the attention warps' latency, not the bytes in
+// flight, sets the pace.
+constexpr int kBAttnStages = 2;
+constexpr int kBAttnSmem = kBAttnStages * kBAttnStage + 1024;
 
 struct BatchState {
   int* tokens;    // [B] input token of the step (the previous step's output)
@@ -292,15 +297,17 @@ __global__ void __launch_bounds__(kBAttnThreads) kb_attn(const __grid_constant__
   constexpr int kWarps = kBAttnThreads / 32;
   __shared__ __align__(16) float qsm[G][kHeadDim];
   __shared__ float wm[kWarps][G], wl[kWarps][G];
-  __shared__ unsigned long long full[2], empty[2];
+  constexpr int kS = kBAttnStages;
+  __shared__ unsigned long long full[kS], empty[kS];
   __shared__ int failed;
   const int g = blockIdx.x, sp = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (tid == 0) {
-    tc_mbar_init(&full[0]);
-    tc_mbar_init(&full[1]);
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(tc_smem(&empty[0])), "r"(kWarps) : "memory");
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(tc_smem(&empty[1])), "r"(kWarps) : "memory");
+#pragma unroll
+    for (int i = 0; i < kS; ++i) {
+      tc_mbar_init(&full[i]);
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(tc_smem(&empty[i])), "r"(kWarps) : "memory");
+    }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     tma_prefetch_map(&kvmap);
     failed = 0;
@@ -317,10 +324,10 @@ __global__ void __launch_bounds__(kBAttnThreads) kb_attn(const __grid_constant__
   }
   const long long seq_row = ((long long)b * NKV + g) * max_seq;
   const int nt = (hi - lo + kBAttnTile - 1) / kBAttnTile;
-  auto issue = [&](int t) {  // one thread: tile t into stage t & 1
+  auto issue = [&](int t) {  // one thread: tile t into stage t % kS
     const long long row = seq_row + lo + (long long)t * kBAttnTile;
-    unsigned long long* mb = &full[t & 1];
-    unsigned char* st = stages + (t & 1) * kBAttnStage;
+    unsigned long long* mb = &full[t % kS];
+    unsigned char* st = stages + (t % kS) * kBAttnStage;
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(tc_smem(mb)), "r"(kBAttnStage)
                  : "memory");
     // KV rows are read once per step: evict-first keeps the step's small tensors in L2
@@ -332,14 +339,8 @@ __global__ void __launch_bounds__(kBAttnThreads) kb_attn(const __grid_constant__
   };
   __syncthreads();  // barrier init visible
   int issued = 0;   // thread 0 only
-  if (tid == 0) {
-    issue(0);
-    issued = 1;
-    if (nt > 1) {
-      issue(1);
-      issued = 2;
-    }
-  }
+  if (tid == 0)
+    for (; issued < min(kS, nt); ++issued) issue(issued);
   for (int e = tid; e < G * kHeadDim; e += kBAttnThreads)
     qsm[e / kHeadDim][e % kHeadDim] = q[((long long)b * NH + (long long)g * G) * kHeadDim + e];
   __syncthreads();
@@ -357,17 +358,17 @@ __global__ void __launch_bounds__(kBAttnThreads) kb_attn(const __grid_constant__
   int consumed = 0;  // tiles this warp has waited for
   bool ok = true;
   for (int t = 0; t < nt && ok; ++t) {
-    const int buf = t & 1;
-    if (tid == 0 && t >= 1 && t + 1 < nt) {  // refill the stage tile t-1 used with tile t+1
-      ok = tc_mbar_wait(&empty[(t + 1) & 1], (unsigned)((t - 1) >> 1) & 1u);
+    const int buf = t % kS;
+    if (tid == 0 && t >= 1 && t - 1 + kS < nt) {  // refill the stage tile t-1 used with tile t-1+kS
+      ok = tc_mbar_wait(&empty[(t - 1) % kS], (unsigned)((t - 1) / kS) & 1u);
       if (ok) {
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        issue(t + 1);
-        issued = t + 2;
+        issue(t - 1 + kS);
+        issued = t + kS;
       }
     }
     ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-    if (ok) ok = tc_mbar_wait(&full[buf], (unsigned)(t >> 1) & 1u);
+    if (ok) ok = tc_mbar_wait(&full[buf], (unsigned)(t / kS) & 1u);
     ok = __all_sync(0xffffffffu, ok);
     if (!ok) break;
     consumed = t + 1;
@@ -448,7 +449,7 @@ __global__ void __launch_bounds__(kBAttnThreads) kb_attn(const __grid_constant__
     // Copies still in flight land in this CTA's shared memory: give each a
     // bounded chance to finish before exiting.
     if (tid == 0) {
-      for (int t = consumed; t < issued; ++t) (void)tc_mbar_wait(&full[t & 1], (unsigned)(t >> 1) & 1u);
+      for (int t = consumed; t < issued; ++t) (void)tc_mbar_wait(&full[t % kS], (unsigned)(t / kS) & 1u);
       atomicOr(err, kBErrTimeout);
     }
     pdl_trigger();
