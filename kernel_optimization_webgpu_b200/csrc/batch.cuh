@@ -753,13 +753,24 @@ __global__ void __launch_bounds__(128 * G) kb_prefill_attn(const __grid_constant
     issue(0);
     if (nkt > 1) issue(1);
   }
-  // Q tile -> f16 hi/lo, swizzled like the K boxes. Rows beyond n are zero.
-  for (int e = tid; e < G * kPfTile * 32; e += 128 * G) {  // 4 dims per item
+  // Q tile -> f16 hi/lo, swizzled like the K boxes. Rows beyond n are zero. Each
+  // thread's 16 float4 loads are all issued before the first split (one round trip).
+  constexpr int kQPer = kPfTile * 32 / 128;  // items (4 dims each) per thread: G * 64 * 32 over 128 * G threads
+  float4 qv[kQPer];
+#pragma unroll
+  for (int i = 0; i < kQPer; ++i) {
+    const int e = tid + i * 128 * G;
     const int hh = e / (kPfTile * 32), r = (e / 32) % kPfTile, d4 = e % 32;
     const int p = qt * kPfTile + r;
-    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (p < n)
-      v = *reinterpret_cast<const float4*>(q + ((long long)b * n + p) * QS + ((long long)g * G + hh) * kHeadDim + 4 * d4);
+    qv[i] = p < n ? *reinterpret_cast<const float4*>(q + ((long long)b * n + p) * QS +
+                                                      ((long long)g * G + hh) * kHeadDim + 4 * d4)
+                  : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+#pragma unroll
+  for (int i = 0; i < kQPer; ++i) {
+    const int e = tid + i * 128 * G;
+    const int hh = e / (kPfTile * 32), r = (e / 32) % kPfTile, d4 = e % 32;
+    const float4 v = qv[i];
     unsigned h01, l01, h23, l23;
     split_pair(v.x, v.y, h01, l01);
     split_pair(v.z, v.w, h23, l23);
