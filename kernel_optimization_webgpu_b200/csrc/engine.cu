@@ -938,7 +938,7 @@ void launch_gemm_t(TcArgs a, int splits, cudaStream_t s) {
   if (!ok) throw QdError{QD_E_CUDA, "GEMM tensor maps: " + err};
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((a.n_rows + kTcM - 1) / kTcM, (a.B + BN - 1) / BN, splits);
-  cfg.blockDim = dim3(kTcThreads + 32);
+  cfg.blockDim = dim3(tc_block_threads<BN, AF16>());
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];

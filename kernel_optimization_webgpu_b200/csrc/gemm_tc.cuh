@@ -16,12 +16,16 @@
 // and y = (D_main + D_corr * 2^-11) * 2^-S leave an error near 2^-22 relative
 // (the dropped lo*lo term), i.e. f32 rounding level.
 //
-// Per CTA: 128 threads. Each k-tile (64 columns = two q4 blocks) is
-// dequantised by the threads straight into the 128-byte-swizzled K-major smem
-// layout the MMA reads, the activation hi/lo tiles are copied in, and thread 0
-// issues the MMAs and commits them to the stage's mbarrier. Two stages overlap
-// the dequantisation of tile k+1 with the MMAs of tile k, and the raw weights of
-// tile k+1 are fetched into registers while tile k is written to shared memory.
+// Per CTA: 128 R consumer threads (R = 2, or 4 for the prefill tile BN = 256)
+// and one producer warp. Each k-tile (64 columns = two q4 blocks) is dequantised
+// by R threads per weight row straight into the 128-byte-swizzled K-major smem
+// layout the MMA reads, the activation hi/lo tiles are copied in by TMA, and
+// thread 0 issues the MMAs and commits them to the stage's mbarrier. A double-
+// buffered A stage overlaps the dequantisation of tile k+1 with the MMAs of tile k.
+// The dequantise -> barrier -> MMA-issue chain of a k-tile is what keeps the tensor
+// pipe waiting, so it is spread over as many threads as the block allows
+// (prefill, 32 x 512 prompt rows: 235k prompt tok/s with one thread per row,
+// 271k with two, 284k with four).
 //
 // Split-K: gridDim.z CTAs share a row tile, each over its own run of k-tiles,
 // and store partial sums [split][B][N]; the kernel that consumes the result
@@ -39,7 +43,6 @@
 
 namespace qd {
 
-constexpr int kTcThreads = 128;
 constexpr int kTcM = 128;            // weight rows per CTA (UMMA M)
 constexpr int kTcK = 64;             // k-tile: one 128-byte swizzle row of f16
 constexpr int kWShift = 10;          // weights are scaled by 2^10 into the f16 normal range (|scale| <= 8)
@@ -201,18 +204,38 @@ __device__ __forceinline__ void warp_argmax_columns(float (&v)[32], uint32_t (&i
   }
 }
 
-// Reduction barrier over the 128 consumer threads (named barrier 1): true if
+// Reduction barrier over the `count` consumer threads (named barrier 1): true if
 // any thread passes `pred`.
-__device__ __forceinline__ bool consumers_any(bool pred) {
+__device__ __forceinline__ bool consumers_any(bool pred, int count) {
   unsigned r;
   asm volatile(
       "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.or.pred q, 1, %2, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
       : "=r"(r)
-      : "r"((unsigned)pred), "r"(kTcThreads)
+      : "r"((unsigned)pred), "r"(count)
       : "memory");
   return r != 0;
 }
 
+// Consumer threads per weight row: each dequantises 8 / R of the row's eight
+// nibble words of a k-tile (R = 2: one q4 block each). More threads shorten the
+// dequantise -> barrier -> MMA-issue chain of every k-tile, which otherwise leaves
+// the tensor pipe idle between k-tiles.
+template <int BN, bool AF16>
+__host__ __device__ constexpr int tc_row_threads() {
+  return (!AF16 && BN == 256) ? 4 : 2;
+}
+template <int BN, bool AF16>
+__host__ __device__ constexpr int tc_consumers() {
+  return kTcM * tc_row_threads<BN, AF16>();
+}
+template <int BN, bool AF16>
+__host__ __device__ constexpr int tc_block_threads() {  // consumers + the producer warp
+  return tc_consumers<BN, AF16>() + 32;
+}
+template <int BN, bool AF16>
+__host__ __device__ constexpr int tc_min_blocks() {  // q4 at BN = 64 (decode) runs two CTAs per SM
+  return (!AF16 && BN <= 64) ? 2 : 1;
+}
 template <int BN, bool AF16>
 __host__ __device__ constexpr int tc_stages() {
   // q4 at BN = 64 (decode): two stages keep the CTA at ~105 KB so two fit per SM
@@ -227,16 +250,21 @@ __host__ __device__ constexpr int tc_smem_total() {
   return tc_stages<BN, AF16>() * tc_stage_bytes<BN, AF16>() + (AF16 ? 0 : 2 * 2 * kTcM * kTcK * 2) + 1024;
 }
 
-// Grid: (ceil(n_rows / 128), ceil(B / BN), splits); 160 threads. Split z covers
-// k-tiles [z * kt_split, min((z + 1) * kt_split, K / 64)).
-// Warp 4 is the producer: one lane streams each k-tile's weights (raw q4
+// Grid: (ceil(n_rows / 128), ceil(B / BN), splits); 128 R + 32 threads. Split z
+// covers k-tiles [z * kt_split, min((z + 1) * kt_split, K / 64)).
+// The last warp is the producer: one lane streams each k-tile's weights (raw q4
 // nibbles, or the f16 table tile) and the x_hi / x_lo tiles into a ring of S
 // stages by TMA, refilling a stage when the MMAs that read it have committed
-// to its "empty" barrier. Warps 0-3 dequantise the nibbles (thread = weight
-// row) into a double-buffered A_hi / A_lo stage; thread 0 then issues the MMAs.
-// The same four warps run the epilogue from TMEM.
+// to its "empty" barrier. The 128 R consumer threads dequantise the nibbles
+// (R threads per weight row, each 8 / R words of it) into a double-buffered
+// A_hi / A_lo stage; thread 0 then issues the MMAs. The consumer warps run the
+// epilogue from TMEM: warp w reads lane quarter w % 4 (the hardware's rule) and
+// its share of the columns.
 template <int BN, bool AF16, int EPI>
-__global__ void __launch_bounds__(kTcThreads + 32, 1) k_gemm_tc(const __grid_constant__ TcArgs a) {
+__global__ void __launch_bounds__(tc_block_threads<BN, AF16>(), tc_min_blocks<BN, AF16>()) k_gemm_tc(const __grid_constant__ TcArgs a) {
+  constexpr int R = tc_row_threads<BN, AF16>();
+  constexpr int kCons = tc_consumers<BN, AF16>();
+  constexpr int kWords = 8 / R;  // nibble words (8 columns each) per consumer thread and k-tile
   constexpr int S = tc_stages<BN, AF16>();
   constexpr int kW = AF16 ? kTcM * kTcK * 2 : kTcM * 32;
   constexpr int kBt = BN * kTcK * 2;
@@ -282,7 +310,7 @@ __global__ void __launch_bounds__(kTcThreads + 32, 1) k_gemm_tc(const __grid_con
   tc_fence_after();
   const unsigned tmem = tmem_base;
 
-  if (warp == kTcThreads / 32) {
+  if (warp == kCons / 32) {
     // ---- producer ----
     if (lane == 0) {
       tma_prefetch_map(&a.tm_w);
@@ -344,7 +372,10 @@ __global__ void __launch_bounds__(kTcThreads + 32, 1) k_gemm_tc(const __grid_con
     // ---- consumers: dequantisation, MMA issue, epilogue ----
     pdl_wait();
     const unsigned idesc = umma_idesc_f16_f32(kTcM, BN);
-    const int n = n0 + tid;
+    // Thread (row, part): weight row n0 + row, words [part * kWords, (part + 1) * kWords)
+    // of every k-tile (the q4 block of word j is j / 4).
+    const int row = tid & (kTcM - 1), part = tid >> 7;
+    const int n = n0 + row;
     const bool row_live = n < a.n_rows;
     uint32_t sc_cur = 0, sc_next = 0;
     if constexpr (!AF16) {
@@ -365,20 +396,31 @@ __global__ void __launch_bounds__(kTcThreads + 32, 1) k_gemm_tc(const __grid_con
         unsigned char* A_hi = abuf + st * 2 * kA;
         unsigned char* A_lo = A_hi + kA;
         if (ok) {
-          const uint4* raw = reinterpret_cast<const uint4*>(stg + tid * 32);
-          const uint4 q0 = raw[0], q1 = raw[1];
-          const uint32_t ws[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+          uint32_t ws[kWords];
+          if constexpr (kWords == 4) {
+            const uint4 q0 = reinterpret_cast<const uint4*>(stg + row * 32)[part];
+            ws[0] = q0.x;
+            ws[1] = q0.y;
+            ws[2] = q0.z;
+            ws[3] = q0.w;
+          } else {
+            static_assert(kWords == 2, "2 or 4 consumer threads per row");
+            const uint2 q0 = reinterpret_cast<const uint2*>(stg + row * 32)[part];
+            ws[0] = q0.x;
+            ws[1] = q0.y;
+          }
           // f16x2 arithmetic, exact: q = n - 8 from the biased pattern 0x6400 | n (1024 + n);
           // hi = q * s' (s' = scale * 2^10, exact in f16) rounded once, as f32 math then a
           // round to f16 would; lo = (q * s' - hi) * 2^11 with the residual from one fma.
           const __half2 s2 = *reinterpret_cast<const __half2*>(&sc_cur);
           const __half2 k1024 = __float2half2_rn(1024.0f), bias = __float2half2_rn(1032.0f);
           const __half2 k2048 = __float2half2_rn(kLoScale);
-          const __half2 sa = __hmul2(__low2half2(s2), k1024), sb = __hmul2(__high2half2(s2), k1024);
+          const bool blk1 = part * kWords >= 4;  // this thread's words lie in the k-tile's second q4 block
+          const __half2 scl = __hmul2(blk1 ? __high2half2(s2) : __low2half2(s2), k1024);
 #pragma unroll
-          for (int wi = 0; wi < 8; ++wi) {  // 8 columns per word -> one 16-byte chunk of f16
-            const uint32_t w = ws[wi];
-            const __half2 scl = wi < 4 ? sa : sb;
+          for (int wl = 0; wl < kWords; ++wl) {  // 8 columns per word -> one 16-byte chunk of f16
+            const int wi = part * kWords + wl;   // word of the row's k-tile
+            const uint32_t w = ws[wl];
             uint32_t hi_p[4], lo_p[4];
 #pragma unroll
             for (int i = 0; i < 4; ++i) {  // pair i = columns (i, i + 4) of the word
@@ -394,7 +436,7 @@ __global__ void __launch_bounds__(kTcThreads + 32, 1) k_gemm_tc(const __grid_con
                                        __byte_perm(hi_p[0], hi_p[1], 0x7632), __byte_perm(hi_p[2], hi_p[3], 0x7632));
             const uint4 Lo = make_uint4(__byte_perm(lo_p[0], lo_p[1], 0x5410), __byte_perm(lo_p[2], lo_p[3], 0x5410),
                                         __byte_perm(lo_p[0], lo_p[1], 0x7632), __byte_perm(lo_p[2], lo_p[3], 0x7632));
-            const unsigned off = sw128_off(tid, wi * 8);
+            const unsigned off = sw128_off(row, wi * 8);
             *reinterpret_cast<uint4*>(A_hi + off) = H;
             *reinterpret_cast<uint4*>(A_lo + off) = Lo;
           }
@@ -403,7 +445,7 @@ __global__ void __launch_bounds__(kTcThreads + 32, 1) k_gemm_tc(const __grid_con
             sc_next = *reinterpret_cast<const uint32_t*>(a.s + (long long)n * a.s_stride + (kt0 + i + 2) * 4);
         }
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        if (consumers_any(!ok)) {
+        if (consumers_any(!ok, kCons)) {
           ok = false;
           break;
         }
@@ -449,22 +491,28 @@ __global__ void __launch_bounds__(kTcThreads + 32, 1) k_gemm_tc(const __grid_con
     // Wait for the last MMAs (they complete in order).
     if (tid == 0 && committed >= 0)
       ok = tc_mbar_wait(&adone[committed & 1], (unsigned)(committed >> 1) & 1u) && ok;
-    if (consumers_any(!ok) || (tid == 0 && committed != nk - 1)) ok = false;
+    if (consumers_any(!ok, kCons) || (tid == 0 && committed != nk - 1)) ok = false;
     if (!ok && tid == 0) atomicOr(&failed, 1);
   }
   __syncthreads();
   tc_fence_after();
   pdl_trigger();
 
-  if (tid < kTcThreads && !failed) {
-    // Epilogue: warp w reads TMEM lanes 32w..32w+31 = weight rows n0 + 32w + lane.
-    const int n = n0 + warp * 32 + lane;
+  if (tid < kCons && !failed) {
+    // Epilogue: warp w reads TMEM lanes 32 (w % 4) .. + 31 = weight rows n0 + 32 (w % 4)
+    // + lane, columns [cp * kCols, (cp + 1) * kCols) with cp = w / 4 (column parts of
+    // at least 32 columns; warps beyond the parts only join the barrier below).
+    constexpr int kParts = (R < BN / 32) ? R : BN / 32;
+    constexpr int kCols = BN / kParts;
+    static_assert(kCols % 32 == 0, "column parts are whole 32-column steps");
+    const int quarter = warp & 3, cp = warp >> 2;
+    const int n = n0 + quarter * 32 + lane;
     const bool row_live = n < a.n_rows;
-    const unsigned lane_base = (unsigned)(warp * 32) << 16;
+    const unsigned lane_base = (unsigned)(quarter * 32) << 16;
     const float unscale = AF16 ? 1.0f : 1.0f / (float)(1 << kWShift);
     float* y = a.y ? a.y + (long long)blockIdx.z * a.y_split : nullptr;
 #pragma unroll 1
-    for (int c0 = 0; c0 < BN; c0 += 32) {
+    for (int c0 = cp * kCols; c0 < (cp + 1) * kCols && cp < kParts; c0 += 32) {
       float dm[32], dc[32];
       tmem_ld32(tmem + lane_base + c0, dm);
       tmem_ld32(tmem + lane_base + BN + c0, dc);
@@ -506,13 +554,13 @@ __global__ void __launch_bounds__(kTcThreads + 32, 1) k_gemm_tc(const __grid_con
           if (!row_live) dm[j] = kNegMax;
         }
         warp_argmax_columns(dm, id, lane);
-        red_v[warp][c0 + lane] = dm[0];
-        red_i[warp][c0 + lane] = id[0];
+        red_v[quarter][c0 + lane] = dm[0];
+        red_i[quarter][c0 + lane] = id[0];
       }
     }
     if constexpr (EPI == kTcArgmax) {
-      asm volatile("bar.sync 1, %0;" ::"r"(kTcThreads) : "memory");
-      for (int j = tid; j < BN; j += kTcThreads) {
+      asm volatile("bar.sync 1, %0;" ::"r"(kCons) : "memory");
+      for (int j = tid; j < BN; j += kCons) {
         const int b = b0 + j;
         if (b >= a.B) continue;
         float bv = red_v[0][j];
