@@ -25,7 +25,7 @@
 // The dequantise -> barrier -> MMA-issue chain of a k-tile is what keeps the tensor
 // pipe waiting, so it is spread over as many threads as the block allows
 // (prefill, 32 x 512 prompt rows: 235k prompt tok/s with one thread per row,
-// 271k with two, 284k with four).
+// 271k with two, 284k with four; 294k once a warp of its own issues the MMAs).
 //
 // Split-K: gridDim.z CTAs share a row tile, each over its own run of k-tiles,
 // and store partial sums [split][B][N]; the kernel that consumes the result
@@ -204,18 +204,6 @@ __device__ __forceinline__ void warp_argmax_columns(float (&v)[32], uint32_t (&i
   }
 }
 
-// Reduction barrier over the `count` consumer threads (named barrier 1): true if
-// any thread passes `pred`.
-__device__ __forceinline__ bool consumers_any(bool pred, int count) {
-  unsigned r;
-  asm volatile(
-      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.or.pred q, 1, %2, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
-      : "=r"(r)
-      : "r"((unsigned)pred), "r"(count)
-      : "memory");
-  return r != 0;
-}
-
 // Consumer threads per weight row: each dequantises 8 / R of the row's eight
 // nibble words of a k-tile (R = 2: one q4 block each). More threads shorten the
 // dequantise -> barrier -> MMA-issue chain of every k-tile, which otherwise leaves
@@ -229,8 +217,8 @@ __host__ __device__ constexpr int tc_consumers() {
   return kTcM * tc_row_threads<BN, AF16>();
 }
 template <int BN, bool AF16>
-__host__ __device__ constexpr int tc_block_threads() {  // consumers + the producer warp
-  return tc_consumers<BN, AF16>() + 32;
+__host__ __device__ constexpr int tc_block_threads() {  // consumers + the producer warp + the MMA-issuer warp
+  return tc_consumers<BN, AF16>() + 64;
 }
 template <int BN, bool AF16>
 __host__ __device__ constexpr int tc_min_blocks() {  // q4 at BN = 64 (decode) runs two CTAs per SM
@@ -250,16 +238,18 @@ __host__ __device__ constexpr int tc_smem_total() {
   return tc_stages<BN, AF16>() * tc_stage_bytes<BN, AF16>() + (AF16 ? 0 : 2 * 2 * kTcM * kTcK * 2) + 1024;
 }
 
-// Grid: (ceil(n_rows / 128), ceil(B / BN), splits); 128 R + 32 threads. Split z
+// Grid: (ceil(n_rows / 128), ceil(B / BN), splits); 128 R + 64 threads. Split z
 // covers k-tiles [z * kt_split, min((z + 1) * kt_split, K / 64)).
-// The last warp is the producer: one lane streams each k-tile's weights (raw q4
+// Warp 4R is the producer: one lane streams each k-tile's weights (raw q4
 // nibbles, or the f16 table tile) and the x_hi / x_lo tiles into a ring of S
 // stages by TMA, refilling a stage when the MMAs that read it have committed
 // to its "empty" barrier. The 128 R consumer threads dequantise the nibbles
 // (R threads per weight row, each 8 / R words of it) into a double-buffered
-// A_hi / A_lo stage; thread 0 then issues the MMAs. The consumer warps run the
-// epilogue from TMEM: warp w reads lane quarter w % 4 (the hardware's rule) and
-// its share of the columns.
+// A_hi / A_lo stage and arrive on its "afull" barrier; one lane of warp 4R + 1
+// issues the MMAs of a k-tile once its A stage and activation tiles are in, so
+// no CTA barrier sits between the k-tiles. The consumer warps run the epilogue
+// from TMEM: warp w reads lane quarter w % 4 (the hardware's rule) and its share
+// of the columns.
 template <int BN, bool AF16, int EPI>
 __global__ void __launch_bounds__(tc_block_threads<BN, AF16>(), tc_min_blocks<BN, AF16>()) k_gemm_tc(const __grid_constant__ TcArgs a) {
   constexpr int R = tc_row_threads<BN, AF16>();
@@ -275,7 +265,8 @@ __global__ void __launch_bounds__(tc_block_threads<BN, AF16>(), tc_min_blocks<BN
       reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   unsigned char* abuf = ring + S * kStage;  // q4: [2][A_hi | A_lo]
   // full_w: the stage's weight tile landed; full_b: its x_hi / x_lo tiles landed
-  __shared__ unsigned long long full_w[S], full_b[S], empty[S], adone[2];
+  // afull: the consumers' A tile of the buffer is written (q4); adone: the MMAs that read it are done
+  __shared__ unsigned long long full_w[S], full_b[S], empty[S], adone[2], afull[2];
   __shared__ unsigned tmem_base;
   __shared__ float red_v[EPI == kTcArgmax ? 4 : 1][EPI == kTcArgmax ? BN : 1];
   __shared__ uint32_t red_i[EPI == kTcArgmax ? 4 : 1][EPI == kTcArgmax ? BN : 1];
@@ -302,6 +293,8 @@ __global__ void __launch_bounds__(tc_block_threads<BN, AF16>(), tc_min_blocks<BN
     }
     tc_mbar_init(&adone[0]);
     tc_mbar_init(&adone[1]);
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(tc_smem(&afull[0])), "r"(kCons) : "memory");
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(tc_smem(&afull[1])), "r"(kCons) : "memory");
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     failed = 0;
   }
@@ -368,131 +361,129 @@ __global__ void __launch_bounds__(tc_block_threads<BN, AF16>(), tc_min_blocks<BN
           (void)tc_mbar_wait(&full_b[i], (unsigned)(last[i] / S) & 1u);
         }
     }
-  } else {
-    // ---- consumers: dequantisation, MMA issue, epilogue ----
+  } else if (warp == kCons / 32 + 1) {
+    // ---- MMA issuer (one lane) ----
+    if (lane == 0) {
+      const unsigned idesc = umma_idesc_f16_f32(kTcM, BN);
+      bool ok = true;
+      int committed = -1;  // last tile whose MMAs were committed
+      for (int i = 0; i < nk; ++i) {
+        const int slot = i % S, st = i & 1;
+        unsigned char* stg = ring + slot * kStage;
+        // q4: the consumers' dequantised A tile of k-tile i (all of them arrived on afull);
+        // the f16 table: its TMA tile. Then the activation tiles.
+        if constexpr (!AF16) ok = tc_mbar_wait(&afull[st], (unsigned)(i >> 1) & 1u);
+        else ok = tc_mbar_wait(&full_w[slot], (unsigned)(i / S) & 1u);
+        ok = ok && tc_mbar_wait(&full_b[slot], (unsigned)(i / S) & 1u);
+        if (!ok) break;
+        tc_fence_after();
+#pragma unroll
+        for (int ks = 0; ks < kTcK / 16; ++ks) {
+          const unsigned long long dbh = umma_desc_k_sw128(tc_smem(stg + kW) + ks * 32);
+          const unsigned long long dbl = umma_desc_k_sw128(tc_smem(stg + kW + kBt) + ks * 32);
+          const bool acc = i > 0 || ks > 0;
+          if constexpr (!AF16) {
+            const unsigned char* A_hi = abuf + st * 2 * kA;
+            const unsigned long long dah = umma_desc_k_sw128(tc_smem(A_hi) + ks * 32);
+            const unsigned long long dal = umma_desc_k_sw128(tc_smem(A_hi + kA) + ks * 32);
+            umma_f16(tmem, dah, dbh, idesc, acc);
+            umma_f16(tmem + BN, dah, dbl, idesc, acc);
+            umma_f16(tmem + BN, dal, dbh, idesc, true);
+          } else {
+            const unsigned long long da = umma_desc_k_sw128(tc_smem(stg) + ks * 32);
+            umma_f16(tmem, da, dbh, idesc, acc);
+            umma_f16(tmem + BN, da, dbl, idesc, acc);
+          }
+        }
+        umma_commit(&empty[slot]);
+        umma_commit(&adone[st]);
+        committed = i;
+      }
+      // Wait for the last MMAs (they complete in order).
+      if (committed >= 0) ok = tc_mbar_wait(&adone[committed & 1], (unsigned)(committed >> 1) & 1u) && ok;
+      if (!ok || committed != nk - 1) atomicOr(&failed, 1);
+    }
+  } else if constexpr (!AF16) {
+    // ---- consumers: dequantisation of every k-tile's weights into the A stage ----
     pdl_wait();
-    const unsigned idesc = umma_idesc_f16_f32(kTcM, BN);
     // Thread (row, part): weight row n0 + row, words [part * kWords, (part + 1) * kWords)
     // of every k-tile (the q4 block of word j is j / 4).
     const int row = tid & (kTcM - 1), part = tid >> 7;
     const int n = n0 + row;
     const bool row_live = n < a.n_rows;
     uint32_t sc_cur = 0, sc_next = 0;
-    if constexpr (!AF16) {
+    {
       const char* srow = a.s + (long long)(row_live ? n : 0) * a.s_stride;
       if (row_live) {
         sc_cur = *reinterpret_cast<const uint32_t*>(srow + kt0 * 4);
         if (nk > 1) sc_next = *reinterpret_cast<const uint32_t*>(srow + (kt0 + 1) * 4);
       }
     }
-    bool ok = true;
-    int committed = -1;  // thread 0: last tile whose MMAs were committed
     for (int i = 0; i < nk; ++i) {
       const int slot = i % S, st = i & 1;
       unsigned char* stg = ring + slot * kStage;
-      if constexpr (!AF16) {
-        ok = tc_mbar_wait(&full_w[slot], (unsigned)(i / S) & 1u) && ok;
-        if (i >= 2) ok = tc_mbar_wait(&adone[st], (unsigned)((i - 2) >> 1) & 1u) && ok;
-        unsigned char* A_hi = abuf + st * 2 * kA;
-        unsigned char* A_lo = A_hi + kA;
-        if (ok) {
-          uint32_t ws[kWords];
-          if constexpr (kWords == 4) {
-            const uint4 q0 = reinterpret_cast<const uint4*>(stg + row * 32)[part];
-            ws[0] = q0.x;
-            ws[1] = q0.y;
-            ws[2] = q0.z;
-            ws[3] = q0.w;
-          } else {
-            static_assert(kWords == 2, "2 or 4 consumer threads per row");
-            const uint2 q0 = reinterpret_cast<const uint2*>(stg + row * 32)[part];
-            ws[0] = q0.x;
-            ws[1] = q0.y;
-          }
-          // f16x2 arithmetic, exact: q = n - 8 from the biased pattern 0x6400 | n (1024 + n);
-          // hi = q * s' (s' = scale * 2^10, exact in f16) rounded once, as f32 math then a
-          // round to f16 would; lo = (q * s' - hi) * 2^11 with the residual from one fma.
-          const __half2 s2 = *reinterpret_cast<const __half2*>(&sc_cur);
-          const __half2 k1024 = __float2half2_rn(1024.0f), bias = __float2half2_rn(1032.0f);
-          const __half2 k2048 = __float2half2_rn(kLoScale);
-          const bool blk1 = part * kWords >= 4;  // this thread's words lie in the k-tile's second q4 block
-          const __half2 scl = __hmul2(blk1 ? __high2half2(s2) : __low2half2(s2), k1024);
-#pragma unroll
-          for (int wl = 0; wl < kWords; ++wl) {  // 8 columns per word -> one 16-byte chunk of f16
-            const int wi = part * kWords + wl;   // word of the row's k-tile
-            const uint32_t w = ws[wl];
-            uint32_t hi_p[4], lo_p[4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {  // pair i = columns (i, i + 4) of the word
-              const uint32_t bits = ((w >> (4 * i)) & 0x000F000Fu) | 0x64006400u;
-              const __half2 q = __hsub2(*reinterpret_cast<const __half2*>(&bits), bias);
-              const __half2 h = __hmul2(q, scl);
-              const __half2 l = __hmul2(__hfma2(q, scl, __hneg2(h)), k2048);
-              hi_p[i] = *reinterpret_cast<const uint32_t*>(&h);
-              lo_p[i] = *reinterpret_cast<const uint32_t*>(&l);
-            }
-            // back to column order: (c0,c1) (c2,c3) (c4,c5) (c6,c7)
-            const uint4 H = make_uint4(__byte_perm(hi_p[0], hi_p[1], 0x5410), __byte_perm(hi_p[2], hi_p[3], 0x5410),
-                                       __byte_perm(hi_p[0], hi_p[1], 0x7632), __byte_perm(hi_p[2], hi_p[3], 0x7632));
-            const uint4 Lo = make_uint4(__byte_perm(lo_p[0], lo_p[1], 0x5410), __byte_perm(lo_p[2], lo_p[3], 0x5410),
-                                        __byte_perm(lo_p[0], lo_p[1], 0x7632), __byte_perm(lo_p[2], lo_p[3], 0x7632));
-            const unsigned off = sw128_off(row, wi * 8);
-            *reinterpret_cast<uint4*>(A_hi + off) = H;
-            *reinterpret_cast<uint4*>(A_lo + off) = Lo;
-          }
-          sc_cur = sc_next;
-          if (row_live && i + 2 < nk)
-            sc_next = *reinterpret_cast<const uint32_t*>(a.s + (long long)n * a.s_stride + (kt0 + i + 2) * 4);
-        }
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        if (consumers_any(!ok, kCons)) {
-          ok = false;
-          break;
-        }
-        if (tid == 0 && (ok = tc_mbar_wait(&full_b[slot], (unsigned)(i / S) & 1u))) {
-          tc_fence_after();
-#pragma unroll
-          for (int ks = 0; ks < kTcK / 16; ++ks) {
-            const unsigned long long dah = umma_desc_k_sw128(tc_smem(A_hi) + ks * 32);
-            const unsigned long long dal = umma_desc_k_sw128(tc_smem(A_lo) + ks * 32);
-            const unsigned long long dbh = umma_desc_k_sw128(tc_smem(stg + kW) + ks * 32);
-            const unsigned long long dbl = umma_desc_k_sw128(tc_smem(stg + kW + kBt) + ks * 32);
-            const bool acc = i > 0 || ks > 0;
-            umma_f16(tmem, dah, dbh, idesc, acc);
-            umma_f16(tmem + BN, dah, dbl, idesc, acc);
-            umma_f16(tmem + BN, dal, dbh, idesc, true);
-          }
-          umma_commit(&empty[slot]);
-          umma_commit(&adone[st]);
-          committed = i;
-        }
-      } else {
-        if (tid == 0) {  // the table tile arrives ready to use: only the MMAs to issue
-          if (!tc_mbar_wait(&full_w[slot], (unsigned)(i / S) & 1u) || !tc_mbar_wait(&full_b[slot], (unsigned)(i / S) & 1u)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-#pragma unroll
-          for (int ks = 0; ks < kTcK / 16; ++ks) {
-            const unsigned long long da = umma_desc_k_sw128(tc_smem(stg) + ks * 32);
-            const unsigned long long dbh = umma_desc_k_sw128(tc_smem(stg + kW) + ks * 32);
-            const unsigned long long dbl = umma_desc_k_sw128(tc_smem(stg + kW + kBt) + ks * 32);
-            const bool acc = i > 0 || ks > 0;
-            umma_f16(tmem, da, dbh, idesc, acc);
-            umma_f16(tmem + BN, da, dbl, idesc, acc);
-          }
-          umma_commit(&empty[slot]);
-          umma_commit(&adone[st]);
-          committed = i;
-        }
+      // the weight tile landed, and the MMAs that last read this A buffer (tile i - 2) are done
+      bool ok = tc_mbar_wait(&full_w[slot], (unsigned)(i / S) & 1u);
+      if (ok && i >= 2) ok = tc_mbar_wait(&adone[st], (unsigned)((i - 2) >> 1) & 1u);
+      if (!ok) {  // the issuer then times out on afull and records the failure as well
+        atomicOr(&failed, 1);
+        break;
       }
+      unsigned char* A_hi = abuf + st * 2 * kA;
+      unsigned char* A_lo = A_hi + kA;
+      uint32_t ws[kWords];
+      if constexpr (kWords == 4) {
+        const uint4 q0 = reinterpret_cast<const uint4*>(stg + row * 32)[part];
+        ws[0] = q0.x;
+        ws[1] = q0.y;
+        ws[2] = q0.z;
+        ws[3] = q0.w;
+      } else {
+        static_assert(kWords == 2, "2 or 4 consumer threads per row");
+        const uint2 q0 = reinterpret_cast<const uint2*>(stg + row * 32)[part];
+        ws[0] = q0.x;
+        ws[1] = q0.y;
+      }
+      // f16x2 arithmetic, exact: q = n - 8 from the biased pattern 0x6400 | n (1024 + n);
+      // hi = q * s' (s' = scale * 2^10, exact in f16) rounded once, as f32 math then a
+      // round to f16 would; lo = (q * s' - hi) * 2^11 with the residual from one fma.
+      const __half2 s2 = *reinterpret_cast<const __half2*>(&sc_cur);
+      const __half2 k1024 = __float2half2_rn(1024.0f), bias = __float2half2_rn(1032.0f);
+      const __half2 k2048 = __float2half2_rn(kLoScale);
+      const bool blk1 = part * kWords >= 4;  // this thread's words lie in the k-tile's second q4 block
+      const __half2 scl = __hmul2(blk1 ? __high2half2(s2) : __low2half2(s2), k1024);
+#pragma unroll
+      for (int wl = 0; wl < kWords; ++wl) {  // 8 columns per word -> one 16-byte chunk of f16
+        const int wi = part * kWords + wl;   // word of the row's k-tile
+        const uint32_t w = ws[wl];
+        uint32_t hi_p[4], lo_p[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {  // pair i = columns (i, i + 4) of the word
+          const uint32_t bits = ((w >> (4 * i)) & 0x000F000Fu) | 0x64006400u;
+          const __half2 q = __hsub2(*reinterpret_cast<const __half2*>(&bits), bias);
+          const __half2 h = __hmul2(q, scl);
+          const __half2 l = __hmul2(__hfma2(q, scl, __hneg2(h)), k2048);
+          hi_p[i] = *reinterpret_cast<const uint32_t*>(&h);
+          lo_p[i] = *reinterpret_cast<const uint32_t*>(&l);
+        }
+        // back to column order: (c0,c1) (c2,c3) (c4,c5) (c6,c7)
+        const uint4 H = make_uint4(__byte_perm(hi_p[0], hi_p[1], 0x5410), __byte_perm(hi_p[2], hi_p[3], 0x5410),
+                                   __byte_perm(hi_p[0], hi_p[1], 0x7632), __byte_perm(hi_p[2], hi_p[3], 0x7632));
+        const uint4 Lo = make_uint4(__byte_perm(lo_p[0], lo_p[1], 0x5410), __byte_perm(lo_p[2], lo_p[3], 0x5410),
+                                    __byte_perm(lo_p[0], lo_p[1], 0x7632), __byte_perm(lo_p[2], lo_p[3], 0x7632));
+        const unsigned off = sw128_off(row, wi * 8);
+        *reinterpret_cast<uint4*>(A_hi + off) = H;
+        *reinterpret_cast<uint4*>(A_lo + off) = Lo;
+      }
+      sc_cur = sc_next;
+      if (row_live && i + 2 < nk)
+        sc_next = *reinterpret_cast<const uint32_t*>(a.s + (long long)n * a.s_stride + (kt0 + i + 2) * 4);
+      // generic-proxy stores -> visible to the MMAs (async proxy), then this thread's arrival
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tc_smem(&afull[st])) : "memory");
     }
-    // Wait for the last MMAs (they complete in order).
-    if (tid == 0 && committed >= 0)
-      ok = tc_mbar_wait(&adone[committed & 1], (unsigned)(committed >> 1) & 1u) && ok;
-    if (consumers_any(!ok, kCons) || (tid == 0 && committed != nk - 1)) ok = false;
-    if (!ok && tid == 0) atomicOr(&failed, 1);
+  } else {
+    pdl_wait();  // the f16 table's consumers only run the epilogue
   }
   __syncthreads();
   tc_fence_after();
