@@ -22,7 +22,7 @@ def rel(a, b):
 
 
 @pytest.mark.parametrize("m,n,k", [(1, 256, 64), (3, 3072, 1024), (64, 1024, 3072), (64, 2048, 1024),
-                                   (100, 200, 128), (300, 1024, 2048)])
+                                   (100, 200, 128), (300, 1024, 2048), (1000, 384, 1024)])
 def test_q4_gemm_matches_oracle_rows(m, n, k):
     _, w, s = synth.matvec_case(n, k, seed=11)
     x = np.random.default_rng(m).standard_normal((m, k)).astype(np.float32)
