@@ -483,6 +483,25 @@ void decode(qd_batch* b, int steps, int32_t* out_ids) {
 }
 
 // ---- prefill ------------------------------------------------------------------------
+// Residual (+ one partial) + RMSNorm of `rows` rows into the GEMM operands: one warp
+// per row where the hidden size allows (128 NV columns, NV = 4 or 8), else one CTA
+// per row.
+void rows_norm(qd_batch* b, float* h, const float* parts, const __half* embed, const int* tokens, const float* w,
+               long long rows, cudaStream_t s) {
+  const Dims d = dims(b->e);
+  const unsigned grid = (unsigned)((rows + kNormThreads / 32 - 1) / (kNormThreads / 32));
+  const int np = parts ? 1 : 0;
+  if (d.H == 1024)
+    launch_ex(kb_resid_norm_rows<8>, dim3(grid), dim3(kNormThreads), 0, s, h, parts, np, 0LL, embed, tokens, d.V, w,
+              (int)rows, d.eps, b->w_xh, b->w_xl, b->errw);
+  else if (d.H == 512)
+    launch_ex(kb_resid_norm_rows<4>, dim3(grid), dim3(kNormThreads), 0, s, h, parts, np, 0LL, embed, tokens, d.V, w,
+              (int)rows, d.eps, b->w_xh, b->w_xl, b->errw);
+  else
+    launch_ex(kb_resid_norm, dim3((unsigned)rows), dim3(kNormThreads), 0, s, h, parts, np, 0LL, embed, tokens, d.V, w,
+              d.H, d.eps, b->w_xh, b->w_xl, b->errw);
+}
+
 // All prompts at once: B * n rows through every layer (GEMMs over the rows,
 // causal attention inside each prompt), then the LM head on each prompt's last
 // row; each sequence's first generated id becomes its next input at position n.
@@ -502,11 +521,9 @@ void prefill(qd_batch* b, const int32_t* ids, int n, int32_t* first_ids) {
   for (int l = 0; l < d.L; ++l) {
     const LayerDev& L = e->layers[l];
     if (l == 0)
-      launch_ex(kb_resid_norm, dim3((unsigned)T), dim3(kNormThreads), 0, s, b->w_h, (const float*)nullptr, 0, 0LL,
-                (const __half*)e->embed, (const int*)b->w_tok, d.V, L.n_in, d.H, d.eps, b->w_xh, b->w_xl, b->errw);
+      rows_norm(b, b->w_h, nullptr, e->embed, b->w_tok, L.n_in, T, s);
     else
-      launch_ex(kb_resid_norm, dim3((unsigned)T), dim3(kNormThreads), 0, s, b->w_h, (const float*)b->w_y, 1, 0LL,
-                (const __half*)nullptr, (const int*)nullptr, d.V, L.n_in, d.H, d.eps, b->w_xh, b->w_xl, b->errw);
+      rows_norm(b, b->w_h, b->w_y, nullptr, nullptr, L.n_in, T, s);
     gemm_q4(L.qkv, d.H, d.R, b->w_xh, b->w_xl, (int)T, 1, d.H / kTcK, b->w_y, s, b->errw);
     launch(kb_rope_cache, dim3(rope_grid), s, (const float*)b->w_y, 1, 0LL, (int)T, d.NH, d.NKV, L.n_q, L.n_k, d.eps,
            (const float*)e->cos_t, (const float*)e->sin_t, e->opt.rope_row_stride, (const int*)nullptr, n, 0LL,
@@ -523,15 +540,12 @@ void prefill(qd_batch* b, const int32_t* ids, int n, int32_t* first_ids) {
                 d.NH, d.NKV, b->max_seq, scale, b->w_xh, b->w_xl, b->errw);
     }
     gemm_q4(L.o, d.QS, d.H, b->w_xh, b->w_xl, (int)T, 1, d.QS / kTcK, b->w_y, s, b->errw);
-    launch_ex(kb_resid_norm, dim3((unsigned)T), dim3(kNormThreads), 0, s, b->w_h, (const float*)b->w_y, 1, 0LL,
-              (const __half*)nullptr, (const int*)nullptr, d.V, L.n_post, d.H, d.eps, b->w_xh, b->w_xl, b->errw);
+    rows_norm(b, b->w_h, b->w_y, nullptr, nullptr, L.n_post, T, s);
     // gate/up: silu(gate) * up goes straight into the down GEMM's operands
     gemm_q4_silu(L.gu, d.H, d.I, b->w_xh, b->w_xl, (int)T, b->w_ah, b->w_al, s, b->errw);
     gemm_q4(L.d, d.I, d.H, b->w_ah, b->w_al, (int)T, 1, d.I / kTcK, b->w_y, s, b->errw);
   }
-  launch_ex(kb_resid_norm, dim3((unsigned)T), dim3(kNormThreads), 0, s, b->w_h, (const float*)b->w_y, 1, 0LL,
-            (const __half*)nullptr, (const int*)nullptr, d.V, (const float*)e->final_norm, d.H, d.eps, b->w_xh,
-            b->w_xl, b->errw);
+  rows_norm(b, b->w_h, b->w_y, nullptr, nullptr, e->final_norm, T, s);
   // LM head on each prompt's last row; the merge feeds the id back and moves the position to n.
   lm_head(b, b->w_xh + (size_t)(n - 1) * d.H, b->w_xl + (size_t)(n - 1) * d.H, (long long)n * d.H, B,
           b->keep_logits ? b->logits : nullptr, s);

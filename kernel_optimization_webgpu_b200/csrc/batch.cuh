@@ -168,6 +168,92 @@ static __global__ void __launch_bounds__(kNormThreads) kb_resid_norm(float* h, c
   }
 }
 
+// The same with one warp per row, for many rows of K = 128 NV columns (prefill):
+// lane l holds float4s l, l + 32, ... of the row, so each lane has all its h and
+// partial loads in flight at once and the sum of squares needs no CTA barrier.
+// Partials: parts[s * part_stride + row * K + e], s < nparts, added in order.
+template <int NV>
+static __global__ void __launch_bounds__(kNormThreads) kb_resid_norm_rows(float* h, const float* parts, int nparts,
+                                                                          long long part_stride, const __half* embed,
+                                                                          const int* tokens, int vocab, const float* w,
+                                                                          int rows, float eps, __half* x_hi,
+                                                                          __half* x_lo, int* err) {
+  constexpr int K = 128 * NV;
+  pdl_wait();
+  const int lane = threadIdx.x & 31;
+  const long long b = (long long)blockIdx.x * (kNormThreads / 32) + (threadIdx.x >> 5);
+  if (b >= rows) {
+    pdl_trigger();
+    return;
+  }
+  float4 v[NV];
+  float4* hr = reinterpret_cast<float4*>(h + b * K);
+  if (embed) {
+    int tok = tokens[b];
+    if (tok < 0 || tok >= vocab) {
+      if (lane == 0) atomicOr(err, kErrToken);
+      tok = 0;
+    }
+    const uint2* er = reinterpret_cast<const uint2*>(embed + (long long)tok * K);
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const uint2 u = er[lane + 32 * i];
+      const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+      const float2 c = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+      v[i] = make_float4(a.x, a.y, c.x, c.y);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < NV; ++i) v[i] = hr[lane + 32 * i];
+    if (parts) {
+      const float4* p4 = reinterpret_cast<const float4*>(parts) + b * (K / 4);
+      float4 acc[NV];
+#pragma unroll
+      for (int i = 0; i < NV; ++i) acc[i] = p4[lane + 32 * i];
+      for (int s = 1; s < nparts; ++s) {
+        const float4* ps = p4 + (long long)s * (part_stride >> 2);
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+          const float4 y = ps[lane + 32 * i];
+          acc[i].x += y.x;
+          acc[i].y += y.y;
+          acc[i].z += y.z;
+          acc[i].w += y.w;
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        v[i].x += acc[i].x;
+        v[i].y += acc[i].y;
+        v[i].z += acc[i].z;
+        v[i].w += acc[i].w;
+      }
+    }
+  }
+  float ss = 0.0f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) ss += v[i].x * v[i].x + v[i].y * v[i].y + v[i].z * v[i].z + v[i].w * v[i].w;
+  ss = warp_sum(ss);
+  pdl_trigger();
+  const float inv = rsqrtf(ss / (float)K + eps);
+  const float4* w4 = reinterpret_cast<const float4*>(w);
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int e4 = lane + 32 * i;
+    if (embed || parts) hr[e4] = v[i];
+    const float4 ww = w4[e4];
+    __half h0, l0, h1, l1, h2, l2, h3, l3;
+    split_f16(v[i].x * inv * ww.x, h0, l0);
+    split_f16(v[i].y * inv * ww.y, h1, l1);
+    split_f16(v[i].z * inv * ww.z, h2, l2);
+    split_f16(v[i].w * inv * ww.w, h3, l3);
+    __half2 hh[2] = {__halves2half2(h0, h1), __halves2half2(h2, h3)};
+    __half2 ll[2] = {__halves2half2(l0, l1), __halves2half2(l2, l3)};
+    *reinterpret_cast<uint2*>(x_hi + b * K + 4 * e4) = *reinterpret_cast<const uint2*>(hh);
+    *reinterpret_cast<uint2*>(x_lo + b * K + 4 * e4) = *reinterpret_cast<const uint2*>(ll);
+  }
+}
+
 // ---- head RMSNorm + RoPE + KV append --------------------------------------------
 // Row r of a GEMM output laid out [q_heads*128 | NKV*128 (k) | NKV*128 (v)]
 // (split-K partials, summed here). Row r belongs to sequence
