@@ -621,10 +621,12 @@ def run_prefill(args, world, rank, local):
             "e2e": {"value": round(PF_PROMPTS * PF_LEN / t_e2e, 1), "unit": "tok/s",
                     "h2d_bytes_per_step": mine * PF_LEN * 4, "d2h_bytes_per_step": mine * 4,
                     "step": "one qd_batch_prefill call: the prompts' ids in, each prompt's first id out"},
-            "gpu_launches": args.steps * (shape.layers * 9 + 3),
+            "gpu_launches": args.steps * (shape.layers * 8 + 3),  # per layer: 2 norms, 4 GEMMs, RoPE, attention
             "clocks": clk.summary(),
             "generated_ids_sample": [int(first[0])] + more[:3, 0].tolist(),
         }
+        if world == 1 and not args.no_cpu:
+            line["cpu_baseline"] = time_cpu_prefill(rt, all_ids[0])
         print(json.dumps(line), flush=True)
     return 0
 
@@ -656,6 +658,21 @@ def time_cpu_batched(rt, bt, steps=3):
     return {"value": round(tps, 4), "unit": UNIT, "cores": O.lib().qo_num_threads(), "kind": "port",
             "sample": f"{steps} decode tokens of one sequence at positions 2048.. over its 2048-row context "
                       "(the oracle has no batching: 64 sequences cost 64x this), WGSL math restated in C (OpenMP)"}
+
+
+def time_cpu_prefill(rt, ids, n_tokens=256):
+    """Oracle prefill of the first n_tokens ids of one prompt (positions 0..n-1, one
+    forward per token: the oracle has no batched prefill) on the host cores."""
+    from oracle import oracle as O
+    model = O.Model(rt)
+    sess = model.session(max_seq=n_tokens + 1, kv_f16=True)
+    t0 = time.perf_counter()
+    for i in range(n_tokens):
+        sess.forward(int(ids[i]), i)
+    dt = time.perf_counter() - t0
+    return {"value": round(n_tokens / dt, 4), "unit": "tok/s", "cores": O.lib().qo_num_threads(), "kind": "port",
+            "sample": f"prompt positions 0..{n_tokens - 1} of the first prompt, one token per forward "
+                      "(the oracle has no batching or batched prefill), WGSL math restated in C (OpenMP)"}
 
 
 def main():
