@@ -579,16 +579,33 @@ static __global__ void __launch_bounds__(kHeadDim) kb_attn_combine(const float2*
   const int h = blockIdx.x, b = blockIdx.y, d = threadIdx.x, QS = NH * kHeadDim;
   const float2* ml = part_ml + (long long)b * splits * NH + h;
   const float* po = part_o + (long long)b * splits * QS + (long long)h * kHeadDim + d;
-  float M = -INFINITY;
-#pragma unroll 8
-  for (int s = 0; s < splits; ++s) M = fmaxf(M, ml[(long long)s * NH].x);
-  float L = 0.0f, O = 0.0f;
-#pragma unroll 8
-  for (int s = 0; s < splits; ++s) {
-    const float2 m = ml[(long long)s * NH];
-    const float f = m.y > 0.0f ? expf(m.x - M) : 0.0f;
-    L += m.y * f;
-    O += po[(long long)s * QS] * f;
+  float M = -INFINITY, L = 0.0f, O = 0.0f;
+  // Up to 8 splits at a time: all of their loads in flight before the first use.
+  for (int s0 = 0; s0 < splits; s0 += 8) {
+    float2 m[8];
+    float o[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int s = min(s0 + k, splits - 1);
+      m[k] = ml[(long long)s * NH];
+      o[k] = po[(long long)s * QS];
+    }
+    float Mc = M;
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+      if (s0 + k < splits) Mc = fmaxf(Mc, m[k].x);
+    // rescale what the earlier groups summed (online softmax over split groups)
+    const float r = (M == -INFINITY) ? 0.0f : expf(M - Mc);
+    L *= r;
+    O *= r;
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+      if (s0 + k < splits) {
+        const float f = m[k].y > 0.0f ? expf(m[k].x - Mc) : 0.0f;
+        L += m[k].y * f;
+        O += o[k] * f;
+      }
+    M = Mc;
   }
   pdl_trigger();
   __half hh, ll;
