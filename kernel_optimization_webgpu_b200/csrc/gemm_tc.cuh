@@ -16,16 +16,18 @@
 // and y = (D_main + D_corr * 2^-11) * 2^-S leave an error near 2^-22 relative
 // (the dropped lo*lo term), i.e. f32 rounding level.
 //
-// Per CTA: 128 R consumer threads (R = 2, or 4 for the prefill tile BN = 256)
-// and one producer warp. Each k-tile (64 columns = two q4 blocks) is dequantised
-// by R threads per weight row straight into the 128-byte-swizzled K-major smem
-// layout the MMA reads, the activation hi/lo tiles are copied in by TMA, and
-// thread 0 issues the MMAs and commits them to the stage's mbarrier. A double-
-// buffered A stage overlaps the dequantisation of tile k+1 with the MMAs of tile k.
-// The dequantise -> barrier -> MMA-issue chain of a k-tile is what keeps the tensor
-// pipe waiting, so it is spread over as many threads as the block allows
-// (prefill, 32 x 512 prompt rows: 235k prompt tok/s with one thread per row,
-// 271k with two, 284k with four; 294k once a warp of its own issues the MMAs).
+// Per CTA: 128 R consumer threads (R = 2, or 4 for the prefill tile BN = 256), a
+// producer warp and an MMA-issuer warp. Each k-tile (64 columns = two q4 blocks)
+// is dequantised by R threads per weight row straight into the 128-byte-swizzled
+// K-major smem layout the MMA reads, the activation hi/lo tiles are copied in by
+// TMA, and one lane of the issuer warp issues the MMAs once the consumers have
+// arrived on the A buffer's barrier, committing them to the stage's mbarriers. A
+// double-buffered A stage overlaps the dequantisation of tile k+1 with the MMAs of
+// tile k. The chain dequantise -> hand-over -> MMA issue of a k-tile is what kept the
+// tensor pipe waiting, so it is spread over as many threads as the block allows and
+// carries no CTA barrier (prefill, 32 x 512 prompt rows: 235k prompt tok/s with one
+// thread per row issuing behind a CTA barrier, 271k with two, 284k with four; 294k
+// once a warp of its own issues the MMAs).
 //
 // Split-K: gridDim.z CTAs share a row tile, each over its own run of k-tiles,
 // and store partial sums [split][B][N]; the kernel that consumes the result
@@ -206,8 +208,8 @@ __device__ __forceinline__ void warp_argmax_columns(float (&v)[32], uint32_t (&i
 
 // Consumer threads per weight row: each dequantises 8 / R of the row's eight
 // nibble words of a k-tile (R = 2: one q4 block each). More threads shorten the
-// dequantise -> barrier -> MMA-issue chain of every k-tile, which otherwise leaves
-// the tensor pipe idle between k-tiles.
+// dequantisation of every k-tile, which otherwise leaves the tensor pipe idle
+// between k-tiles; the decode tile (BN = 64) keeps R = 2 so that two CTAs fit per SM.
 template <int BN, bool AF16>
 __host__ __device__ constexpr int tc_row_threads() {
   return (!AF16 && BN == 256) ? 4 : 2;
