@@ -232,6 +232,10 @@ def run_reference(args, world, rank):
     """The reference's CPU path: its WGSL math restated in C (oracle), all host threads."""
     if rank != 0:
         return 0
+    # torchrun sets OMP_NUM_THREADS=1 for every rank; this arm runs on rank 0 alone and
+    # uses every host thread
+    from oracle import oracle as O
+    O.lib().qo_set_num_threads(len(os.sched_getaffinity(0)))
     rt = runtime_dir()
     synth.ensure_runtime(rt, synth.QWEN3_0_6B, seed=2)
     steps = max(1, min(args.steps, 48))

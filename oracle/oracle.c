@@ -29,6 +29,15 @@ int qo_num_threads(void) {
 #endif
 }
 
+/* Threads of the parallel loops from now on (n >= 1; a no-op without OpenMP). */
+void qo_set_num_threads(int n) {
+#ifdef _OPENMP
+  if (n >= 1) omp_set_num_threads(n);
+#else
+  (void)n;
+#endif
+}
+
 /* halfToFloat, src/bench/webgpu-runtime.js:1732-1739 (exact f16 -> f32). */
 float qo_half_to_float(uint16_t h) {
   const float sign = (h & 0x8000u) ? -1.0f : 1.0f;

@@ -83,6 +83,7 @@ int qo_greedy(qo_session* s, const int32_t* ids, int n_prompt, int max_new, int3
               float* top2_margins);
 
 int qo_num_threads(void);
+void qo_set_num_threads(int n);
 
 #ifdef __cplusplus
 }

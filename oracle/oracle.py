@@ -64,6 +64,7 @@ def lib():
         L.qo_next_token.argtypes = [vp, vp, _u32p, vp]; L.qo_next_token.restype = i32
         L.qo_greedy.argtypes = [vp, vp, i32, i32, vp, vp]; L.qo_greedy.restype = i32
         L.qo_num_threads.restype = i32
+        L.qo_set_num_threads.argtypes = [i32]
         _lib = L
     return _lib
 

@@ -1,0 +1,27 @@
+"""bench.py's reference arm on the host cores: one JSON line with the fields the
+measurement contract asks for (no GPU needed: the arm times the oracle, the
+reference's WGSL math restated in C, on the CPU)."""
+import json
+import os
+import subprocess
+import sys
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def test_reference_arm_prints_one_contract_line():
+    out = subprocess.run([sys.executable, "bench.py", "--impl", "reference", "--steps", "2", "--warmup", "1"],
+                         cwd=ROOT, capture_output=True, text=True, timeout=600)
+    assert out.returncode == 0, out.stderr[-2000:]
+    lines = [l for l in out.stdout.splitlines() if l.startswith("{")]
+    assert len(lines) == 1, out.stdout
+    d = json.loads(lines[0])
+    assert d["impl"] == "reference"
+    assert d["metric"] == "decode tok/s" and d["unit"] == "tok/s" and d["higher_is_better"] is True
+    assert d["value"] > 0 and d["n_gpus"] == 1 and d["steps"] >= 1
+    cb = d["cpu_baseline"]
+    assert cb["value"] == d["value"] and cb["unit"] == d["unit"]
+    assert cb["kind"] in ("reference", "port") and cb["cores"] >= 1 and cb["sample"]
+    e2e = d["e2e"]
+    assert e2e["value"] == d["value"] and e2e["unit"] == d["unit"]
+    assert e2e["h2d_bytes_per_step"] == 0 and e2e["d2h_bytes_per_step"] == 0
