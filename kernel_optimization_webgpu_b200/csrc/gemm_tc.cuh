@@ -223,13 +223,15 @@ __host__ __device__ constexpr int tc_block_threads() {  // consumers + the produ
   return tc_consumers<BN, AF16>() + 64;
 }
 template <int BN, bool AF16>
-__host__ __device__ constexpr int tc_min_blocks() {  // q4 at BN = 64 (decode) runs two CTAs per SM
-  return (!AF16 && BN <= 64) ? 2 : 1;
+__host__ __device__ constexpr int tc_min_blocks() {  // the decode tiles (BN = 64) run two CTAs per SM
+  return BN <= 64 ? 2 : 1;
 }
 template <int BN, bool AF16>
 __host__ __device__ constexpr int tc_stages() {
-  // q4 at BN = 64 (decode): two stages keep the CTA at ~105 KB so two fit per SM
-  return AF16 ? (BN <= 64 ? 4 : 3) : (BN <= 64 ? 2 : (BN <= 128 ? 3 : 2));
+  // BN = 64 (decode): two stages (q4, ~105 KB) or three (the f16 LM-head table,
+  // ~97 KB) keep the CTA small enough for two per SM (b64 LM head: 15.9k -> 16.1k
+  // tok/s against four stages and one CTA per SM)
+  return AF16 ? 3 : (BN <= 64 ? 2 : (BN <= 128 ? 3 : 2));
 }
 template <int BN, bool AF16>
 __host__ __device__ constexpr int tc_stage_bytes() {
