@@ -124,3 +124,20 @@ def test_qwen_profile_mirrors_the_reference_profile():
     assert (p["layers"], p["hiddenSize"], p["intermediateSize"], p["attentionHeads"], p["kvHeads"],
             p["headDim"], p["vocabSize"], p["normEpsilon"]) == (s.layers, s.hidden, s.intermediate, s.heads,
                                                                s.kv_heads, s.head_dim, s.vocab, s.eps)
+
+
+def test_bindings_match_the_declared_arity():
+    """Every ctypes binding passes exactly as many arguments as its C declaration
+    takes (a mismatch would pass garbage through the ABI without any error)."""
+    text = open(os.path.join(ROOT, "include", "qdecode.h")).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    decls = dict(re.findall(r"\b(qd_[a-z0-9_]+)\s*\(([^;{]*?)\)\s*;", text, flags=re.S))
+    decls.pop("qd_token_cb", None)
+    assert set(decls) == set(header_functions())
+    L = _lib.load()
+    for name, params in decls.items():
+        p = params.strip()
+        n = 0 if p in ("", "void") else len(p.split(","))
+        argtypes = getattr(L, name).argtypes
+        assert argtypes is not None, name
+        assert len(argtypes) == n, (name, n, len(argtypes))
