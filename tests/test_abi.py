@@ -141,3 +141,17 @@ def test_bindings_match_the_declared_arity():
         argtypes = getattr(L, name).argtypes
         assert argtypes is not None, name
         assert len(argtypes) == n, (name, n, len(argtypes))
+
+
+def test_bindings_match_the_declared_return_types():
+    """size_t results come back as 64-bit values, strings as char pointers, void as None."""
+    text = open(os.path.join(ROOT, "include", "qdecode.h")).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    want = {"int": C.c_int, "size_t": C.c_size_t, "const char*": C.c_char_p, "void": None}
+    L = _lib.load()
+    seen = 0
+    for ret, name in re.findall(r"(int|size_t|const char\s*\*|void)\s+(qd_[a-z0-9_]+)\s*\(", text):
+        ret = re.sub(r"\s+", "", ret).replace("constchar*", "const char*")
+        assert getattr(L, name).restype is want[ret], (name, ret)
+        seen += 1
+    assert seen == len(header_functions())
