@@ -416,8 +416,8 @@ def run_ours(args, world, rank, local):
                          "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4),
                          "traffic": B1_TRAFFIC if eng_kernel == 1 else None,
-                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch "
-                                           "(profiles/persistent_decode_b1_warp_states.md)" if eng_kernel == 1 else None,
+                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one token launch "
+                                           "of this workload" if eng_kernel == 1 else None,
                          "bytes_per_step": int(bytes_avg), "peak_source": peak_kind},
             "e2e": {"value": round(e2e, 2), "unit": UNIT, "h2d_bytes_per_step": PROMPT_LEN * 4,
                     "d2h_bytes_per_step": NEW_TOKENS * 4,

@@ -264,7 +264,9 @@ int qd_gqa_decode(const float* q, const void* k_cache, const void* v_cache, int 
  *    about) are rejected with QD_E_RANGE; use qd_gqa_decode for those.
  *  - The first call on each device looks up that array's device address (a CUDA
  *    symbol query, with the device current); make that first call before any
- *    stream capture begins.
+ *    stream capture begins. The address is kept per device together with the id
+ *    of the CUDA context it belongs to; the first call in a new context (after
+ *    cudaDeviceReset, say) looks it up again, so it too belongs outside a capture.
  *  - All calls on a device share the one array and it keeps the last call's
  *    contents. Nothing in it needs to start at zero: each call writes every
  *    partial it reads. Calls whose kernels overlap on the GPU (other streams,

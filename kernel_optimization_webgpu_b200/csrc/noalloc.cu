@@ -25,28 +25,61 @@ static __device__ __align__(256) unsigned char g_attn_scratch[QD_NOALLOC_SCRATCH
 
 constexpr int kMaxDevices = 64;
 std::mutex g_mu;
+// Per device: the symbol address and the unique id of the CUDA context it was
+// looked up in. A device reset or another context gets a new id (ids are never
+// reused within a process), which makes the next call look the address up again.
 void* g_scratch_ptr[kMaxDevices] = {};
+unsigned long long g_scratch_ctx[kMaxDevices] = {};
 
 int fail(int code, const std::string& msg) {
   qd::set_thread_error(msg);  // read back with qd_last_error(NULL)
   return code;
 }
 
+// cuCtxGetCurrent / cuCtxGetId through the runtime's driver entry points (the
+// library does not link the driver library itself).
+typedef int (*CtxGetCurrentFn)(void**);
+typedef int (*CtxGetIdFn)(void*, unsigned long long*);
+
+bool current_context_id(unsigned long long* id) {
+  static CtxGetCurrentFn get_current = nullptr;
+  static CtxGetIdFn get_id = nullptr;
+  static bool resolved = false;
+  if (!resolved) {
+    void* f0 = nullptr;
+    void* f1 = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f0, cudaEnableDefault) == cudaSuccess &&
+        cudaGetDriverEntryPoint("cuCtxGetId", &f1, cudaEnableDefault) == cudaSuccess) {
+      get_current = reinterpret_cast<CtxGetCurrentFn>(f0);
+      get_id = reinterpret_cast<CtxGetIdFn>(f1);
+    }
+    resolved = true;
+  }
+  void* ctx = nullptr;
+  if (!get_current || !get_id || get_current(&ctx) != 0 || !ctx) return false;
+  return get_id(ctx, id) == 0;
+}
+
 // The device address of g_attn_scratch on the current device. On the host the
 // name g_attn_scratch is only a stand-in, so the address has to be asked for,
-// once per device, with that device current.
+// with that device current: once per device (and again when the device's
+// context is a new one).
 int scratch_address(void** out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
     return fail(QD_E_CUDA, "qd_gqa_decode_noalloc: no current CUDA device");
   std::lock_guard<std::mutex> lock(g_mu);
-  if (!g_scratch_ptr[dev]) {
+  unsigned long long ctx = 0;
+  const bool have_ctx = current_context_id(&ctx);
+  if (!g_scratch_ptr[dev] || !have_ctx || ctx != g_scratch_ctx[dev]) {
     void* p = nullptr;
     const cudaError_t rc = cudaGetSymbolAddress(&p, g_attn_scratch);
     if (rc != cudaSuccess || !p)
       return fail(QD_E_CUDA, std::string("qd_gqa_decode_noalloc: cudaGetSymbolAddress failed: ") +
                                  cudaGetErrorString(rc));
     g_scratch_ptr[dev] = p;
+    // the lookup made the context current if it was not yet
+    g_scratch_ctx[dev] = current_context_id(&ctx) ? ctx : 0;
   }
   *out = g_scratch_ptr[dev];
   return QD_OK;
@@ -88,7 +121,9 @@ int qd_gqa_decode_noalloc(const float* q, const void* k_cache, const void* v_cac
   if (group != 1 && group != 2 && group != 4 && group != 8)
     return fail(QD_E_INVALID, "qd_gqa_decode_noalloc: q_heads / kv_heads must be 1, 2, 4 or 8");
   if (kv_dtype != QD_KV_F16 && kv_dtype != QD_KV_F32) return fail(QD_E_INVALID, "qd_gqa_decode_noalloc: bad kv_dtype");
-  // Same partials layout as qd_gqa_decode: [splits][q_heads] (max, sum) then [splits][q_heads][128].
+  // Partials, per split and query head as in qd_gqa_decode: (max, sum) pairs
+  // [splits][q_heads] at offset 0, then outputs [splits][q_heads][128] from the
+  // next 256-byte boundary (qd_gqa_decode's workspace uses other offsets).
   const size_t splits = (seq_len + kAttnChunk - 1) / kAttnChunk;
   const size_t ml_bytes = (splits * q_heads * sizeof(float2) + 255) & ~size_t(255);
   const size_t need = ml_bytes + splits * q_heads * kHeadDim * sizeof(float);

@@ -1,5 +1,5 @@
 // Node-API addon over libqdecode.so: the native half of cuda-runtime.js.
-// Built only where Node headers exist. It converts JS
+// Built only where Node headers (node_api.h) exist. It converts JS
 // values to the C ABI of include/qdecode.h and back; no logic of its own.
 #include <node_api.h>
 

@@ -1,6 +1,6 @@
 """CUDA path vs the CPU oracle through the C ABI (needs a B200).
 
-Tolerances: north_star allows 1e-2 relative for logits and matvec outputs; the
+Tolerances: the contract allows 1e-2 relative for logits and matvec outputs; the
 kernels accumulate in f32 like the reference, so these tests hold them to a
 tighter 1e-4 (max |diff| / max |reference|) and greedy ids to bit-exact.
 """
