@@ -74,11 +74,23 @@ def f16_round(a: np.ndarray) -> np.ndarray:
 
 
 def q4_projection(rng: np.random.Generator, out_size: int, in_size: int,
-                  scale_std: float = 0.02) -> tuple[np.ndarray, np.ndarray]:
-    """Random MatMulNBits weight: u32 words [out][in/8] of uniform nibbles, f16-valued f32 scales."""
+                  scale_std: float = 0.02, nibbles: str = "uniform") -> tuple[np.ndarray, np.ndarray]:
+    """Random MatMulNBits weight: u32 words [out][in/8] of random nibbles, f16-valued f32 scales.
+
+    nibbles "uniform": every nibble uniform on 0..15 (mean 7.5, so each weight
+    carries a -0.5 * scale bias against the zero point 8); "centered": uniform on
+    1..15, symmetric around the zero point."""
     if in_size % BLOCK_SIZE:
         raise ValueError("in_size must be a multiple of the block size")
-    words = rng.integers(0, 2**32, size=(out_size, in_size // 8), dtype=np.uint64).astype(np.uint32)
+    if nibbles == "uniform":
+        words = rng.integers(0, 2**32, size=(out_size, in_size // 8), dtype=np.uint64).astype(np.uint32)
+    elif nibbles == "centered":
+        nib = rng.integers(1, 16, size=(out_size, in_size // 8, 8), dtype=np.uint32)
+        words = np.zeros((out_size, in_size // 8), np.uint32)
+        for i in range(8):
+            words |= nib[:, :, i] << np.uint32(4 * i)
+    else:
+        raise ValueError(f"unknown nibble distribution {nibbles!r}")
     scales = np.abs(rng.standard_normal(out_size * (in_size // BLOCK_SIZE))) * scale_std
     scales = f16_round(scales).astype(np.float32)
     return words, scales
@@ -106,11 +118,14 @@ def _write(path: str, arr: np.ndarray) -> int:
 
 def write_runtime(out_dir: str, shape: Shape = QWEN3_0_6B, seed: int = 2,
                   norm_mode: str = "random", embed_std: float = 0.02,
-                  scale_std: float = 0.02) -> dict:
+                  scale_std: float = 0.02, nibbles: str = "uniform") -> dict:
     """Write a complete runtime directory and return its manifest.
 
     norm_mode "random" draws every RMSNorm weight as f16(1 + 0.1 N(0,1)) so that
     a wrong weight index shows up in parity; "ones" gives unit weights.
+    nibbles: see q4_projection. With "uniform" nibbles the per-weight bias drives
+    a random-init Qwen3-0.6B-shape model to emit one id over and over; "centered"
+    nibbles give a model whose greedy ids change from step to step.
     Draw order (fixed, part of the format): embedding, then per layer the four
     norms followed by q, k, v, o, gate, up, down; the final norm last.
     """
@@ -156,7 +171,7 @@ def write_runtime(out_dir: str, shape: Shape = QWEN3_0_6B, seed: int = 2,
             le["norms"][key] = entry(f"model.layers.{layer}.{key}_norm.weight", f, [size], n)
         for key in PROJECTIONS:
             out_size, in_size = shape.proj_dims(key)
-            words, scales = q4_projection(rng, out_size, in_size, scale_std)
+            words, scales = q4_projection(rng, out_size, in_size, scale_std, nibbles)
             wf, sf = f"{d}/{key}_weight_q4.bin", f"{d}/{key}_scales_f32.bin"
             nw = _write(os.path.join(out_dir, wf), words)
             ns = _write(os.path.join(out_dir, sf), scales)
@@ -177,7 +192,7 @@ def write_runtime(out_dir: str, shape: Shape = QWEN3_0_6B, seed: int = 2,
     n = _write(os.path.join(out_dir, "shared/final_norm.f16"), fn)
     manifest["finalNorm"] = entry("model.norm.weight", "shared/final_norm.f16", [shape.hidden], n)
     manifest["synthetic"] = {"seed": seed, "normMode": norm_mode, "embedStd": embed_std,
-                             "scaleStd": scale_std, "shape": asdict(shape)}
+                             "scaleStd": scale_std, "nibbles": nibbles, "shape": asdict(shape)}
     with open(os.path.join(out_dir, "manifest.json"), "w") as f:
         json.dump(manifest, f, indent=2)
         f.write("\n")
@@ -185,16 +200,17 @@ def write_runtime(out_dir: str, shape: Shape = QWEN3_0_6B, seed: int = 2,
 
 
 def ensure_runtime(out_dir: str, shape: Shape = QWEN3_0_6B, seed: int = 2,
-                   norm_mode: str = "random") -> dict:
+                   norm_mode: str = "random", nibbles: str = "uniform") -> dict:
     """Write the runtime directory unless a matching one already exists there."""
     path = os.path.join(out_dir, "manifest.json")
     if os.path.exists(path):
         with open(path) as f:
             m = json.load(f)
         syn = m.get("synthetic", {})
-        if syn.get("seed") == seed and syn.get("normMode") == norm_mode and syn.get("shape") == asdict(shape):
+        if (syn.get("seed") == seed and syn.get("normMode") == norm_mode and syn.get("shape") == asdict(shape)
+                and syn.get("nibbles", "uniform") == nibbles):
             return m
-    return write_runtime(out_dir, shape, seed, norm_mode)
+    return write_runtime(out_dir, shape, seed, norm_mode, nibbles=nibbles)
 
 
 # ---- single-kernel workloads -------------------------------------------------

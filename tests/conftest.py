@@ -28,3 +28,13 @@ def qwen_runtime(tmp_path_factory):
     d = str(tmp_path_factory.mktemp("qwen_seed2"))
     synth.write_runtime(d, synth.QWEN3_0_6B, seed=2)
     return d
+
+
+@pytest.fixture(scope="session")
+def qwen_runtime_centered(tmp_path_factory):
+    """Qwen3-0.6B-shape random-init weights (seed 5) with nibbles centred on the zero
+    point: a model whose greedy ids change from step to step."""
+    from kernel_optimization_webgpu_b200 import synth
+    d = str(tmp_path_factory.mktemp("qwen_seed5_centered"))
+    synth.write_runtime(d, synth.QWEN3_0_6B, seed=5, nibbles="centered")
+    return d

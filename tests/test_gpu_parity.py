@@ -284,3 +284,109 @@ def test_stepping_interface_matches_generate_and_flags_overrun(tiny_runtime):
         eng.set_stream(None)
         ids, _ = eng.generate_greedy(prompt, 6)   # the engine stays usable
         assert ids == want
+
+
+# ---- every step's logits, varied ids, variants, the RoPE stride option ------------
+
+def _engine_step_logits(eng, prompt, n):
+    """Greedy ids and each step's logits through the stepping entry points."""
+    eng.decode_begin(prompt, n)
+    logits = []
+    for _ in range(n):
+        eng.decode_step()
+        logits.append(eng.logits())
+    return eng.decode_sync(n), logits
+
+
+def _oracle_step_logits(model, prompt, n, **session_kw):
+    sess = model.session(**session_kw)
+    for i, t in enumerate(prompt[:-1]):
+        sess.forward(t, i)
+    tok, ids, logits, margins = prompt[-1], [], [], []
+    for step in range(n):
+        sess.forward(tok, len(prompt) - 1 + step)
+        tok, lg, margin = sess.next_token()
+        ids.append(tok)
+        logits.append(lg)
+        margins.append(margin)
+    return ids, logits, margins
+
+
+def _check_steps(got_ids, got_logits, want_ids, want_logits, margins):
+    for step, (g, w) in enumerate(zip(got_logits, want_logits)):
+        err = rel(g, w)
+        print(f"step {step}: id {want_ids[step]} top-2 margin {margins[step]:.4g} logits rel err {err:.2e}")
+        assert err < TOL, (step, err)
+    assert got_ids == want_ids, (got_ids, want_ids, margins)
+
+
+@pytest.mark.parametrize("persistent", [1, 0])
+def test_engine_qwen_shape_config2_every_step_logits(qwen_runtime, persistent):
+    """Config 2 at the Qwen3-0.6B shape: all 24 steps' logits against the oracle at
+    1e-4 (this seed-2 model emits one id at every step, so the ids alone say little)."""
+    rng = np.random.Generator(np.random.PCG64(2))
+    prompt = rng.integers(0, 151936, size=8).tolist()
+    want_ids, want_logits, margins = _oracle_step_logits(O.Model(qwen_runtime), prompt, 24, max_seq=64,
+                                                         kv_f16=True)
+    with R.Engine(qwen_runtime, max_seq=64, persistent=persistent) as eng:
+        got_ids, got_logits = _engine_step_logits(eng, prompt, 24)
+    _check_steps(got_ids, got_logits, want_ids, want_logits, margins)
+
+
+@pytest.mark.parametrize("persistent", [1, 0])
+def test_engine_qwen_shape_varied_ids(qwen_runtime_centered, persistent):
+    """A Qwen3-0.6B-shape model whose greedy ids change from step to step (seed 5,
+    nibbles centred on the zero point): bit-exact ids and every step's logits."""
+    rng = np.random.Generator(np.random.PCG64(2))
+    prompt = rng.integers(0, 151936, size=8).tolist()
+    want_ids, want_logits, margins = _oracle_step_logits(O.Model(qwen_runtime_centered), prompt, 24, max_seq=64,
+                                                         kv_f16=True)
+    assert len(set(want_ids)) >= 12, want_ids
+    with R.Engine(qwen_runtime_centered, max_seq=64, persistent=persistent) as eng:
+        got_ids, got_logits = _engine_step_logits(eng, prompt, 24)
+        ids, _ = eng.generate_greedy(prompt, 24)
+    _check_steps(got_ids, got_logits, want_ids, want_logits, margins)
+    assert ids == want_ids
+
+
+def test_variants_emit_identical_ids(tiny_runtime):
+    """The reference's own bar: every variant emits the same greedy ids
+    (docs/05-reproduce.md:98-100, src/bench/ab-page.js:95-97)."""
+    # the reference's fallback prompt (src/bench/ab-page.js:18), folded into TINY's vocabulary
+    prompt = [t % synth.TINY.vocab for t in (3838, 374, 279, 6722, 315, 9625, 30)]
+    got = {}
+    for variant in R.VARIANTS:
+        with R.Engine(tiny_runtime, max_seq=64, variant=variant) as eng:
+            got[variant], _ = eng.generate_greedy(prompt, 12)
+    ctx = R.createWebGpuContext(tiny_runtime)
+    for variant in R.VARIANTS:
+        out = R.runCustomQwenGreedyPrompt(device=ctx["device"], profile={}, inputIds=prompt, maxNewTokens=12,
+                                          variant=variant)
+        assert out["generated"] == got["optimized"], variant
+    ctx["device"].close()
+    assert got["original"] == got["mixed"] == got["optimized"]
+    want, _ = O.Model(tiny_runtime).session(max_seq=64, kv_f16=True).greedy(prompt, 12)
+    assert got["optimized"] == want
+
+
+@pytest.mark.parametrize("n,k", [(3072, 1024), (1024, 3072)])
+def test_q4_matvec_matches_the_original_variant_oracle(n, k):
+    """The CUDA matvec against the restatement of baseline/matmul_nbits_q4.wgsl
+    (the 'original' variant's kernel and its summation order)."""
+    x, w, s = synth.matvec_case(n, k, seed=0)
+    assert rel(run_matvec(x, w, s), O.q4_matvec(x, w, s, original=True)) < TOL
+
+
+@pytest.mark.parametrize("persistent", [1, 0])
+def test_engine_rope_row_stride_option(tiny_runtime, tiny_model, persistent):
+    """rope_row_stride = 64 reads table row p at position p (rope.wgsl:27 reads row
+    2p with the reference's stride 128); the engine follows the oracle either way."""
+    prompt = [11, 4000, 7, 123, 9]
+    with R.Engine(tiny_runtime, max_seq=64, rope_row_stride=64, persistent=persistent) as eng:
+        got_ids, got_logits = _engine_step_logits(eng, prompt, 8)
+    want_ids, want_logits, margins = _oracle_step_logits(tiny_model, prompt, 8, max_seq=64, kv_f16=True,
+                                                         rope_row_stride=64)
+    _check_steps(got_ids, got_logits, want_ids, want_logits, margins)
+    # the option changes the math: the default stride gives other logits
+    _, default_logits, _ = _oracle_step_logits(tiny_model, prompt, 8, max_seq=64, kv_f16=True)
+    assert any(rel(a, b) > 1e-3 for a, b in zip(want_logits, default_logits))
