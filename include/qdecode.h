@@ -203,6 +203,24 @@ int qd_batch_step_lm_slice(qd_batch* b);
 int qd_batch_step_merge(qd_batch* b);
 int qd_batch_shard_sync(qd_batch* b, int steps, int32_t* out_ids);
 
+/* ---- failure-path test hooks ------------------------------------------------------
+ * The reference's only failure detection is the A/B page's uncapturederror guard
+ * (src/bench/ab-page.js:158-161,181-187), which refuses results after a device error.
+ * Here every device-side wait is bounded and a wait that runs out makes the call
+ * return QD_E_TIMEOUT with the engine still usable. These two calls let a test make
+ * one such wait run out on purpose, without any fault:
+ *  - qd_engine_inject_stall: the next persistent decode launch withholds layer 0's
+ *    q/k/v results, so its attention CTAs wait until their 200 ms deadline, raise the
+ *    abort flag and every CTA returns; the generation that contains it returns
+ *    QD_E_TIMEOUT and the next one runs normally. QD_E_INVALID unless the engine
+ *    runs the persistent kernel (qd_engine_uses_persistent == 1).
+ *  - qd_batch_inject_stall: CTA (0, 0, 0) of the next tensor-core GEMM the batch
+ *    launches withholds its first activation tiles, so its MMA issuer waits until
+ *    its 1 s deadline; the decode or prefill call that contains it returns
+ *    QD_E_TIMEOUT. Both only enqueue (on the engine's stream). */
+int qd_engine_inject_stall(qd_engine* e);
+int qd_batch_inject_stall(qd_batch* b);
+
 /* runCustomQwenGreedyPrompt over `batch` prompts of n_prompt ids each: prefill,
  * then max_new_tokens greedy tokens per prompt. ids [batch][n_prompt], out_ids
  * [batch][max_new_tokens] (host). Uses a temporary batch of max_seq

@@ -35,7 +35,7 @@ EXPORTS = (
     "qd_batch_positions", "qd_batch_decode", "qd_batch_prefill", "qd_batch_keep_logits", "qd_batch_logits",
     "qd_batch_read_kv", "qd_batch_write_kv", "qd_batch_step_kernels", "qd_generate_batch",
     "qd_batch_set_vocab_shard", "qd_batch_step_layers", "qd_batch_step_lm_slice", "qd_batch_step_merge",
-    "qd_batch_shard_sync",
+    "qd_batch_shard_sync", "qd_engine_inject_stall", "qd_batch_inject_stall",
 )
 
 
@@ -172,6 +172,10 @@ def load(build_if_stale: bool = True):
         getattr(L, name).restype = i32
     L.qd_batch_shard_sync.argtypes = [vp, i32, vp]
     L.qd_batch_shard_sync.restype = i32
+    L.qd_engine_inject_stall.argtypes = [vp]
+    L.qd_engine_inject_stall.restype = i32
+    L.qd_batch_inject_stall.argtypes = [vp]
+    L.qd_batch_inject_stall.restype = i32
     _lib = L
     return L
 

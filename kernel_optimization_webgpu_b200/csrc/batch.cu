@@ -119,6 +119,7 @@ void gemm_q4(const char* base, int K, int n_rows, const __half* xh, const __half
   a.ldy = n_rows;
   a.y_split = (long long)rows * n_rows;
   a.err = err;
+  a.stall = err ? err + 1 : nullptr;
   launch_gemm(a, splits, kGemmQ4Store, s);
 }
 
@@ -135,6 +136,7 @@ void gemm_q4_silu(const char* base, int K, int I, const __half* xh, const __half
   a.y_hi = out_hi;
   a.y_lo = out_lo;
   a.err = err;
+  a.stall = err ? err + 1 : nullptr;
   launch_gemm(a, 1, kGemmQ4Silu, s);
 }
 
@@ -155,6 +157,7 @@ void lm_head(qd_batch* b, const __half* xh, const __half* xl, long long ldx, int
   a.part_v = b->lm_pv;
   a.part_i = b->lm_pi;
   a.err = b->errw;
+  a.stall = b->errw + 1;
   launch_gemm(a, 1, kGemmF16Argmax, s);
 }
 
@@ -389,7 +392,7 @@ void create_batch(qd_engine* e, int B, int max_seq, qd_batch* b) {
   const size_t o_ml = take((size_t)B * b->splits * d.NH * 8), o_po = take((size_t)B * b->splits * d.QS * 4);
   const size_t o_pv = take((size_t)B * b->lm_tiles * 4), o_pi = take((size_t)B * b->lm_tiles * 4);
   const size_t o_res = take((size_t)B * 8), o_tok = take((size_t)B * 4), o_pos = take((size_t)B * 4);
-  const size_t o_out = take((size_t)b->max_steps * B * 4), o_step = take(4), o_err = take(4);
+  const size_t o_out = take((size_t)b->max_steps * B * 4), o_step = take(4), o_err = take(8);  // [0] status word, [1] stall hook
   if (cudaMalloc(&b->dec, off) != cudaSuccess) throw QdError{QD_E_NOMEM, "cannot allocate batch step buffers"};
   QD_CK(cudaMemsetAsync(b->dec, 0, off, e->stream));
   char* base = static_cast<char*>(b->dec);
@@ -883,6 +886,20 @@ int qd_batch_write_kv(qd_batch* b, int layer, int seq, int pos0, int count, cons
         QD_CK(cudaMemcpy(dst, tmp.data(), tmp.size() * 2, cudaMemcpyHostToDevice));
       }
     }
+  } catch (const QdError& err) {
+    return bfail(b, err);
+  }
+  return QD_OK;
+}
+
+int qd_batch_inject_stall(qd_batch* b) {
+  if (!b) return bfail(nullptr, QdError{QD_E_INVALID, "batch is NULL"});
+  try {
+    qd_engine* e = b->e;
+    QD_CK(cudaSetDevice(e->dev));
+    static const int one = 1;
+    QD_CK(cudaMemcpyAsync(b->errw + 1, &one, sizeof(int), cudaMemcpyHostToDevice, e->stream));
+    QD_CK(cudaStreamSynchronize(e->stream));
   } catch (const QdError& err) {
     return bfail(b, err);
   }

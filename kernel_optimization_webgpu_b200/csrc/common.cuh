@@ -34,6 +34,9 @@ struct DevState {
   // Below: owned by the device (the host only repairs them after a failure).
   int epoch;          // launches of the persistent decode kernel so far (exchange-word tag)
   int abort;          // set by a persistent kernel whose wait expired
+  // Test hook (qd_engine_inject_stall): the persistent launch whose epoch equals
+  // this withholds layer 0's q/k/v stores, so its waits run out; 0 = never.
+  int stall_epoch;
 };
 
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }

@@ -894,6 +894,7 @@ void check_state(qd_engine* e) {
     e->pinned_state->epoch += 2;
     e->pinned_state->abort = 0;
     e->pinned_state->err = 0;
+    e->pinned_state->stall_epoch = 0;
     QD_CK(cudaMemcpyAsync(e->st, e->pinned_state, sizeof(DevState), cudaMemcpyHostToDevice, e->stream));
     QD_CK(cudaMemsetAsync(e->lm_counter, 0, 4, e->stream));
     if (e->clus) {  // a failed launch may leave partial sums and counts in either parity
@@ -1219,6 +1220,24 @@ int qd_decode_sync(qd_engine* e, int32_t* out_ids, int n) {
     check_state(e);
     const int k = std::min(n, e->stepping_max_new);
     for (int i = 0; out_ids && i < k; ++i) out_ids[i] = *reinterpret_cast<volatile int*>(e->out_host + i);
+  } catch (const QdError& err) {
+    return fail(e, err);
+  }
+  return QD_OK;
+}
+
+int qd_engine_inject_stall(qd_engine* e) {
+  if (!e) return fail(nullptr, QdError{QD_E_INVALID, "engine is NULL"});
+  try {
+    if (!e->persist || e->clus) throw QdError{QD_E_INVALID, "the stall hook needs the persistent decode kernel"};
+    QD_CK(cudaSetDevice(e->dev));
+    // The next launch tags its words with the device's epoch + 1.
+    QD_CK(cudaMemcpyAsync(e->pinned_state, e->st, sizeof(DevState), cudaMemcpyDeviceToHost, e->stream));
+    QD_CK(cudaStreamSynchronize(e->stream));
+    e->pinned_state->stall_epoch = e->pinned_state->epoch + 1;
+    QD_CK(cudaMemcpyAsync(&e->st->stall_epoch, &e->pinned_state->stall_epoch, sizeof(int), cudaMemcpyHostToDevice,
+                          e->stream));
+    QD_CK(cudaStreamSynchronize(e->stream));
   } catch (const QdError& err) {
     return fail(e, err);
   }

@@ -88,6 +88,10 @@ struct TcArgs {
   __half* y_hi;               // kTcSilu: the next GEMM's operands [B][ldy]
   __half* y_lo;
   int* err;                   // device status word (bit kTcErrTimeout)
+  // Test hook (qd_batch_inject_stall): CTA (0, 0, 0) of the first launch that finds
+  // *stall non-zero clears it and withholds its first activation tiles, so that
+  // CTA's waits run out and it reports kTcErrTimeout. NULL: no hook.
+  int* stall;
 };
 
 constexpr int kTcErrTimeout = 8;
@@ -314,9 +318,11 @@ __global__ void __launch_bounds__(tc_block_threads<BN, AF16>(), tc_min_blocks<BN
       tma_prefetch_map(&a.tm_xh);
       tma_prefetch_map(&a.tm_xl);
       bool ok = true;
-      int last[S];
+      int last_w[S], last_b[S];  // newest k-tile whose weight / activation tiles each stage was given
 #pragma unroll
-      for (int i = 0; i < S; ++i) last[i] = -1;
+      for (int i = 0; i < S; ++i) last_w[i] = last_b[i] = -1;
+      const bool withhold = a.stall && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 &&
+                            atomicExch(a.stall, 0) != 0;
       // With one column tile (decode) every weight tile is read exactly once per
       // launch: evict-first. With several (prefill) the other column tiles reread
       // it from L2, so it keeps the normal policy.
@@ -334,6 +340,7 @@ __global__ void __launch_bounds__(tc_block_threads<BN, AF16>(), tc_min_blocks<BN
         asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(tc_smem(&full_w[k])), "r"(kW)
                      : "memory");
         load_w(ring + k * kStage, k, &full_w[k]);
+        last_w[k] = k;
       }
       pdl_wait();
       for (int k = 0; k < nk; ++k) {
@@ -347,23 +354,24 @@ __global__ void __launch_bounds__(tc_block_threads<BN, AF16>(), tc_min_blocks<BN
           asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(tc_smem(&full_w[slot])), "r"(kW)
                        : "memory");
           load_w(st, k, &full_w[slot]);
+          last_w[slot] = k;
         }
+        if (withhold && k == 0) continue;  // test hook: k-tile 0's activations never arrive
         asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(tc_smem(&full_b[slot])),
                      "r"(2 * kBt)
                      : "memory");
         tma_load_2d(st + kW, &a.tm_xh, (kt0 + k) * kTcK, b0, &full_b[slot]);
         tma_load_2d(st + kW + kBt, &a.tm_xl, (kt0 + k) * kTcK, b0, &full_b[slot]);
-        last[slot] = k;
+        last_b[slot] = k;
       }
       if (!ok) atomicOr(&failed, 1);
       // Nothing may still be landing in shared memory when the CTA exits: the
       // newest tile of each stage is the only one that can be in flight.
 #pragma unroll
-      for (int i = 0; i < S; ++i)
-        if (last[i] >= 0) {
-          (void)tc_mbar_wait(&full_w[i], (unsigned)(last[i] / S) & 1u);
-          (void)tc_mbar_wait(&full_b[i], (unsigned)(last[i] / S) & 1u);
-        }
+      for (int i = 0; i < S; ++i) {
+        if (last_w[i] >= 0) (void)tc_mbar_wait(&full_w[i], (unsigned)(last_w[i] / S) & 1u);
+        if (last_b[i] >= 0) (void)tc_mbar_wait(&full_b[i], (unsigned)(last_b[i] / S) & 1u);
+      }
     }
   } else if (warp == kCons / 32 + 1) {
     // ---- MMA issuer (one lane) ----

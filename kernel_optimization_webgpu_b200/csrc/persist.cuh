@@ -526,6 +526,7 @@ __global__ void __launch_bounds__(kPT, 1) k_decode_persistent(const __grid_const
 
   const int pos = a.st->pos;
   const unsigned epoch = (unsigned)a.st->epoch + 1u;
+  const bool stall = a.st->stall_epoch != 0 && (unsigned)a.st->stall_epoch == epoch;
   if (pos < 0 || pos >= a.max_seq) {  // the host keeps positions in range; never index out of bounds
     if (threadIdx.x == 0) atomicOr(&a.st->err, kErrPosition);
     return;
@@ -588,7 +589,7 @@ __global__ void __launch_bounds__(kPT, 1) k_decode_persistent(const __grid_const
       const int n = rg.qkv_hi - rg.qkv_lo;
       stage_dots(S.ring + (chunk % kSlots) * kSlotBytes, n, 1, (int)a.rec_h, H / kBlockCols, 1, S.xs, S.res);
       __syncthreads();
-      if (threadIdx.x < n) st_word(xq + rg.qkv_lo + threadIdx.x, S.res[threadIdx.x], epoch);
+      if (threadIdx.x < n && !(stall && l == 0)) st_word(xq + rg.qkv_lo + threadIdx.x, S.res[threadIdx.x], epoch);
       __syncthreads();
       stamp(tl, ev + 2);
       if (threadIdx.x == 0) issue_chunk(a, S, rg, chunk + kSlots, n_chunks);

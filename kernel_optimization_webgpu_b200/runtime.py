@@ -168,6 +168,11 @@ class Engine:
         check(_lib.load().qd_engine_logits(self._h, out.ctypes.data), self._h)
         return out
 
+    def inject_stall(self) -> None:
+        """Test hook: the next persistent decode launch withholds layer 0's q/k/v
+        results, so its bounded waits run out (qd_engine_inject_stall)."""
+        check(_lib.load().qd_engine_inject_stall(self._h), self._h)
+
     def hidden(self) -> np.ndarray:
         out = np.zeros(self.profile["hidden"], np.float32)
         check(_lib.load().qd_engine_hidden(self._h, out.ctypes.data), self._h)
@@ -265,6 +270,11 @@ class Batch:
     @property
     def step_kernels(self) -> int:
         return int(_lib.load().qd_batch_step_kernels(self._h))
+
+    def inject_stall(self) -> None:
+        """Test hook: one CTA of the next tensor-core GEMM withholds its first
+        activation tiles, so its bounded waits run out (qd_batch_inject_stall)."""
+        check(_lib.load().qd_batch_inject_stall(self._h))
 
     # ---- vocabulary-sharded LM head (qd_batch_set_vocab_shard) ----------------------------
     def set_vocab_shard(self, rank: int, world: int, device=None) -> dict:
