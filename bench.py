@@ -45,10 +45,18 @@ WORKLOAD = ("batch-1 greedy decode, Qwen3-0.6B shape (28 layers, hidden 1024, 16
 METRIC, UNIT = "decode tok/s", "tok/s"
 B64, B64_CTX, B64_SEED = 64, 2048, 3
 PF_PROMPTS, PF_LEN, PF_NEW, PF_SEED = 32, 512, 16, 4
+B64_STEPS, PF_STEPS = 128, 10   # steps of the config-3 / config-4 objects of the default line
 WORKLOAD_PF = ("prefill, Qwen3-0.6B shape: 32 prompts x 512 random ids (seed 4) as tcgen05 dequant-GEMMs over all "
                "prompt rows with causal GQA attention (mma.sync), then 16 greedy decode tokens per prompt")
 WORKLOAD_B64 = ("batched greedy decode, Qwen3-0.6B shape, 64 independent sequences per GPU, each over a "
                 "2048-position f16 KV context from seeded synthetic hidden states (seed 3), tcgen05 GEMMs")
+
+
+def b1_config(world: int) -> dict:
+    """The config object of the batch-1 line (the GPU arm and the reference arm alike)."""
+    return {"workload": WORKLOAD, "global_batch": world, "seq_len": PROMPT_LEN + NEW_TOKENS,
+            "parallelism": f"replicas x{world} (batch-1 decode does not shard)",
+            "l2": "inputs larger than L2 (559 MB of weights streamed per token, L2 126 MB)"}
 
 
 def prompt_ids():
@@ -194,6 +202,10 @@ def max_over_ranks(x: float, world: int) -> float:
     return float(t.item())
 
 
+def _min_over_ranks(x: float, world: int) -> float:
+    return -max_over_ranks(-x, world)
+
+
 def prepare_runtime(world: int, rank: int) -> str:
     d = runtime_dir()
     if rank == 0:
@@ -238,14 +250,17 @@ def run_reference(args, world, rank):
     O.lib().qo_set_num_threads(len(os.sched_getaffinity(0)))
     rt = runtime_dir()
     synth.ensure_runtime(rt, synth.QWEN3_0_6B, seed=2)
-    steps = max(1, min(args.steps, 48))
-    tps, cores, n = time_cpu_decode(rt, steps, max(1, min(args.warmup, 4)))
-    sample = f"{n} decode tokens of the batch-1 workload (positions 7..30, after an 8-token prefill)"
+    # the GPU arm's steps and warm-up (each step is one ~30 ms oracle token: a
+    # default-length run stays within a few minutes)
+    steps, warm = max(1, min(args.steps, 2000)), max(args.warmup, 3)
+    tps, cores, n = time_cpu_decode(rt, steps, warm)
+    sample = (f"{n} decode tokens of the batch-1 workload (positions 7..30, after an 8-token prefill), "
+              f"on rank 0's host cores")
     line = {"metric": METRIC, "value": round(tps, 4), "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
-            "steps": n, "warmup": max(1, min(args.warmup, 4)), "ms_per_step": round(1000.0 / tps, 3),
+            "steps": n, "warmup": warm, "ms_per_step": round(1000.0 / tps, 3),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded random-init weights, reference runtime layout)",
-            "config": {"workload": WORKLOAD, "parallelism": "host cores (OpenMP)"},
+            "config": b1_config(world),
             "cpu_baseline": {"value": round(tps, 4), "unit": UNIT, "cores": cores, "kind": "port",
                              "sample": sample},
             "e2e": {"value": round(tps, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -392,6 +407,16 @@ def run_ours(args, world, rank, local):
     t_e2e = max_over_ranks(t_e2e, world)
     e2e = world * n_e2e * NEW_TOKENS / t_e2e
 
+    eng.close()
+    sub = {}
+    if not args.b1_only:
+        # configs 3 and 4 in the same run (every rank takes part: collectives inside)
+        sub["b64"] = measure_b64(args, world, rank, local, B64_STEPS, 3)
+        if world > 1:
+            sub["b64_vocab_shard"] = measure_b64(args, world, rank, local, B64_STEPS, 3, vocab_shard=True,
+                                                 with_cpu=False)
+        sub["prefill"] = measure_prefill(args, world, rank, local, PF_STEPS, 3)
+
     extra = {}
     cpu = None
     if rank == 0 and world == 1:
@@ -401,7 +426,6 @@ def run_ours(args, world, rank, local):
             cpu = {"value": round(tps, 4), "unit": UNIT, "cores": cores, "kind": "port",
                    "sample": f"{n} decode tokens of the batch-1 workload (positions 7..30) on the host "
                              f"cores, WGSL math restated in C (OpenMP)"}
-    eng.close()
     if rank == 0:
         clocks = clk.summary()
         line = {
@@ -409,9 +433,7 @@ def run_ours(args, world, rank, local):
             "warmup": max(args.warmup, 3), "ms_per_step": round(ms_per_step, 5), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded random-init weights, reference runtime layout)",
-            "config": {"workload": WORKLOAD, "global_batch": world, "seq_len": PROMPT_LEN + NEW_TOKENS,
-                       "parallelism": f"replicas x{world} (batch-1 decode does not shard)",
-                       "l2": "inputs larger than L2 (559 MB of weights streamed per token, L2 126 MB)"},
+            "config": b1_config(world),
             "roofline": {"bound": "hbm", "kernel": token_kernel_desc,
                          "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4),
@@ -429,12 +451,16 @@ def run_ours(args, world, rank, local):
         }
         if cpu:
             line["cpu_baseline"] = cpu
+        line.update({k: v for k, v in sub.items() if v is not None})
         print(json.dumps(line), flush=True)
     return 0
 
 
-def run_b64(args, world, rank, local):
-    """Config 3: 64 sequences per GPU, 2048-position context, greedy steps."""
+def measure_b64(args, world, rank, local, steps, warmup, vocab_shard=False, with_cpu=True):
+    """Config 3: 64 sequences per GPU over a 2048-position context, `steps` greedy
+    steps; the line's fields (rank 0) or None. With vocab_shard the LM head is split
+    by vocabulary over the ranks (two NCCL all-gathers per step); the sharded ids of
+    the first steps are checked against the replicated head's on the same batch."""
     import torch
 
     from kernel_optimization_webgpu_b200 import runtime as R
@@ -442,8 +468,9 @@ def run_b64(args, world, rank, local):
     rt = prepare_runtime(world, rank)
     peak, peak_kind = peaks()
     shape = synth.QWEN3_0_6B
-    warm = max(args.warmup, 3)
-    max_seq = B64_CTX + warm + args.steps + 1
+    warm = max(warmup, 3)
+    parity_steps = 4 if vocab_shard else 0
+    max_seq = B64_CTX + warm + steps + parity_steps + 1
     nb = args.batch
     eng = R.Engine(rt, device=local, max_seq=64)
     stream = torch.cuda.Stream()
@@ -454,12 +481,12 @@ def run_b64(args, world, rank, local):
     t0 = time.perf_counter()
     bt.fill_context(B64_CTX, B64_SEED + rank)
     fill_s = time.perf_counter() - t0
-    bt.set_tokens(tokens, [B64_CTX] * nb)
     gather = None
-    if args.vocab_shard:
+    shard_parity, allgather_ms = None, None
+    if vocab_shard:
         import torch.distributed as dist
 
-        bt.set_vocab_shard(rank, world)
+        bufs = bt.set_vocab_shard(rank, world)
 
         def gather(out, inp):
             if world > 1:
@@ -467,14 +494,24 @@ def run_b64(args, world, rank, local):
             elif out.data_ptr() != inp.data_ptr():
                 out.view(inp.shape).copy_(inp)
 
+        # parity: the same steps with the replicated LM head, then sharded
+        bt.set_tokens(tokens, [B64_CTX] * nb)
+        want = bt.decode(parity_steps)
+        bt.set_tokens(tokens, [B64_CTX] * nb)
+        with torch.cuda.stream(stream):
+            got = bt.decode_sharded(parity_steps, gather)
+        same = float(np.array_equal(want, got))
+        shard_parity = bool(_min_over_ranks(same, world) == 1.0)
+    bt.set_tokens(tokens, [B64_CTX] * nb)
+    if vocab_shard:
         with torch.cuda.stream(stream):
             bt.decode_sharded(warm, gather)
     else:
         bt.decode(warm, want_ids=False)
     step_kernels = bt.step_kernels
 
-    # timed: exactly K steps, device time with events on the engine's stream (synchronised around)
-    positions = [B64_CTX + warm + i for i in range(args.steps)]
+    # timed: exactly `steps` steps, device time with events on the engine's stream
+    positions = [B64_CTX + warm + i for i in range(steps)]
     barrier(world)
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -482,20 +519,37 @@ def run_b64(args, world, rank, local):
         with torch.cuda.stream(stream):
             torch.cuda._sleep(20_000_000)  # hold the stream while the host enqueues
         e0.record(stream)
-        if args.vocab_shard:
+        if vocab_shard:
             with torch.cuda.stream(stream):
-                bt.decode_sharded(args.steps, gather)
+                bt.decode_sharded(steps, gather)
         else:
-            bt.decode(args.steps, want_ids=False)
+            bt.decode(steps, want_ids=False)
         e1.record(stream)
         e1.synchronize()
     torch.cuda.synchronize()
     barrier(world)
     t_local = e0.elapsed_time(e1) / 1000.0
     t_max = max_over_ranks(t_local, world)
-    value = world * nb * args.steps / t_max
+    value = world * nb * steps / t_max
     step_bytes = sum(batch_step_bytes(shape, [p] * nb) for p in positions) / len(positions)
-    achieved = step_bytes / (t_local / args.steps) / 1e9
+    if vocab_shard:  # each rank reads only its slice of the LM-head table
+        step_bytes -= shape.vocab * shape.hidden * 2 * (world - 1) / world
+    achieved = step_bytes / (t_local / steps) / 1e9
+
+    if vocab_shard:
+        # the step's two collectives alone, same sizes, same stream
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier(world)
+        torch.cuda.synchronize()
+        with torch.cuda.stream(stream):
+            a0.record(stream)
+            for _ in range(steps):
+                for key in ("gather_hi", "gather_lo"):
+                    gather(bufs[key], bufs[key][rank * nb:(rank + 1) * nb])
+                gather(bufs["pairs_all"], bufs["pairs_local"])
+            a1.record(stream)
+        a1.synchronize()
+        allgather_ms = max_over_ranks(a0.elapsed_time(a1) / steps, world)
 
     # e2e: host tokens and positions in, host ids out, through the public calls
     bt.set_tokens(tokens, [B64_CTX] * nb)
@@ -503,54 +557,65 @@ def run_b64(args, world, rank, local):
     torch.cuda.synchronize()
     t0 = time.perf_counter()
     bt.set_tokens(tokens, [B64_CTX] * nb)
-    if args.vocab_shard:
+    if vocab_shard:
         with torch.cuda.stream(stream):
-            ids = bt.decode_sharded(args.steps, gather)
+            ids = bt.decode_sharded(steps, gather)
     else:
-        ids = bt.decode(args.steps)
+        ids = bt.decode(steps)
     t_e2e = max_over_ranks(time.perf_counter() - t0, world)
-    e2e = world * nb * args.steps / t_e2e
+    e2e = world * nb * steps / t_e2e
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu:
+    if rank == 0 and world == 1 and with_cpu and not args.no_cpu:
         cpu = time_cpu_batched(rt, bt)
     bt.close()
     eng.close()
-    if rank == 0:
-        line = {
-            "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": warm, "ms_per_step": round(t_max * 1000.0 / args.steps, 5), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic (seeded random-init weights and context, reference runtime layout)",
-            "config": {"workload": WORKLOAD_B64 if nb == B64 else WORKLOAD_B64.replace("64 independent", f"{nb} independent"),
-                       "global_batch": nb * world, "seq_len": max_seq,
-                       "parallelism": (f"sequences sharded: {nb} per GPU x {world}; LM head split by vocabulary "
-                                       f"over the {world} ranks (NCCL all-gathers of the final-norm rows and of the "
-                                       f"(index, max) pairs)") if args.vocab_shard else
-                                      f"sequences sharded: {nb} per GPU x {world} (no collective)",
-                       "l2": "inputs larger than L2 (about 15.5 GB of KV plus 559 MB of weights per step)",
-                       "context_fill_s": round(fill_s, 3)},
-            "roofline": {"bound": "hbm", "kernel": "decode step of 64 sequences (one CUDA graph: 28 layers x "
-                                                   "10 kernels + LM head/argmax)",
-                         "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(achieved / peak, 4), "traffic": None,
-                         "bytes_per_step": int(step_bytes), "peak_source": peak_kind},
-            "e2e": {"value": round(e2e, 2), "unit": UNIT, "h2d_bytes_per_step": round(2 * nb * 4 / args.steps, 2),
-                    "d2h_bytes_per_step": nb * 4,
-                    "step": f"qd_batch_set_tokens (64 ids + positions in) + qd_batch_decode({args.steps}) "
-                            "with every generated id copied out"},
-            "gpu_launches": args.steps * step_kernels,
-            "clocks": clk.summary(),
-            "generated_ids_sample": ids[:2, :4].tolist(),
-        }
-        if cpu:
-            line["cpu_baseline"] = cpu
+    if rank != 0:
+        return None
+    par = (f"sequences sharded: {nb} per GPU x {world}; LM head split by vocabulary over the {world} ranks "
+           f"(NCCL all-gathers of the final-norm rows and of the (index, max) pairs)") if vocab_shard else \
+        f"sequences sharded: {nb} per GPU x {world} (no collective)"
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": steps,
+        "warmup": warm, "ms_per_step": round(t_max * 1000.0 / steps, 5), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded random-init weights and context, reference runtime layout)",
+        "config": {"workload": WORKLOAD_B64 if nb == B64 else WORKLOAD_B64.replace("64 independent", f"{nb} independent"),
+                   "global_batch": nb * world, "seq_len": max_seq, "parallelism": par,
+                   "l2": "inputs larger than L2 (about 15.5 GB of KV plus 559 MB of weights per step)",
+                   "context_fill_s": round(fill_s, 3)},
+        "roofline": {"bound": "hbm", "kernel": f"decode step of {nb} sequences (one CUDA graph: 28 layers x "
+                                               "10 kernels + LM head/argmax)",
+                     "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": None,
+                     "bytes_per_step": int(step_bytes), "peak_source": peak_kind},
+        "e2e": {"value": round(e2e, 2), "unit": UNIT, "h2d_bytes_per_step": round(2 * nb * 4 / steps, 2),
+                "d2h_bytes_per_step": nb * 4,
+                "step": f"qd_batch_set_tokens ({nb} ids + positions in) + qd_batch_decode({steps}) "
+                        "with every generated id copied out"},
+        "gpu_launches": steps * step_kernels,
+        "clocks": clk.summary(),
+        "generated_ids_sample": ids[:2, :4].tolist(),
+    }
+    if vocab_shard:
+        line["shard_parity"] = shard_parity
+        line["shard_parity_steps"] = parity_steps
+        line["allgather_ms_per_step"] = round(allgather_ms, 5)
+    if cpu:
+        line["cpu_baseline"] = cpu
+    return line
+
+
+def run_b64(args, world, rank, local):
+    line = measure_b64(args, world, rank, local, args.steps, args.warmup, args.vocab_shard)
+    if line is not None:
         print(json.dumps(line), flush=True)
     return 0
 
 
-def run_prefill(args, world, rank, local):
-    """Config 4: 32 prompts x 512 ids prefilled together (split over the ranks), then 16 tokens."""
+def measure_prefill(args, world, rank, local, steps, warmup, with_cpu=True):
+    """Config 4: 32 prompts x 512 ids prefilled together (split over the ranks), then
+    16 tokens; the line's fields (rank 0) or None."""
     import torch
 
     from kernel_optimization_webgpu_b200 import runtime as R
@@ -568,7 +633,7 @@ def run_prefill(args, world, rank, local):
     stream = torch.cuda.Stream()
     eng.set_stream(stream)
     bt = R.Batch(eng, mine, PF_LEN + PF_NEW)
-    warm = max(args.warmup, 3)
+    warm = max(warmup, 3)
     for _ in range(warm):
         bt.prefill(ids)
     barrier(world)
@@ -578,12 +643,12 @@ def run_prefill(args, world, rank, local):
         with torch.cuda.stream(stream):
             torch.cuda._sleep(20_000_000)
         e0.record(stream)
-        for _ in range(args.steps):
+        for _ in range(steps):
             first = bt.prefill(ids)
         e1.record(stream)
         e1.synchronize()
     barrier(world)
-    t_local = e0.elapsed_time(e1) / 1000.0 / args.steps
+    t_local = e0.elapsed_time(e1) / 1000.0 / steps
     t_max = max_over_ranks(t_local, world)
     value = PF_PROMPTS * PF_LEN / t_max
     flops_local = prefill_flops(shape, mine, PF_LEN)
@@ -599,15 +664,15 @@ def run_prefill(args, world, rank, local):
     barrier(world)
     torch.cuda.synchronize()
     t0 = time.perf_counter()
-    for _ in range(args.steps):
+    for _ in range(steps):
         bt.prefill(ids)
-    t_e2e = max_over_ranks((time.perf_counter() - t0) / args.steps, world)
+    t_e2e = max_over_ranks((time.perf_counter() - t0) / steps, world)
     bt.close()
     eng.close()
     if rank == 0:
         line = {
             "metric": "prefill tok/s", "value": round(value, 1), "unit": "tok/s", "n_gpus": world,
-            "steps": args.steps, "warmup": warm, "ms_per_step": round(t_max * 1000.0, 4), "higher_is_better": True,
+            "steps": steps, "warmup": warm, "ms_per_step": round(t_max * 1000.0, 4), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f32 (f16 hi/lo tensor-core operands)",
             "data": "synthetic (seeded random-init weights and prompt ids, reference runtime layout)",
             "config": {"workload": WORKLOAD_PF, "global_batch": PF_PROMPTS, "seq_len": PF_LEN,
@@ -625,12 +690,19 @@ def run_prefill(args, world, rank, local):
             "e2e": {"value": round(PF_PROMPTS * PF_LEN / t_e2e, 1), "unit": "tok/s",
                     "h2d_bytes_per_step": mine * PF_LEN * 4, "d2h_bytes_per_step": mine * 4,
                     "step": "one qd_batch_prefill call: the prompts' ids in, each prompt's first id out"},
-            "gpu_launches": args.steps * (shape.layers * 8 + 3),  # per layer: 2 norms, 4 GEMMs, RoPE, attention
+            "gpu_launches": steps * (shape.layers * 8 + 3),  # per layer: 2 norms, 4 GEMMs, RoPE, attention
             "clocks": clk.summary(),
             "generated_ids_sample": [int(first[0])] + more[:3, 0].tolist(),
         }
-        if world == 1 and not args.no_cpu:
+        if world == 1 and with_cpu and not args.no_cpu:
             line["cpu_baseline"] = time_cpu_prefill(rt, all_ids[0])
+        return line
+    return None
+
+
+def run_prefill(args, world, rank, local):
+    line = measure_prefill(args, world, rank, local, args.steps, args.warmup)
+    if line is not None:
         print(json.dumps(line), flush=True)
     return 0
 
@@ -691,6 +763,8 @@ def main():
     ap.add_argument("--batch", type=int, default=B64, help="b64 workload: sequences per GPU (profiling cases)")
     ap.add_argument("--vocab-shard", action="store_true",
                     help="b64 workload: split the LM head by vocabulary over the ranks (NCCL all-gathers)")
+    ap.add_argument("--b1-only", action="store_true",
+                    help="default workload: skip the b64 / prefill objects of the line")
     ap.add_argument("--decode-only", action="store_true",
                     help="prefill + warm-up + timed decode steps only (for profiler launch lists)")
     args = ap.parse_args()

@@ -25,3 +25,8 @@ def test_reference_arm_prints_one_contract_line():
     e2e = d["e2e"]
     assert e2e["value"] == d["value"] and e2e["unit"] == d["unit"]
     assert e2e["h2d_bytes_per_step"] == 0 and e2e["d2h_bytes_per_step"] == 0
+    # the same config object and warm-up rule as the GPU arm's line
+    sys.path.insert(0, ROOT)
+    import bench
+    assert d["config"] == bench.b1_config(1)
+    assert d["warmup"] == 3 and d["steps"] == 2
