@@ -203,6 +203,48 @@ int qd_batch_step_lm_slice(qd_batch* b);
 int qd_batch_step_merge(qd_batch* b);
 int qd_batch_shard_sync(qd_batch* b, int steps, int32_t* out_ids);
 
+/* ---- the reference's benchmark exports -------------------------------------------
+ * runKernelBenchmarks(device, profile) (webgpu-runtime.js:62-96): each field is the
+ * reference's result field of the same name (camelCase there). Timings are CUDA-event
+ * milliseconds per launch over back-to-back launches on the engine's stream (the
+ * reference: wall clock per submit). Error fields compare the GPU result with a
+ * double-precision CPU evaluation of the same math (the reference's cpu* checks,
+ * errorStats :1540-1552). Inputs are the reference's own fixtures:
+ *  - q8 matvec hidden -> intermediate (runQ8Comparison :1438, createQ8Inputs :1464):
+ *    baseline = one thread per row, optimized = one warp per row with 128-bit loads;
+ *  - q8 MLP block rms -> gate/up -> silu*up -> down (runQwenMlpBlockComparison :1058);
+ *  - layer 0's resident q4 gate projection on sin(0.017 i) (runRealQwenQ4Projection :984);
+ *  - decode attention over 128 positions of createVector data (runGqaDecodeComparison :902);
+ *  - one decode layer (layer 0, position 0, input sin(0.013 i)) (runRealQwenLayer0Decode :614);
+ *  - RMSNorm of cos(0.013 i) (runRmsNorm :1636).
+ * The layer runs overwrite the engine's hidden state and KV row 0; the next
+ * generation starts from its own prompt as always. */
+typedef struct qd_kernel_bench {
+  double baseline_matvec_ms, optimized_matvec_ms, matvec_speedup;
+  double baseline_bytes, optimized_bytes, memory_reduction;
+  double max_abs_error, mean_abs_error;
+  double block_default_ms, block_optimized_ms, block_speedup, block_max_abs_error, block_mean_abs_error;
+  double real_q4_ms, real_q4_max_abs_error, real_q4_mean_abs_error;
+  double gqa_ms, gqa_max_abs_error, gqa_mean_abs_error;
+  int gqa_seq_len;
+  int layer0_finite;
+  double layer0_decode_ms, layer0_mean_abs;
+  double rms_ms, estimated_gbps;
+} qd_kernel_bench;
+int qd_run_kernel_benchmarks(qd_engine* e, qd_kernel_bench* out);
+
+/* runFullDecoderStackBenchmark(device, profile) (webgpu-runtime.js:98-163): every
+ * layer plus the final RMSNorm for one token whose hidden input is sin(0.013 i),
+ * at position 0 (attention over its own K/V only, as the reference's stack bench
+ * without a cache). warmup_ms is the first run, ms the second (CUDA events);
+ * finite / mean_abs describe the final-norm output. */
+typedef struct qd_stack_bench {
+  double ms, warmup_ms;
+  int layers, finite;
+  double mean_abs;
+} qd_stack_bench;
+int qd_run_full_decoder_stack_benchmark(qd_engine* e, qd_stack_bench* out);
+
 /* ---- failure-path test hooks ------------------------------------------------------
  * The reference's only failure detection is the A/B page's uncapturederror guard
  * (src/bench/ab-page.js:158-161,181-187), which refuses results after a device error.

@@ -36,6 +36,7 @@ EXPORTS = (
     "qd_batch_read_kv", "qd_batch_write_kv", "qd_batch_step_kernels", "qd_generate_batch",
     "qd_batch_set_vocab_shard", "qd_batch_step_layers", "qd_batch_step_lm_slice", "qd_batch_step_merge",
     "qd_batch_shard_sync", "qd_engine_inject_stall", "qd_batch_inject_stall",
+    "qd_run_kernel_benchmarks", "qd_run_full_decoder_stack_benchmark",
 )
 
 
@@ -55,6 +56,21 @@ class QdStats(C.Structure):
     _fields_ = [("generate_ms", C.c_double), ("first_token_ms", C.c_double),
                 ("steady_ms_per_token", C.c_double), ("generated_tokens", C.c_int),
                 ("prompt_tokens", C.c_int)]
+
+
+class QdKernelBench(C.Structure):
+    _fields_ = [(n, C.c_double) for n in (
+        "baseline_matvec_ms", "optimized_matvec_ms", "matvec_speedup", "baseline_bytes", "optimized_bytes",
+        "memory_reduction", "max_abs_error", "mean_abs_error", "block_default_ms", "block_optimized_ms",
+        "block_speedup", "block_max_abs_error", "block_mean_abs_error", "real_q4_ms", "real_q4_max_abs_error",
+        "real_q4_mean_abs_error", "gqa_ms", "gqa_max_abs_error", "gqa_mean_abs_error")] + [
+        ("gqa_seq_len", C.c_int), ("layer0_finite", C.c_int), ("layer0_decode_ms", C.c_double),
+        ("layer0_mean_abs", C.c_double), ("rms_ms", C.c_double), ("estimated_gbps", C.c_double)]
+
+
+class QdStackBench(C.Structure):
+    _fields_ = [("ms", C.c_double), ("warmup_ms", C.c_double), ("layers", C.c_int), ("finite", C.c_int),
+                ("mean_abs", C.c_double)]
 
 
 TOKEN_CB = C.CFUNCTYPE(C.c_int, C.c_int32, C.c_void_p)
@@ -172,6 +188,10 @@ def load(build_if_stale: bool = True):
         getattr(L, name).restype = i32
     L.qd_batch_shard_sync.argtypes = [vp, i32, vp]
     L.qd_batch_shard_sync.restype = i32
+    L.qd_run_kernel_benchmarks.argtypes = [vp, C.POINTER(QdKernelBench)]
+    L.qd_run_kernel_benchmarks.restype = i32
+    L.qd_run_full_decoder_stack_benchmark.argtypes = [vp, C.POINTER(QdStackBench)]
+    L.qd_run_full_decoder_stack_benchmark.restype = i32
     L.qd_engine_inject_stall.argtypes = [vp]
     L.qd_engine_inject_stall.restype = i32
     L.qd_batch_inject_stall.argtypes = [vp]

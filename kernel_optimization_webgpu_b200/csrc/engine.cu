@@ -147,7 +147,7 @@ void set_rows(StageArgs& a, const char* base, int k, bool pairs) {
   a.w_sub = a.s_sub = pairs ? rec : 0;
 }
 
-void enqueue_layer(qd_engine* e, int l, cudaStream_t s) {
+void enqueue_layer(qd_engine* e, int l, cudaStream_t s, bool embed_at_layer0 = true) {
   const qd_profile& p = e->p;
   const LayerDev& L = e->layers[l];
   const int qsize = p.heads * kHeadDim, kvsize = p.kv_heads * kHeadDim;
@@ -158,7 +158,7 @@ void enqueue_layer(qd_engine* e, int l, cudaStream_t s) {
     a.rows = e->rows_qkv; a.nb = p.hidden / kBlockCols; a.k_valid = p.hidden;
     a.src = e->h; a.norm_w = L.n_in; a.eps = p.eps; a.out = e->qkv;
     const StagePlan sp = plan_stage(a.rows, a.nb, e->sms);
-    if (l == 0) {
+    if (l == 0 && embed_at_layer0) {
       a.embed = e->embed; a.tokens = e->tokens; a.st = e->st; a.vocab = p.vocab; a.h_out = e->h;
       a.max_seq = e->opt.max_seq;
       launch_stage<kProEmbed, kEpiStore>(a, sp, s);
@@ -913,6 +913,31 @@ double ms_since(std::chrono::steady_clock::time_point t0) {
 }
 
 }  // namespace
+
+namespace qd {
+
+void bench_layer_from_hidden(qd_engine* e, int l, cudaStream_t s) { enqueue_layer(e, l, s, false); }
+
+void bench_set_position(qd_engine* e, int pos) { set_state(e, pos, 0); }
+
+void bench_check_state(qd_engine* e) { check_state(e); }
+
+void bench_rows_matvec(qd_engine* e, const char* base, long long row_stride, int rows, int k, const float* x,
+                       float* y, cudaStream_t s) {
+  StageArgs a{};
+  const long long nb = k / kBlockCols;
+  a.w = base;
+  a.s = base + nb * 16;
+  a.w_stride = a.s_stride = row_stride;
+  a.rows = rows;
+  a.nb = (int)nb;
+  a.k_valid = k;
+  a.src = x;
+  a.out = y;
+  launch_stage<kProPlain, kEpiStore>(a, plan_stage(rows, a.nb, e->sms), s);
+}
+
+}  // namespace qd
 
 // ---------------------------------------------------------------------------
 // ---- tcgen05 GEMM ---------------------------------------------------------------

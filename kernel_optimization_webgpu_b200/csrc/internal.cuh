@@ -92,6 +92,16 @@ void launch_gemm(TcArgs a, int splits, int mode, cudaStream_t s);
 // Splits actually used for K columns when `want` are asked for (no empty split).
 int gemm_plan_splits(int K, int want, int* kt_split);
 
+// Used by the benchmark entries (bench_api.cu), defined in engine.cu:
+// one decoder layer whose input is the engine's hidden vector (layer 0 included,
+// no embedding gather); the decode position the layer kernels read; the device
+// status check after a run; a q4 matvec over row records (row r at base + r * row_stride).
+void bench_layer_from_hidden(qd_engine* e, int l, cudaStream_t s);
+void bench_set_position(qd_engine* e, int pos);
+void bench_check_state(qd_engine* e);
+void bench_rows_matvec(qd_engine* e, const char* base, long long row_stride, int rows, int k, const float* x,
+                       float* y, cudaStream_t s);
+
 }  // namespace qd
 
 // Bytes of one q4 row record: nb 16-byte blocks then nb f16 scales, padded to 16.

@@ -115,10 +115,95 @@ napi_value GenerateGreedy(napi_env env, napi_callback_info info) {
   return res;
 }
 
+bool set_num(napi_env env, napi_value obj, const char* key, double value) {
+  napi_value v;
+  return napi_create_double(env, value, &v) == napi_ok && napi_set_named_property(env, obj, key, v) == napi_ok;
+}
+
+// kernelBenchmarks(engine) -> the runKernelBenchmarks result object (qd_run_kernel_benchmarks)
+napi_value KernelBenchmarks(napi_env env, napi_callback_info info) {
+  size_t argc = 1;
+  napi_value argv[1];
+  NAPI_OK(napi_get_cb_info(env, info, &argc, argv, nullptr, nullptr));
+  void* data = nullptr;
+  NAPI_OK(napi_get_value_external(env, argv[0], &data));
+  qd_engine* e = static_cast<qd_engine*>(data);
+  qd_kernel_bench b{};
+  const int rc = qd_run_kernel_benchmarks(e, &b);
+  if (rc != QD_OK) return throw_qd(env, e, rc);
+  napi_value r;
+  NAPI_OK(napi_create_object(env, &r));
+  const struct {
+    const char* key;
+    double value;
+  } fields[] = {
+      {"baselineMatvecMs", b.baseline_matvec_ms}, {"optimizedMatvecMs", b.optimized_matvec_ms},
+      {"matvecSpeedup", b.matvec_speedup}, {"baselineBytes", b.baseline_bytes},
+      {"optimizedBytes", b.optimized_bytes}, {"memoryReduction", b.memory_reduction},
+      {"maxAbsError", b.max_abs_error}, {"meanAbsError", b.mean_abs_error},
+      {"blockDefaultMs", b.block_default_ms}, {"blockOptimizedMs", b.block_optimized_ms},
+      {"blockSpeedup", b.block_speedup}, {"blockMaxAbsError", b.block_max_abs_error},
+      {"blockMeanAbsError", b.block_mean_abs_error}, {"realQ4Ms", b.real_q4_ms},
+      {"realQ4MaxAbsError", b.real_q4_max_abs_error}, {"realQ4MeanAbsError", b.real_q4_mean_abs_error},
+      {"gqaMs", b.gqa_ms}, {"gqaMaxAbsError", b.gqa_max_abs_error}, {"gqaMeanAbsError", b.gqa_mean_abs_error},
+      {"gqaSeqLen", (double)b.gqa_seq_len}, {"layer0DecodeMs", b.layer0_decode_ms},
+      {"layer0Finite", (double)b.layer0_finite}, {"layer0MeanAbs", b.layer0_mean_abs}, {"rmsMs", b.rms_ms},
+      {"estimatedGbps", b.estimated_gbps},
+  };
+  for (const auto& f : fields)
+    if (!set_num(env, r, f.key, f.value)) return throw_qd(env, e, QD_E_INVALID);
+  return r;
+}
+
+// engineProfile(engine) -> {layers, hidden, intermediate, heads, kvHeads, headDim, vocab}
+napi_value EngineProfile(napi_env env, napi_callback_info info) {
+  size_t argc = 1;
+  napi_value argv[1];
+  NAPI_OK(napi_get_cb_info(env, info, &argc, argv, nullptr, nullptr));
+  void* data = nullptr;
+  NAPI_OK(napi_get_value_external(env, argv[0], &data));
+  qd_engine* e = static_cast<qd_engine*>(data);
+  qd_profile p{};
+  const int rc = qd_engine_profile(e, &p);
+  if (rc != QD_OK) return throw_qd(env, e, rc);
+  napi_value r;
+  NAPI_OK(napi_create_object(env, &r));
+  if (!set_num(env, r, "layers", p.layers) || !set_num(env, r, "hidden", p.hidden) ||
+      !set_num(env, r, "intermediate", p.intermediate) || !set_num(env, r, "heads", p.heads) ||
+      !set_num(env, r, "kvHeads", p.kv_heads) || !set_num(env, r, "headDim", p.head_dim) ||
+      !set_num(env, r, "vocab", p.vocab))
+    return throw_qd(env, e, QD_E_INVALID);
+  return r;
+}
+
+// fullDecoderStackBenchmark(engine) -> {ms, warmupMs, layers, finite, meanAbs}
+napi_value FullDecoderStackBenchmark(napi_env env, napi_callback_info info) {
+  size_t argc = 1;
+  napi_value argv[1];
+  NAPI_OK(napi_get_cb_info(env, info, &argc, argv, nullptr, nullptr));
+  void* data = nullptr;
+  NAPI_OK(napi_get_value_external(env, argv[0], &data));
+  qd_engine* e = static_cast<qd_engine*>(data);
+  qd_stack_bench b{};
+  const int rc = qd_run_full_decoder_stack_benchmark(e, &b);
+  if (rc != QD_OK) return throw_qd(env, e, rc);
+  napi_value r;
+  NAPI_OK(napi_create_object(env, &r));
+  if (!set_num(env, r, "ms", b.ms) || !set_num(env, r, "warmupMs", b.warmup_ms) ||
+      !set_num(env, r, "layers", b.layers) || !set_num(env, r, "finite", b.finite) ||
+      !set_num(env, r, "meanAbs", b.mean_abs))
+    return throw_qd(env, e, QD_E_INVALID);
+  return r;
+}
+
 napi_value Init(napi_env env, napi_value exports) {
   napi_property_descriptor props[] = {
       {"engineCreate", nullptr, EngineCreate, nullptr, nullptr, nullptr, napi_default, nullptr},
       {"generateGreedy", nullptr, GenerateGreedy, nullptr, nullptr, nullptr, napi_default, nullptr},
+      {"engineProfile", nullptr, EngineProfile, nullptr, nullptr, nullptr, napi_default, nullptr},
+      {"kernelBenchmarks", nullptr, KernelBenchmarks, nullptr, nullptr, nullptr, napi_default, nullptr},
+      {"fullDecoderStackBenchmark", nullptr, FullDecoderStackBenchmark, nullptr, nullptr, nullptr, napi_default,
+       nullptr},
   };
   napi_define_properties(env, exports, sizeof(props) / sizeof(props[0]), props);
   return exports;

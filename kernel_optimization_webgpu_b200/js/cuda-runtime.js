@@ -1,7 +1,8 @@
-// Drop-in replacement for the decode exports of src/bench/webgpu-runtime.js,
-// backed by libqdecode.so through the Node-API addon (qdecode.node).
-// Same names, arguments, result object and over-length error as the reference
-// (createWebGpuContext :43-60, runCustomQwenGreedyPrompt :165-214).
+// Drop-in replacement for the exports of src/bench/webgpu-runtime.js, backed by
+// libqdecode.so through the Node-API addon (qdecode.node). Same names, arguments,
+// result objects and over-length error as the reference (createWebGpuContext
+// :43-60, runKernelBenchmarks :62-96, runFullDecoderStackBenchmark :98-163,
+// runCustomQwenGreedyPrompt :165-214).
 import { createRequire } from "node:module";
 
 const require = createRequire(import.meta.url);
@@ -56,4 +57,25 @@ export async function runCustomQwenGreedyPrompt({
     firstTokenMs: res.generated.length ? res.firstTokenMs : null,
     outputText: decodeToken ? decodeToken(res.generated) : res.generated.join(" "),
   };
+}
+
+function checkProfile(engineProfile, profile) {
+  for (const [key, ours] of [["hiddenSize", "hidden"], ["intermediateSize", "intermediate"],
+                             ["attentionHeads", "heads"], ["kvHeads", "kvHeads"], ["headDim", "headDim"]]) {
+    if (profile?.[key] !== undefined && engineProfile?.[ours] !== undefined && profile[key] !== engineProfile[ours]) {
+      throw new Error(`profile.${key}=${profile[key]} does not match the runtime (${engineProfile[ours]})`);
+    }
+  }
+}
+
+export async function runKernelBenchmarks(device, profile) {
+  const engine = engineFor(device, 1);
+  checkProfile(native.engineProfile(engine), profile);
+  return native.kernelBenchmarks(engine);
+}
+
+export async function runFullDecoderStackBenchmark(device, profile) {
+  const engine = engineFor(device, 1);
+  checkProfile(native.engineProfile(engine), profile);
+  return native.fullDecoderStackBenchmark(engine);
 }

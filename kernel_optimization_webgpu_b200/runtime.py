@@ -439,6 +439,53 @@ def runCustomQwenGreedyPrompt(*, device: CudaDevice, profile: dict, inputIds: Se
 
 run_custom_qwen_greedy_prompt = runCustomQwenGreedyPrompt
 
+# result field -> qd_kernel_bench member (runKernelBenchmarks, webgpu-runtime.js:62-96)
+_KERNEL_BENCH_FIELDS = {
+    "baselineMatvecMs": "baseline_matvec_ms", "optimizedMatvecMs": "optimized_matvec_ms",
+    "matvecSpeedup": "matvec_speedup", "baselineBytes": "baseline_bytes", "optimizedBytes": "optimized_bytes",
+    "memoryReduction": "memory_reduction", "maxAbsError": "max_abs_error", "meanAbsError": "mean_abs_error",
+    "blockDefaultMs": "block_default_ms", "blockOptimizedMs": "block_optimized_ms",
+    "blockSpeedup": "block_speedup", "blockMaxAbsError": "block_max_abs_error",
+    "blockMeanAbsError": "block_mean_abs_error", "realQ4Ms": "real_q4_ms",
+    "realQ4MaxAbsError": "real_q4_max_abs_error", "realQ4MeanAbsError": "real_q4_mean_abs_error",
+    "gqaMs": "gqa_ms", "gqaMaxAbsError": "gqa_max_abs_error", "gqaMeanAbsError": "gqa_mean_abs_error",
+    "gqaSeqLen": "gqa_seq_len", "layer0DecodeMs": "layer0_decode_ms", "layer0Finite": "layer0_finite",
+    "layer0MeanAbs": "layer0_mean_abs", "rmsMs": "rms_ms", "estimatedGbps": "estimated_gbps",
+}
+
+
+def _check_profile(eng: Engine, profile: dict) -> None:
+    p = eng.profile
+    for key, ours in (("hiddenSize", "hidden"), ("intermediateSize", "intermediate"),
+                      ("attentionHeads", "heads"), ("kvHeads", "kv_heads"), ("headDim", "head_dim")):
+        if key in profile and int(profile[key]) != p[ours]:
+            raise ValueError(f"profile.{key}={profile[key]} does not match the runtime ({p[ours]})")
+
+
+def runKernelBenchmarks(device: CudaDevice, profile: dict) -> dict:
+    """runKernelBenchmarks (webgpu-runtime.js:62-96) on the B200 engine: the same
+    result fields (qd_run_kernel_benchmarks)."""
+    eng = device.engine(1, "optimized")
+    _check_profile(eng, profile)
+    out = _lib.QdKernelBench()
+    check(_lib.load().qd_run_kernel_benchmarks(eng._h, C.byref(out)), eng._h)
+    return {js: getattr(out, c) for js, c in _KERNEL_BENCH_FIELDS.items()}
+
+
+def runFullDecoderStackBenchmark(device: CudaDevice, profile: dict) -> dict:
+    """runFullDecoderStackBenchmark (webgpu-runtime.js:98-163): {ms, warmupMs, layers,
+    finite, meanAbs} (qd_run_full_decoder_stack_benchmark)."""
+    eng = device.engine(1, "optimized")
+    _check_profile(eng, profile)
+    out = _lib.QdStackBench()
+    check(_lib.load().qd_run_full_decoder_stack_benchmark(eng._h, C.byref(out)), eng._h)
+    return {"ms": out.ms, "warmupMs": out.warmup_ms, "layers": out.layers, "finite": out.finite,
+            "meanAbs": out.mean_abs}
+
+
+run_kernel_benchmarks = runKernelBenchmarks
+run_full_decoder_stack_benchmark = runFullDecoderStackBenchmark
+
 
 # ---- kernel level (torch CUDA tensors as device memory) -------------------------
 
@@ -510,5 +557,6 @@ def gqa_decode(q, k_cache, v_cache, seq_len: int, q_heads: int, kv_heads: int, y
     return y
 
 
-__all__ = ["Engine", "QdError", "createWebGpuContext", "runCustomQwenGreedyPrompt", "qwen_profile",
+__all__ = ["Engine", "QdError", "createWebGpuContext", "runCustomQwenGreedyPrompt", "runKernelBenchmarks",
+           "runFullDecoderStackBenchmark", "qwen_profile",
            "qwenProfile", "q4_matvec", "lm_head_argmax", "gqa_decode", "LmHeadWorkspace"]

@@ -168,3 +168,17 @@ def test_bindings_match_the_declared_return_types():
         assert getattr(L, name).restype is want[ret], (name, ret)
         seen += 1
     assert seen == len(header_functions())
+
+
+def test_js_shim_exports_the_reference_functions():
+    """The JS shim exports the four functions of src/bench/webgpu-runtime.js that callers
+    import (createWebGpuContext, runKernelBenchmarks, runFullDecoderStackBenchmark,
+    runCustomQwenGreedyPrompt), and the addon registers every native call the shim uses."""
+    js = open(os.path.join(ROOT, "kernel_optimization_webgpu_b200", "js", "cuda-runtime.js")).read()
+    exported = set(re.findall(r"export async function (\w+)", js))
+    assert exported == {"createWebGpuContext", "runKernelBenchmarks", "runFullDecoderStackBenchmark",
+                        "runCustomQwenGreedyPrompt"}
+    used = set(re.findall(r"native\.(\w+)\(", js))
+    addon = open(os.path.join(ROOT, "kernel_optimization_webgpu_b200", "js", "addon.cc")).read()
+    registered = set(re.findall(r'\{"(\w+)", nullptr,', addon))
+    assert used and used <= registered, used - registered
