@@ -242,6 +242,7 @@ PArgs persist_args(qd_engine* e, bool with_head) {
   a.logits = e->logits; a.part_v = e->lm_pv; a.part_i = e->lm_pi; a.counter = e->lm_counter;
   a.with_head = with_head ? 1 : 0; a.lm_rows = e->lm_rows; a.timeline = e->timeline;
   a.rec_h = rec_bytes(p.hidden); a.rec_q = rec_bytes(p.heads * kHeadDim); a.rec_i = rec_bytes(p.intermediate);
+  a.OS = e->os; a.rec_og = e->rec_og; a.oslice_rows = e->oslice_rows; a.oacc = e->oacc;
   return a;
 }
 
@@ -262,6 +263,26 @@ cudaError_t prepare_persist_t(size_t smem, int* blocks) {
   return cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks, k_decode_persistent<G, KVT>, kPT, smem);
 }
 
+// Packs, for one layer, the O-projection slices of the fused attention stage: slice
+// (g, s) holds rows [H s / OS, H (s+1) / OS) restricted to KV head g's G * 128 input
+// columns, as row records (G * 4 q4 blocks, their f16 scales, padding to 16 bytes).
+__global__ void k_pack_oslices(const char* o, char* dst, int H, int NKV, int OS, int G, long long rec_q, int nbq,
+                               long long rec_og, long long rows_max) {
+  const int nbg = G * 4;  // 32-column blocks of one KV head's columns
+  const long long n = (long long)NKV * OS * rows_max;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const int slice = (int)(i / rows_max), rl = (int)(i % rows_max);
+    const int g = slice / OS, s = slice % OS;
+    const int lo = (int)((long long)H * s / OS), hi = (int)((long long)H * (s + 1) / OS);
+    char* out = dst + i * rec_og;
+    for (long long b = 0; b < rec_og; ++b) out[b] = 0;
+    if (lo + rl >= hi) continue;
+    const char* row = o + (long long)(lo + rl) * rec_q;
+    for (int b = 0; b < nbg * 16; ++b) out[b] = row[(long long)g * nbg * 16 + b];
+    for (int b = 0; b < nbg * 2; ++b) out[nbg * 16 + b] = row[(long long)nbq * 16 + (long long)g * nbg * 2 + b];
+  }
+}
+
 // Decide whether the persistent kernel fits this shape and device; set it up if so.
 void setup_persist(qd_engine* e) {
   const qd_profile& p = e->p;
@@ -272,13 +293,18 @@ void setup_persist(qd_engine* e) {
   cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, e->dev);
   cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, e->dev);
   const long long rec_h = rec_bytes(H), rec_q = rec_bytes(QS), rec_i = rec_bytes(I);
+  // attention CTAs per KV head: each owns H / OS rows of the O projection
+  const int OS = std::min(16, g / std::max(1, p.kv_heads));
+  const long long rec_og = rec_bytes(G * kHeadDim), oslice_rows = OS > 0 ? (H + OS - 1) / OS : 0;
   bool ok = e->opt.persistent && coop && G <= 2 && H <= 1024 && QS <= 2048 && I <= 3072 && p.kv_heads <= g &&
-            per_cta(R, rec_h) <= kSlotBytes && per_cta(H, rec_q) <= kSlotBytes &&
-            per_cta(I, 2 * rec_h) <= kSlotBytes && per_cta(H, rec_i) <= kSlotBytes && 2LL * H <= kSlotBytes;
+            OS >= 1 && oslice_rows <= kMaxRes && oslice_rows * rec_og <= kSlotBytes &&
+            per_cta(R, rec_h) <= kSlotBytes && per_cta(I, 2 * rec_h) <= kSlotBytes && per_cta(H, rec_i) <= kSlotBytes &&
+            2LL * H <= kSlotBytes;
   if (!ok) return;
   const int maxk = std::max(std::max(H, QS), I);
   const long long xs_floats = std::max<long long>(maxk, (long long)kPW * G * kHeadDim);
-  const long long misc_floats = std::max<long long>((G + 2) * kHeadDim + G * kHeadDim + 2 * kHeadDim + 2 * kPW * G, 2 * kPW);
+  const long long misc_floats =
+      std::max<long long>((G + 2) * kHeadDim + G * kHeadDim + 2 * kHeadDim + 2 * kPW * G + G * 64, 2 * kPW);
   const size_t smem = (size_t)kSlots * kSlotBytes + (size_t)(xs_floats + 2 * H) * 4 + kSlots * 8 + kPW * 4 + 16 +
                       (size_t)(kMaxRes + misc_floats) * 4;
   // per-CTA row counts must fit the stage result buffer
@@ -298,10 +324,26 @@ void setup_persist(qd_engine* e) {
   const size_t xbytes = (size_t)(p.layers + 1) * e->xstride * 8;
   if (cudaMalloc(&e->xbuf, xbytes) != cudaSuccess) throw QdError{QD_E_NOMEM, "cannot allocate exchange buffers"};
   QD_CK(cudaMemset(e->xbuf, 0, xbytes));
+  // O slices of the fused attention stage, and their double-buffered sums
+  e->os = OS;
+  e->rec_og = rec_og;
+  e->oslice_rows = oslice_rows;
+  const long long slices_per_layer = (long long)p.kv_heads * OS * oslice_rows * rec_og;
+  if (cudaMalloc(&e->oslices, (size_t)slices_per_layer * p.layers) != cudaSuccess)
+    throw QdError{QD_E_NOMEM, "cannot allocate the packed O slices"};
+  for (int l = 0; l < p.layers; ++l)
+    k_pack_oslices<<<64, 256, 0, e->stream>>>(e->layers[l].o, e->oslices + (size_t)slices_per_layer * l, H,
+                                              p.kv_heads, OS, G, rec_q, QS / kBlockCols, rec_og, oslice_rows);
+  QD_CK(cudaGetLastError());
+  QD_CK(cudaStreamSynchronize(e->stream));
+  const size_t acc_bytes = (size_t)2 * p.layers * H * 8;
+  if (cudaMalloc(&e->oacc, acc_bytes) != cudaSuccess) throw QdError{QD_E_NOMEM, "cannot allocate the O sums"};
+  QD_CK(cudaMemset(e->oacc, 0, acc_bytes));
   std::vector<PLayer> pl(p.layers);
   for (int l = 0; l < p.layers; ++l) {
     const LayerDev& L = e->layers[l];
-    pl[l] = PLayer{L.qkv, L.o, L.gu, L.d, L.n_in, L.n_q, L.n_k, L.n_post, L.kc, L.vc};
+    pl[l] = PLayer{L.qkv, L.o, L.gu, L.d, L.n_in, L.n_q, L.n_k, L.n_post, L.kc, L.vc,
+                   e->oslices + (size_t)slices_per_layer * l};
   }
   if (cudaMalloc(&e->d_players, sizeof(PLayer) * p.layers) != cudaSuccess)
     throw QdError{QD_E_NOMEM, "cannot allocate the layer table"};
@@ -860,6 +902,8 @@ void free_engine(qd_engine* e) {
   if (e->c_acc) cudaFree(e->c_acc);
   if (e->c_cnt) cudaFree(e->c_cnt);
   if (e->d_players) cudaFree(e->d_players);
+  if (e->oslices) cudaFree(e->oslices);
+  if (e->oacc) cudaFree(e->oacc);
   if (e->timeline) cudaFree(e->timeline);
   if (e->out_host) cudaFreeHost(e->out_host);
   if (e->pinned_ids) cudaFreeHost(e->pinned_ids);
@@ -897,6 +941,8 @@ void check_state(qd_engine* e) {
     e->pinned_state->stall_epoch = 0;
     QD_CK(cudaMemcpyAsync(e->st, e->pinned_state, sizeof(DevState), cudaMemcpyHostToDevice, e->stream));
     QD_CK(cudaMemsetAsync(e->lm_counter, 0, 4, e->stream));
+    if (e->oacc)  // a failed launch may leave partial O sums in its parity
+      QD_CK(cudaMemsetAsync(e->oacc, 0, (size_t)2 * e->p.layers * e->p.hidden * 8, e->stream));
     if (e->clus) {  // a failed launch may leave partial sums and counts in either parity
       QD_CK(cudaMemsetAsync(e->c_acc, 0, (size_t)2 * e->p.layers * 2 * e->p.hidden * 8, e->stream));
       QD_CK(cudaMemsetAsync(e->c_cnt, 0, (size_t)2 * e->p.layers * 2 * 32 * 4, e->stream));
@@ -906,6 +952,8 @@ void check_state(qd_engine* e) {
   if (err & kErrTimeout) throw QdError{QD_E_TIMEOUT, "device: a persistent-kernel wait expired; the launch was abandoned"};
   if (err & kErrToken) throw QdError{QD_E_DEVICE, "device: token id outside the vocabulary"};
   if (err & kErrPosition) throw QdError{QD_E_DEVICE, "device: position beyond max_seq"};
+  if (err & kErrOverflow)
+    throw QdError{QD_E_DEVICE, "device: an attention output projection partial beyond the fixed-point range (2^22)"};
 }
 
 double ms_since(std::chrono::steady_clock::time_point t0) {

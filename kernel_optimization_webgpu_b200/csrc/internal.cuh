@@ -156,6 +156,10 @@ struct qd_engine {
   size_t persist_smem = 0;
   int lm_rows = 0;
   unsigned long long* timeline = nullptr;  // stage stamps of the last persistent launch (opt-in)
+  char* oslices = nullptr;                 // O rows x KV-head columns, packed per attention CTA
+  unsigned long long* oacc = nullptr;      // [2][L][H] counted fixed-point O sums
+  int os = 0;                              // attention CTAs per KV head
+  long long rec_og = 0, oslice_rows = 0;
   // cluster decode kernel (cluster.cuh)
   bool clus = false;
   int ncl = 0;                       // clusters of kCC CTAs

@@ -12,6 +12,15 @@
 // {f32 value, epoch}; consumers poll the words they need until each carries
 // this launch's epoch. Value and "ready" travel in one store, so a stage
 // boundary costs one store-to-load trip through L2 instead of a grid barrier.
+//
+// Attention and the O projection are one stage: OS CTAs per KV head each run
+// the head's attention (the same math, redundantly) and multiply it by their
+// slice of O rows x the head's columns; the KV-head partials are summed in
+// 64-bit counted fixed-point words (2^56 + round(v * 2^28) per contribution:
+// the top byte counts contributions, the rest is their exact sum, so the sum
+// does not depend on arrival order), and consumers poll those words until the
+// count reaches the number of KV heads. The accumulators are double-buffered
+// by launch parity; each launch zeroes the other parity for the next one.
 // Every wait has a deadline (globaltimer) and an abort flag: on expiry the
 // kernel sets an error bit, waits for its own copies in flight and returns.
 #pragma once
@@ -26,6 +35,7 @@ constexpr int kSlots = 8;                  // ring slots
 constexpr int kSlotBytes = 24576;          // per slot (the largest per-CTA slice at Qwen3-0.6B shapes)
 constexpr unsigned long long kWaitNs = 200ull * 1000 * 1000;  // deadline of any single wait
 constexpr int kErrTimeout = 4;             // DevErr bit: a wait expired (kernel aborted)
+constexpr int kErrOverflow = 16;           // DevErr bit: an O partial beyond the fixed-point range (clamped)
 constexpr int kMaxRes = 256;               // per-CTA row results of one stage (floats)
 constexpr unsigned kPollBackoffNs = 100;   // pause between re-polls of exchange words
 constexpr int kAttnPf = 2;                 // cached K/V rows each attention warp loads ahead
@@ -42,6 +52,9 @@ struct PLayer {
   const char *qkv, *o, *gu, *d;            // row records (gate/up: pair records)
   const float *n_in, *n_q, *n_k, *n_post;
   void *kc, *vc;
+  // O rows x one KV head's columns, packed per attention CTA: slice (g, s) at
+  // oslice + (g * OS + s) * oslice_rows * rec_og, rows of s's range as row records
+  const char* oslice;
 };
 
 struct PArgs {
@@ -62,6 +75,9 @@ struct PArgs {
   int lm_rows;                             // unused (kept for the host's slot-size check)
   unsigned long long* timeline;            // optional [gridDim.x][timeline_events(L)] stage stamps (ns)
   long long rec_h, rec_q, rec_i;           // row record bytes for K = H, NH*128, I
+  int OS;                                  // attention CTAs per KV head (each owns a slice of O rows)
+  long long rec_og, oslice_rows;           // O slice row record bytes (K = G*128), rows per slice (max)
+  unsigned long long* oacc;                // [2 parities][L][H] counted fixed-point O sums
 };
 
 // ---- small PTX helpers --------------------------------------------------------
@@ -145,6 +161,7 @@ struct PShared {
 // Row ranges of this CTA, computed once per launch.
 struct Ranges {
   int qkv_lo, qkv_hi, h_lo, h_hi, i_lo, i_hi, v_lo, v_hi;
+  int att, ag, as, o_lo, o_hi;             // attention role: KV head ag, O rows [o_lo, o_hi) (att = 0: none)
 };
 
 // The layer-weight chunk i of this CTA: chunks 4l..4l+3 are layer l's QKV, O,
@@ -153,7 +170,10 @@ __device__ __forceinline__ void chunk_src(const PArgs& a, const Ranges& rg, int 
   const PLayer& P = a.layers[i >> 2];
   switch (i & 3) {
     case 0: src = P.qkv + rg.qkv_lo * a.rec_h; bytes = (unsigned)((rg.qkv_hi - rg.qkv_lo) * a.rec_h); break;
-    case 1: src = P.o + rg.h_lo * a.rec_q; bytes = (unsigned)((rg.h_hi - rg.h_lo) * a.rec_q); break;
+    case 1:  // this attention CTA's O slice (nothing for the others)
+      src = P.oslice + (long long)(rg.ag * a.OS + rg.as) * a.oslice_rows * a.rec_og;
+      bytes = rg.att ? (unsigned)((rg.o_hi - rg.o_lo) * a.rec_og) : 0u;
+      break;
     case 2: src = P.gu + rg.i_lo * 2 * a.rec_h; bytes = (unsigned)((rg.i_hi - rg.i_lo) * 2 * a.rec_h); break;
     default: src = P.d + rg.h_lo * a.rec_i; bytes = (unsigned)((rg.h_hi - rg.h_lo) * a.rec_i); break;
   }
@@ -224,6 +244,76 @@ __device__ __forceinline__ bool stage_ok(const PArgs& a, bool mine) {
   return __syncthreads_and(mine ? 1 : 0) != 0;
 }
 
+// ---- counted fixed-point sums ------------------------------------------------------
+constexpr float kFxScale = 268435456.0f;              // 2^28
+constexpr float kFxInv = 3.7252902984619140625e-9f;   // 2^-28
+constexpr float kFxMax = 4194304.0f;                  // 2^22: 16 such partials still fit 55 bits
+
+__device__ __forceinline__ void red_fx(const PArgs& a, unsigned long long* p, float v) {
+  if (!(fabsf(v) < kFxMax)) {  // also catches NaN
+    atomicOr(&a.st->err, kErrOverflow);
+    v = v != v ? 0.0f : copysignf(kFxMax, v);
+  }
+  const long long q = __float2ll_rn(v * kFxScale);
+  asm volatile("red.relaxed.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"((1ull << 56) + (unsigned long long)q)
+               : "memory");
+}
+__device__ __forceinline__ unsigned fx_count(unsigned long long w) { return (unsigned)((w + (1ull << 55)) >> 56); }
+__device__ __forceinline__ float fx_value(unsigned long long w) {
+  const unsigned long long c = (w + (1ull << 55)) >> 56;
+  return __ll2float_rn((long long)(w - (c << 56))) * kFxInv;
+}
+
+// Every thread: poll counted words src[e], e = threadIdx.x + k*kPT < n (n <= 4 kPT),
+// until each holds `need` contributions; dst[e] = base[e] + sum. False on timeout/abort.
+__device__ __forceinline__ bool poll_fx(const PArgs& a, const unsigned long long* src, int n, unsigned need,
+                                        const float* base, float* dst) {
+  constexpr int K = 4;
+  unsigned long long v[K];
+  unsigned pend = 0;
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    const int e = threadIdx.x + k * kPT;
+    v[k] = 0ull;
+    if (e < n) {
+      v[k] = ld_word(src + e);
+      pend |= 1u << k;
+    }
+  }
+  unsigned long long t0 = 0;
+  for (unsigned it = 0;; ++it) {
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      if (((pend >> k) & 1u) && fx_count(v[k]) == need) {
+        pend &= ~(1u << k);
+        const int e = threadIdx.x + k * kPT;
+        dst[e] = base[e] + fx_value(v[k]);
+      }
+    }
+    if (!pend) return true;
+    if (it == 0) t0 = gtimer();
+    else if ((it & 15) == 0 && (aborted(a) || gtimer() - t0 > kWaitNs)) return false;
+    __nanosleep(kPollBackoffNs);
+#pragma unroll
+    for (int k = 0; k < K; ++k)
+      if ((pend >> k) & 1u) v[k] = ld_word(src + threadIdx.x + k * kPT);
+  }
+}
+
+// f16 rounding of a float4 as the f16 KV cache stores it (identity for an f32 cache).
+template <typename KVT> __device__ __forceinline__ float4 rnd4(float4 v);
+template <> __device__ __forceinline__ float4 rnd4<float>(float4 v) { return v; }
+template <> __device__ __forceinline__ float4 rnd4<__half>(float4 v) {
+  const float2 a = __half22float2(__floats2half2_rn(v.x, v.y)), b = __half22float2(__floats2half2_rn(v.z, v.w));
+  return make_float4(a.x, a.y, b.x, b.y);
+}
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
 // Sum over the warp of 4 per-lane values at once (transposing butterfly, 6
 // shuffles): on return lane l holds the total of value l >> 3.
 __device__ __forceinline__ float reduce4(float p0, float p1, float p2, float p3) {
@@ -288,6 +378,36 @@ __device__ __forceinline__ void stage_dots(const char* slot, int n_rows, int nw,
   }
 }
 
+// Block dots of n row records of NB (<= 32) blocks each: lane l owns block l % NB
+// of item (row) warp * (32 / NB) + l / NB + k * kPW * (32 / NB), so every lane does
+// one block dot per step and NB-lane groups reduce with log2(NB) shuffles.
+template <int NB>
+__device__ __forceinline__ void slice_dots(const char* slot, int n_rows, int rec, const float* xs, float* res) {
+  static_assert(NB == 4 || NB == 8 || NB == 16 || NB == 32, "power-of-two blocks per row");
+  constexpr int IPS = 32 / NB;  // items per warp step
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int b = lane % NB, sub = lane / NB;
+  float2 xr[16];
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    const float4 v = reinterpret_cast<const float4*>(xs)[xs_slot(b * 8 + q)];
+    xr[2 * q] = make_float2(v.x, v.y);
+    xr[2 * q + 1] = make_float2(v.z, v.w);
+  }
+  for (int i0 = warp * IPS; i0 < n_rows; i0 += kPW * IPS) {
+    const int it = i0 + sub;
+    float p = 0.0f;
+    if (it < n_rows) {
+      const char* r = slot + it * rec;
+      p = __half2float(reinterpret_cast<const __half*>(r + NB * 16)[b]) *
+          q4_block_dot(reinterpret_cast<const uint4*>(r)[b], xr);
+    }
+#pragma unroll
+    for (int o = NB / 2; o > 0; o >>= 1) p += __shfl_xor_sync(0xffffffffu, p, o);
+    if (b == 0 && it < n_rows) res[it] = p;
+  }
+}
+
 // Every thread: poll words src[e], e = threadIdx.x + k*kPT < n, into shared
 // memory (swizzled staging when swz, else dst[e]). A thread's words are
 // re-polled together, so it pays one round trip after its last word lands.
@@ -330,41 +450,65 @@ __device__ __forceinline__ bool poll_to_smem(const PArgs& a, const unsigned long
   }
 }
 
-// ---- attention for one KV head (G query heads) -----------------------------------
+// ---- attention for one KV head (G query heads) + this CTA's O-projection slice ----
+// Every CTA of the head's group runs the same attention (bitwise identically) and
+// multiplies its result by O rows [o_lo, o_hi) x the head's G*128 columns; the
+// partial goes to the counted fixed-point sums `acc`. Up to `cap` cached positions
+// (the K/V rows fit the activation staging area), the rows are copied into shared
+// memory while the q/k/v words are awaited and the scores, the softmax and the
+// weighted sum run position-parallel; longer contexts use a per-warp online softmax.
 template <int G, typename KVT>
-__device__ __forceinline__ bool attn_stage(const PArgs& a, const PShared& S, int l, int g, int pos, unsigned epoch,
-                           const unsigned long long* xq, unsigned long long* xo) {
+__device__ __forceinline__ bool attn_o_stage(const PArgs& a, const PShared& S, const Ranges& rg, int l, int pos,
+                                             unsigned epoch, const unsigned long long* xq, unsigned long long* acc,
+                                             int chunk, int xs_floats) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int g = rg.ag;
   const PLayer& P = a.layers[l];
   KVT* kc = reinterpret_cast<KVT*>(P.kc);
   KVT* vc = reinterpret_cast<KVT*>(P.vc);
   const long long row_el = (long long)a.NKV * kHeadDim;
   const int QS = a.NH * kHeadDim, KVS = a.NKV * kHeadDim;
-  float* raw = S.misc;                      // [(G + 2) * 128]
-  float* qs = raw + (G + 2) * kHeadDim;     // [G * 128]
-  float* kn = qs + G * kHeadDim;            // [128]
-  float* vn = kn + kHeadDim;                // [128]
-  float2* wml = reinterpret_cast<float2*>(vn + kHeadDim);  // [kPW * G]
+  float* raw = S.misc;                                      // [(G + 2) * 128]
+  float* qs = raw + (G + 2) * kHeadDim;                     // [G * 128]
+  float* kn = qs + G * kHeadDim;                            // [128]
+  float* vn = kn + kHeadDim;                                // [128]
+  float2* wml = reinterpret_cast<float2*>(vn + kHeadDim);   // [kPW * G]
+  float* scs = reinterpret_cast<float*>(wml + kPW * G);     // [G][64] scores / probabilities
+  float* ostage = S.has;                                    // the O dots' input (G * 128), swizzled
+  const int cap = min(63, (xs_floats * 4) / (2 * kHeadDim * (int)sizeof(KVT)));
+  const bool compact = pos <= cap;
+  KVT* Ks = reinterpret_cast<KVT*>(S.xs);                   // [cap][128] cached K rows (compact)
+  KVT* Vs = Ks + cap * kHeadDim;                            // [cap][128]
 
-  // Everything that does not depend on this token's q/k/v, loaded before the wait:
-  // the norm weights, this position's RoPE row and this warp's first cached K/V row.
+  // Everything that does not depend on this token's q/k/v, started before the wait:
+  // the norm weights, this position's RoPE row, and the cached K/V rows.
   const float4 wq4 = reinterpret_cast<const float4*>(P.n_q)[lane];
   const float4 wk4 = reinterpret_cast<const float4*>(P.n_k)[lane];
   const int pair0 = (4 * lane) & (kHeadDim / 2 - 1);
   const long long toff = (long long)pos * a.row_stride + pair0;
   const float4 cr = *reinterpret_cast<const float4*>(a.cos_t + toff);
   const float4 sr = *reinterpret_cast<const float4*>(a.sin_t + toff);
-  // This warp's first kAttnPf cached K/V rows (positions warp + j*kPW < pos),
-  // a software pipeline kAttnPf rows deep through the softmax loop below.
+  constexpr int kChunks = kHeadDim * (int)sizeof(KVT) / 16;  // 16-byte pieces of one row
   float4 kpf[kAttnPf], vpf[kAttnPf];
 #pragma unroll
-  for (int j = 0; j < kAttnPf; ++j) {
-    const int pp = warp + j * kPW;
-    kpf[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-    vpf[j] = kpf[j];
-    if (pp < pos) {
-      kpf[j] = ld4<KVT>(kc + pp * row_el + g * kHeadDim + 4 * lane);
-      vpf[j] = ld4<KVT>(vc + pp * row_el + g * kHeadDim + 4 * lane);
+  for (int j = 0; j < kAttnPf; ++j) kpf[j] = vpf[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (compact) {
+    for (int i = threadIdx.x; i < 2 * pos * kChunks; i += kPT) {
+      const int which = i / (pos * kChunks), r = i - which * pos * kChunks;
+      const int p = r / kChunks, c = r - p * kChunks;
+      const KVT* src = (which ? vc : kc) + p * row_el + g * kHeadDim;
+      KVT* dst = (which ? Vs : Ks) + p * kHeadDim;
+      cp_async16(reinterpret_cast<char*>(dst) + 16 * c, reinterpret_cast<const char*>(src) + 16 * c);
+    }
+    cp_async_commit();
+  } else {
+#pragma unroll
+    for (int j = 0; j < kAttnPf; ++j) {
+      const int pp = warp + j * kPW;
+      if (pp < pos) {
+        kpf[j] = ld4<KVT>(kc + pp * row_el + g * kHeadDim + 4 * lane);
+        vpf[j] = ld4<KVT>(vc + pp * row_el + g * kHeadDim + 4 * lane);
+      }
     }
   }
   // q heads g*G.., k head g, v head g from the QKV exchange words (one word per thread for G <= 2).
@@ -377,15 +521,17 @@ __device__ __forceinline__ bool attn_stage(const PArgs& a, const PShared& S, int
       ok = ok && poll_word(a, xq + src, epoch, raw[e]);
     }
   }
+  if (compact) cp_async_wait_all();
   if (!stage_ok(a, ok)) return false;
 
-  // head RMSNorm + RoPE (q heads, k), cache append (k, v)
+  // head RMSNorm + RoPE (q heads, k); the group's first CTA appends k, v to the cache
+  const bool owner = rg.as == 0;
   for (int t = warp; t < G + 2; t += kPW) {
     const float4 x = reinterpret_cast<const float4*>(raw + t * kHeadDim)[lane];
     KVT* krow = kc + (long long)pos * row_el + g * kHeadDim + 4 * lane;
     KVT* vrow = vc + (long long)pos * row_el + g * kHeadDim + 4 * lane;
     if (t == G + 1) {
-      reinterpret_cast<float4*>(vn)[lane] = st4<KVT>(vrow, x);
+      reinterpret_cast<float4*>(vn)[lane] = owner ? st4<KVT>(vrow, x) : rnd4<KVT>(x);
       continue;
     }
     const float4 w4 = t < G ? wq4 : wk4;
@@ -402,79 +548,140 @@ __device__ __forceinline__ bool attn_stage(const PArgs& a, const PShared& S, int
     const float4 r = make_float4(y.x * cr.x + sign * p.x * sr.x, y.y * cr.y + sign * p.y * sr.y,
                                  y.z * cr.z + sign * p.z * sr.z, y.w * cr.w + sign * p.w * sr.w);
     if (t < G) reinterpret_cast<float4*>(qs + t * kHeadDim)[lane] = r;
-    else reinterpret_cast<float4*>(kn)[lane] = st4<KVT>(krow, r);
+    else reinterpret_cast<float4*>(kn)[lane] = owner ? st4<KVT>(krow, r) : rnd4<KVT>(r);
   }
   __syncthreads();
 
-  // Online softmax per warp over positions warp, warp + kPW, ... <= pos.
-  float4 q[G];
+  if (compact) {
+    // scores: warp w takes positions w, w + kPW, ... <= pos
+    float4 q[G];
 #pragma unroll
-  for (int h = 0; h < G; ++h) q[h] = reinterpret_cast<const float4*>(qs + h * kHeadDim)[lane];
-  float m[G], lsum[G];
-  float4 acc[G];
+    for (int h = 0; h < G; ++h) q[h] = reinterpret_cast<const float4*>(qs + h * kHeadDim)[lane];
+    for (int p = warp; p <= pos; p += kPW) {
+      const float4 k4 = p == pos ? reinterpret_cast<const float4*>(kn)[lane] : ld4<KVT>(Ks + p * kHeadDim + 4 * lane);
+      float d[G];
 #pragma unroll
-  for (int h = 0; h < G; ++h) { m[h] = -INFINITY; lsum[h] = 0.0f; acc[h] = make_float4(0.f, 0.f, 0.f, 0.f); }
-  for (int p = warp; p <= pos; p += kPW) {
-    float4 k4 = kpf[0], v4 = vpf[0];
-    if (p == pos) {
-      k4 = reinterpret_cast<const float4*>(kn)[lane];
-      v4 = reinterpret_cast<const float4*>(vn)[lane];
-    }
+      for (int h = 0; h < G; ++h) d[h] = q[h].x * k4.x + q[h].y * k4.y + q[h].z * k4.z + q[h].w * k4.w;
 #pragma unroll
-    for (int j = 0; j + 1 < kAttnPf; ++j) {
-      kpf[j] = kpf[j + 1];
-      vpf[j] = vpf[j + 1];
+      for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+        for (int h = 0; h < G; ++h) d[h] += __shfl_xor_sync(0xffffffffu, d[h], o);
+      if (lane == 0)
+#pragma unroll
+        for (int h = 0; h < G; ++h) scs[h * 64 + p] = d[h] * a.scale;
     }
-    const int pn = p + kAttnPf * kPW;
-    if (pn < pos) {  // refill the pipeline kAttnPf rows ahead
-      kpf[kAttnPf - 1] = ld4<KVT>(kc + pn * row_el + g * kHeadDim + 4 * lane);
-      vpf[kAttnPf - 1] = ld4<KVT>(vc + pn * row_el + g * kHeadDim + 4 * lane);
+    __syncthreads();
+    // softmax of each head (warp h): probabilities in place
+    if (warp < G) {
+      const float s0 = lane <= pos ? scs[warp * 64 + lane] : -INFINITY;
+      const float s1 = lane + 32 <= pos ? scs[warp * 64 + lane + 32] : -INFINITY;
+      const float m = warp_max(fmaxf(s0, s1));
+      const float e0 = lane <= pos ? expf(s0 - m) : 0.0f, e1 = lane + 32 <= pos ? expf(s1 - m) : 0.0f;
+      const float inv = 1.0f / warp_sum(e0 + e1);
+      if (lane <= pos) scs[warp * 64 + lane] = e0 * inv;
+      if (lane + 32 <= pos) scs[warp * 64 + lane + 32] = e1 * inv;
     }
+    __syncthreads();
+    // weighted sum of the V rows: thread e -> (head e / 128, dim e % 128)
+    for (int e = threadIdx.x; e < G * kHeadDim; e += kPT) {
+      const int h = e / kHeadDim, d = e % kHeadDim;
+      const float* pr = scs + h * 64;
+      float o[4] = {pr[pos] * vn[d], 0.0f, 0.0f, 0.0f};
+      int p = 0;
+      for (; p + 4 <= pos; p += 4) {  // four independent chains: the loads go out together
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          float v;
+          if constexpr (sizeof(KVT) == 2) v = __half2float(reinterpret_cast<const __half*>(Vs)[(p + j) * kHeadDim + d]);
+          else v = reinterpret_cast<const float*>(Vs)[(p + j) * kHeadDim + d];
+          o[j] = fmaf(pr[p + j], v, o[j]);
+        }
+      }
+      for (; p < pos; ++p) {
+        float v;
+        if constexpr (sizeof(KVT) == 2) v = __half2float(reinterpret_cast<const __half*>(Vs)[p * kHeadDim + d]);
+        else v = reinterpret_cast<const float*>(Vs)[p * kHeadDim + d];
+        o[0] = fmaf(pr[p], v, o[0]);
+      }
+      xs_store(ostage, e, (o[0] + o[1]) + (o[2] + o[3]));
+    }
+  } else {
+    // Online softmax per warp over positions warp, warp + kPW, ... <= pos.
+    float4 q[G];
+#pragma unroll
+    for (int h = 0; h < G; ++h) q[h] = reinterpret_cast<const float4*>(qs + h * kHeadDim)[lane];
+    float m[G], lsum[G];
+    float4 accv[G];
+#pragma unroll
+    for (int h = 0; h < G; ++h) { m[h] = -INFINITY; lsum[h] = 0.0f; accv[h] = make_float4(0.f, 0.f, 0.f, 0.f); }
+    for (int p = warp; p <= pos; p += kPW) {
+      float4 k4 = kpf[0], v4 = vpf[0];
+      if (p == pos) {
+        k4 = reinterpret_cast<const float4*>(kn)[lane];
+        v4 = reinterpret_cast<const float4*>(vn)[lane];
+      }
+#pragma unroll
+      for (int j = 0; j + 1 < kAttnPf; ++j) {
+        kpf[j] = kpf[j + 1];
+        vpf[j] = vpf[j + 1];
+      }
+      const int pn = p + kAttnPf * kPW;
+      if (pn < pos) {  // refill the pipeline kAttnPf rows ahead
+        kpf[kAttnPf - 1] = ld4<KVT>(kc + pn * row_el + g * kHeadDim + 4 * lane);
+        vpf[kAttnPf - 1] = ld4<KVT>(vc + pn * row_el + g * kHeadDim + 4 * lane);
+      }
+#pragma unroll
+      for (int h = 0; h < G; ++h) {
+        float d = q[h].x * k4.x + q[h].y * k4.y + q[h].z * k4.z + q[h].w * k4.w;
+        const float sc = warp_sum(d) * a.scale;
+        const float mn = fmaxf(m[h], sc);
+        const float co = expf(m[h] - mn), cn = expf(sc - mn);
+        lsum[h] = lsum[h] * co + cn;
+        accv[h] = make_float4(accv[h].x * co + cn * v4.x, accv[h].y * co + cn * v4.y, accv[h].z * co + cn * v4.z,
+                              accv[h].w * co + cn * v4.w);
+        m[h] = mn;
+      }
+    }
+    // Merge the warps in a fixed order (deterministic).
+    float* wacc = S.xs;  // [kPW][G][128]
 #pragma unroll
     for (int h = 0; h < G; ++h) {
-      float d = q[h].x * k4.x + q[h].y * k4.y + q[h].z * k4.z + q[h].w * k4.w;
-      const float sc = warp_sum(d) * a.scale;
-      const float mn = fmaxf(m[h], sc);
-      const float co = expf(m[h] - mn), cn = expf(sc - mn);
-      lsum[h] = lsum[h] * co + cn;
-      acc[h] = make_float4(acc[h].x * co + cn * v4.x, acc[h].y * co + cn * v4.y, acc[h].z * co + cn * v4.z,
-                           acc[h].w * co + cn * v4.w);
-      m[h] = mn;
+      reinterpret_cast<float4*>(wacc + (warp * G + h) * kHeadDim)[lane] = accv[h];
+      if (lane == 0) wml[warp * G + h] = make_float2(m[h], lsum[h]);
+    }
+    __syncthreads();
+    static_assert(kPW == 16, "the merge pairs two heads per warp");
+    float* fw = raw;  // [G][kPW] (raw is no longer needed)
+    if (threadIdx.x < ((G * kPW + 31) / 32) * 32) {
+      const int h = threadIdx.x / kPW, w = threadIdx.x % kPW;
+      const bool on = h < G;
+      const float2 mw = on ? wml[w * G + h] : make_float2(-INFINITY, 0.0f);
+      float M = mw.x;
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+      const float e = mw.y > 0.0f ? expf(mw.x - M) : 0.0f;
+      float Ls = mw.y * e;
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) Ls += __shfl_xor_sync(0xffffffffu, Ls, o);
+      if (on) fw[h * kPW + w] = e / Ls;
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < G * kHeadDim; e += kPT) {
+      const int h = e / kHeadDim, d = e % kHeadDim;
+      float o = 0.0f;
+#pragma unroll
+      for (int w = 0; w < kPW; ++w) o += wacc[(w * G + h) * kHeadDim + d] * fw[h * kPW + w];
+      xs_store(ostage, e, o);
     }
   }
-  // Merge the warps in a fixed order (deterministic).
-  float* wacc = S.xs;  // [kPW][G][128]
-#pragma unroll
-  for (int h = 0; h < G; ++h) {
-    reinterpret_cast<float4*>(wacc + (warp * G + h) * kHeadDim)[lane] = acc[h];
-    if (lane == 0) wml[warp * G + h] = make_float2(m[h], lsum[h]);
-  }
   __syncthreads();
-  // Per (head, warp) rescale factors exp(m_w - M) / L, computed once: one lane
-  // per (head, warp), reductions over the kPW lanes of a head by shuffles.
-  static_assert(kPW == 16, "the merge pairs two heads per warp");
-  float* fw = raw;  // [G][kPW] (raw is no longer needed)
-  if (threadIdx.x < ((G * kPW + 31) / 32) * 32) {
-    const int h = threadIdx.x / kPW, w = threadIdx.x % kPW;
-    const bool on = h < G;
-    const float2 mw = on ? wml[w * G + h] : make_float2(-INFINITY, 0.0f);
-    float M = mw.x;
-#pragma unroll
-    for (int o = 8; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-    const float e = mw.y > 0.0f ? expf(mw.x - M) : 0.0f;
-    float Ls = mw.y * e;
-#pragma unroll
-    for (int o = 8; o > 0; o >>= 1) Ls += __shfl_xor_sync(0xffffffffu, Ls, o);
-    if (on) fw[h * kPW + w] = e / Ls;
-  }
+
+  // O rows [o_lo, o_hi) over the head's columns -> counted fixed-point sums
+  if (!stage_ok(a, wait_chunk(a, S, chunk))) return false;
+  const int n = rg.o_hi - rg.o_lo;
+  slice_dots<G * kHeadDim / kBlockCols>(S.ring + (chunk % kSlots) * kSlotBytes, n, (int)a.rec_og, ostage, S.res);
   __syncthreads();
-  for (int e = threadIdx.x; e < G * kHeadDim; e += kPT) {
-    const int h = e / kHeadDim, d = e % kHeadDim;
-    float o = 0.0f;
-#pragma unroll
-    for (int w = 0; w < kPW; ++w) o += wacc[(w * G + h) * kHeadDim + d] * fw[h * kPW + w];
-    st_word(xo + (g * G + h) * kHeadDim + d, o, epoch);
-  }
+  if (threadIdx.x < n) red_fx(a, acc + rg.o_lo + threadIdx.x, S.res[threadIdx.x]);
   return true;
 }
 
@@ -538,7 +745,19 @@ __global__ void __launch_bounds__(kPT, 1) k_decode_persistent(const __grid_const
   range_of(H, cta, ng, rg.h_lo, rg.h_hi);
   range_of(I, cta, ng, rg.i_lo, rg.i_hi);
   range_of(a.vocab, cta, ng, rg.v_lo, rg.v_hi);
+  rg.att = cta < a.NKV * a.OS;
+  rg.ag = rg.att ? cta / a.OS : 0;
+  rg.as = rg.att ? cta % a.OS : 0;
+  range_of(H, rg.as, a.OS, rg.o_lo, rg.o_hi);
+  if (!rg.att) rg.o_hi = rg.o_lo;
   const int n_chunks = 4 * a.L;
+  // The next launch's O sums start at zero: clear the other parity's words.
+  {
+    const long long words = (long long)a.L * H;
+    unsigned long long* other = a.oacc + (long long)((epoch + 1u) & 1u) * words;
+    const long long lo = words * cta / ng, hi = words * (cta + 1) / ng;
+    for (long long i = lo + threadIdx.x; i < hi; i += kPT) other[i] = 0ull;
+  }
   if (threadIdx.x == 0) {
     for (int s = 0; s < kSlots; ++s) mbar_init(&S.mbar[s], 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -571,7 +790,7 @@ __global__ void __launch_bounds__(kPT, 1) k_decode_persistent(const __grid_const
   for (int l = 0; l < a.L; ++l) {
     const PLayer& P = a.layers[l];
     unsigned long long* X = a.xb + (long long)l * a.xstride;
-    unsigned long long *xh = X, *xq = X + H, *xa = X + H + R, *xha = X + H + R + QS, *xact = xha + H;
+    unsigned long long *xh = X, *xq = X + H, *xact = X + H + R + QS + H;
     unsigned long long* xnext = a.xb + (long long)(l + 1) * a.xstride;
     const int ev = 1 + l * kTimelinePerLayer;
 
@@ -596,28 +815,23 @@ __global__ void __launch_bounds__(kPT, 1) k_decode_persistent(const __grid_const
       ++chunk;
     }
 
-    // 2. attention (CTAs 0..NKV-1, one KV head each)
-    if (cta < a.NKV) QD_FAIL_IF((!attn_stage<G, KVT>(a, S, l, cta, pos, epoch, xq, xa)));
-    __syncthreads();
-    stamp(tl, ev + 3);
-
-    // 3. O projection + residual
+    // 2. attention + O slice (the attention CTAs; every CTA passes chunk 4l+1, empty for
+    //    the others), then 3. h_attn = h + the O sums (every CTA)
     {
-      QD_FAIL_IF(!stage_ok(a, poll_to_smem(a, xa, QS, epoch, S.xs, true)));
-      stamp(tl, ev + 4);
-      QD_FAIL_IF(!stage_ok(a, wait_chunk(a, S, chunk)));
-      stamp(tl, ev + 11);
-      const int n = rg.h_hi - rg.h_lo;
-      stage_dots(S.ring + (chunk % kSlots) * kSlotBytes, n, 1, (int)a.rec_q, QS / kBlockCols, 2, S.xs, S.res);
-      __syncthreads();
-      if (threadIdx.x < n) {
-        const int r = rg.h_lo + threadIdx.x;
-        st_word(xha + r, S.hs[r] + (S.res[threadIdx.x] + S.res[n + threadIdx.x]), epoch);
+      unsigned long long* acc = a.oacc + ((long long)(epoch & 1u) * a.L + l) * H;
+      if (rg.att) {
+        QD_FAIL_IF((!attn_o_stage<G, KVT>(a, S, rg, l, pos, epoch, xq, acc, chunk, xs_floats)));
+      } else {
+        QD_FAIL_IF(!stage_ok(a, wait_chunk(a, S, chunk)));
       }
       __syncthreads();
-      stamp(tl, ev + 5);
+      stamp(tl, ev + 3);
       if (threadIdx.x == 0) issue_chunk(a, S, rg, chunk + kSlots, n_chunks);
       ++chunk;
+      QD_FAIL_IF(!stage_ok(a, poll_fx(a, acc, H, (unsigned)a.NKV, S.hs, S.has)));
+      stamp(tl, ev + 4);
+      stamp(tl, ev + 11);
+      stamp(tl, ev + 5);
     }
 
     // 4. post-attention RMSNorm + gate/up + silu * up
@@ -625,7 +839,6 @@ __global__ void __launch_bounds__(kPT, 1) k_decode_persistent(const __grid_const
       float nw[2];
 #pragma unroll
       for (int k = 0; k < 2; ++k) nw[k] = threadIdx.x + k * kPT < H ? P.n_post[threadIdx.x + k * kPT] : 0.0f;
-      QD_FAIL_IF(!stage_ok(a, poll_to_smem(a, xha, H, epoch, S.has, false)));
       stamp(tl, ev + 6);
       rms_own(S.has, nw, H, a.eps, S.xs, S.red);
       stamp(tl, ev + 12);
