@@ -41,11 +41,13 @@ constexpr unsigned kPollBackoffNs = 100;   // pause between re-polls of exchange
 constexpr int kAttnPf = 2;                 // cached K/V rows each attention warp loads ahead
 
 // Stage timeline (opt-in): per CTA, event 0 = start, then per layer
-// 14 events (QKV input ready, QKV weights ready, QKV stored, attention done,
-// O input ready, O stored, gate/up input ready, gate/up stored, down input
-// ready, down stored, QKV norm done, O weights ready, gate/up norm done,
-// down weights ready), then LM-head input ready, LM-head done, merged.
-constexpr int kTimelinePerLayer = 14;
+// 19 events (QKV input ready, QKV weights ready, QKV stored, attention + O slice
+// done, h_attn ready, (unused: = h_attn ready), gate/up input ready, gate/up stored,
+// down input ready, down stored, QKV norm done, (unused: = h_attn ready), gate/up
+// norm done, down weights ready; attention CTAs only: q/k/v arrived, head norm +
+// RoPE done, attention done, O slice weights ready, O slice dots done), then
+// LM-head input ready, LM-head done, merged.
+constexpr int kTimelinePerLayer = 19;
 __host__ __device__ constexpr int timeline_events(int layers) { return 1 + kTimelinePerLayer * layers + 3; }
 
 struct PLayer {
@@ -460,7 +462,7 @@ __device__ __forceinline__ bool poll_to_smem(const PArgs& a, const unsigned long
 template <int G, typename KVT>
 __device__ __forceinline__ bool attn_o_stage(const PArgs& a, const PShared& S, const Ranges& rg, int l, int pos,
                                              unsigned epoch, const unsigned long long* xq, unsigned long long* acc,
-                                             int chunk, int xs_floats) {
+                                             int chunk, int xs_floats, unsigned long long* tl, int ev) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int g = rg.ag;
   const PLayer& P = a.layers[l];
@@ -523,6 +525,7 @@ __device__ __forceinline__ bool attn_o_stage(const PArgs& a, const PShared& S, c
   }
   if (compact) cp_async_wait_all();
   if (!stage_ok(a, ok)) return false;
+  stamp(tl, ev + 14);
 
   // head RMSNorm + RoPE (q heads, k); the group's first CTA appends k, v to the cache
   const bool owner = rg.as == 0;
@@ -551,6 +554,7 @@ __device__ __forceinline__ bool attn_o_stage(const PArgs& a, const PShared& S, c
     else reinterpret_cast<float4*>(kn)[lane] = owner ? st4<KVT>(krow, r) : rnd4<KVT>(r);
   }
   __syncthreads();
+  stamp(tl, ev + 15);
 
   if (compact) {
     // scores: warp w takes positions w, w + kPW, ... <= pos
@@ -676,11 +680,14 @@ __device__ __forceinline__ bool attn_o_stage(const PArgs& a, const PShared& S, c
   }
   __syncthreads();
 
+  stamp(tl, ev + 16);
   // O rows [o_lo, o_hi) over the head's columns -> counted fixed-point sums
   if (!stage_ok(a, wait_chunk(a, S, chunk))) return false;
+  stamp(tl, ev + 17);
   const int n = rg.o_hi - rg.o_lo;
   slice_dots<G * kHeadDim / kBlockCols>(S.ring + (chunk % kSlots) * kSlotBytes, n, (int)a.rec_og, ostage, S.res);
   __syncthreads();
+  stamp(tl, ev + 18);
   if (threadIdx.x < n) red_fx(a, acc + rg.o_lo + threadIdx.x, S.res[threadIdx.x]);
   return true;
 }
@@ -820,7 +827,7 @@ __global__ void __launch_bounds__(kPT, 1) k_decode_persistent(const __grid_const
     {
       unsigned long long* acc = a.oacc + ((long long)(epoch & 1u) * a.L + l) * H;
       if (rg.att) {
-        QD_FAIL_IF((!attn_o_stage<G, KVT>(a, S, rg, l, pos, epoch, xq, acc, chunk, xs_floats)));
+        QD_FAIL_IF((!attn_o_stage<G, KVT>(a, S, rg, l, pos, epoch, xq, acc, chunk, xs_floats, tl, ev)));
       } else {
         QD_FAIL_IF(!stage_ok(a, wait_chunk(a, S, chunk)));
       }
