@@ -692,26 +692,20 @@ __device__ __forceinline__ bool attn_o_stage(const PArgs& a, const PShared& S, c
   return true;
 }
 
-// RMSNorm of v[e] (shared memory, e = tid, tid + kPT), in two halves around a CTA
-// barrier the caller already takes: rms_partial leaves each warp's sum of squares of
-// its threads' own values in red[warp] (the values a thread polled itself, so no
-// barrier is needed before it); after the barrier rms_apply sums red in warp order
-// and writes the thread's normed values, times its prefetched weights w, into the
-// swizzled staging. All threads must call both.
-__device__ __forceinline__ void rms_partial(const float* v, int n, float* red) {
-  float ss = 0.0f;
+// RMSNorm of v[e] (shared memory, e = tid, tid + kPT) with the thread's
+// prefetched weights w into the swizzled staging; all threads must call it.
+__device__ __forceinline__ void rms_own(const float* v, const float (&w)[2], int n, float eps, float* xs,
+                                        float* red) {
+  float x[2] = {0.0f, 0.0f}, ss = 0.0f;
 #pragma unroll
   for (int k = 0; k < 2; ++k)
     if (threadIdx.x + k * kPT < n) {
-      const float x = v[threadIdx.x + k * kPT];
-      ss += x * x;
+      x[k] = v[threadIdx.x + k * kPT];
+      ss += x[k] * x[k];
     }
   ss = warp_sum(ss);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
-}
-
-__device__ __forceinline__ void rms_apply(const float* v, const float (&w)[2], int n, float eps, float* xs,
-                                          const float* red) {
+  __syncthreads();
   float t = 0.0f;
 #pragma unroll
   for (int k = 0; k < kPW; ++k) t += red[k];
@@ -719,7 +713,7 @@ __device__ __forceinline__ void rms_apply(const float* v, const float (&w)[2], i
 #pragma unroll
   for (int k = 0; k < 2; ++k) {
     const int e = threadIdx.x + k * kPT;
-    if (e < n) xs_store(xs, e, v[e] * inv * w[k]);
+    if (e < n) xs_store(xs, e, x[k] * inv * w[k]);
   }
 }
 
@@ -812,11 +806,9 @@ __global__ void __launch_bounds__(kPT, 1) k_decode_persistent(const __grid_const
       float nw[2];
 #pragma unroll
       for (int k = 0; k < 2; ++k) nw[k] = threadIdx.x + k * kPT < H ? P.n_in[threadIdx.x + k * kPT] : 0.0f;
-      const bool okp = l > 0 ? poll_to_smem(a, xh, H, epoch, S.hs, false) : true;
-      rms_partial(S.hs, H, S.red);
-      QD_FAIL_IF(!stage_ok(a, okp));
+      if (l > 0) QD_FAIL_IF(!stage_ok(a, poll_to_smem(a, xh, H, epoch, S.hs, false)));
       stamp(tl, ev + 0);
-      rms_apply(S.hs, nw, H, a.eps, S.xs, S.red);
+      rms_own(S.hs, nw, H, a.eps, S.xs, S.red);
       stamp(tl, ev + 10);
       QD_FAIL_IF(!stage_ok(a, wait_chunk(a, S, chunk)));
       stamp(tl, ev + 1);
@@ -832,9 +824,6 @@ __global__ void __launch_bounds__(kPT, 1) k_decode_persistent(const __grid_const
 
     // 2. attention + O slice (the attention CTAs; every CTA passes chunk 4l+1, empty for
     //    the others), then 3. h_attn = h + the O sums (every CTA)
-    float nwp[2];  // post-attention norm weights, loaded ahead of the waits
-#pragma unroll
-    for (int k = 0; k < 2; ++k) nwp[k] = threadIdx.x + k * kPT < H ? P.n_post[threadIdx.x + k * kPT] : 0.0f;
     {
       unsigned long long* acc = a.oacc + ((long long)(epoch & 1u) * a.L + l) * H;
       if (rg.att) {
@@ -846,9 +835,7 @@ __global__ void __launch_bounds__(kPT, 1) k_decode_persistent(const __grid_const
       stamp(tl, ev + 3);
       if (threadIdx.x == 0) issue_chunk(a, S, rg, chunk + kSlots, n_chunks);
       ++chunk;
-      const bool okf = poll_fx(a, acc, H, (unsigned)a.NKV, S.hs, S.has);
-      rms_partial(S.has, H, S.red);
-      QD_FAIL_IF(!stage_ok(a, okf));
+      QD_FAIL_IF(!stage_ok(a, poll_fx(a, acc, H, (unsigned)a.NKV, S.hs, S.has)));
       stamp(tl, ev + 4);
       stamp(tl, ev + 11);
       stamp(tl, ev + 5);
@@ -856,8 +843,11 @@ __global__ void __launch_bounds__(kPT, 1) k_decode_persistent(const __grid_const
 
     // 4. post-attention RMSNorm + gate/up + silu * up
     {
+      float nw[2];
+#pragma unroll
+      for (int k = 0; k < 2; ++k) nw[k] = threadIdx.x + k * kPT < H ? P.n_post[threadIdx.x + k * kPT] : 0.0f;
       stamp(tl, ev + 6);
-      rms_apply(S.has, nwp, H, a.eps, S.xs, S.red);
+      rms_own(S.has, nw, H, a.eps, S.xs, S.red);
       stamp(tl, ev + 12);
       QD_FAIL_IF(!stage_ok(a, wait_chunk(a, S, chunk)));
       const int n = rg.i_hi - rg.i_lo;
