@@ -296,7 +296,10 @@ void setup_persist(qd_engine* e) {
   // attention CTAs per KV head: each owns H / OS rows of the O projection
   const int OS = std::min(16, g / std::max(1, p.kv_heads));
   const long long rec_og = rec_bytes(G * kHeadDim), oslice_rows = OS > 0 ? (H + OS - 1) / OS : 0;
+  // gate/up rows per CTA: whole words of three activations
+  const long long rows_i = 3 * (((I + 2) / 3 + g - 1) / g);
   bool ok = e->opt.persistent && coop && G <= 2 && H <= 1024 && QS <= 2048 && I <= 3072 && p.kv_heads <= g &&
+            rows_i * 2 * rec_h <= kSlotBytes && 2 * rows_i <= kMaxRes / 2 && (I + 2) / 3 <= 4 * kPT &&
             OS >= 1 && oslice_rows <= kMaxRes && oslice_rows * rec_og <= kSlotBytes &&
             per_cta(R, rec_h) <= kSlotBytes && per_cta(I, 2 * rec_h) <= kSlotBytes && per_cta(H, rec_i) <= kSlotBytes &&
             2LL * H <= kSlotBytes;

@@ -96,6 +96,22 @@ __device__ __forceinline__ unsigned long long ld_word(const unsigned long long* 
   asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
+// The gate/up stage's activations travel three to a 16-byte word {a, b, c, epoch},
+// stored and loaded as single 128-bit accesses: a third of the words to poll.
+constexpr int kActPer = 3;
+__device__ __forceinline__ void st_word3(unsigned long long* p, float a, float b, float c, unsigned epoch) {
+  const unsigned long long lo = ((unsigned long long)__float_as_uint(b) << 32) | __float_as_uint(a);
+  const unsigned long long hi = ((unsigned long long)epoch << 32) | __float_as_uint(c);
+  asm volatile("{\n\t.reg .b128 t;\n\tmov.b128 t, {%1, %2};\n\tst.relaxed.gpu.global.b128 [%0], t;\n\t}" ::"l"(p),
+               "l"(lo), "l"(hi)
+               : "memory");
+}
+__device__ __forceinline__ void ld_word3(const unsigned long long* p, unsigned long long& lo, unsigned long long& hi) {
+  asm volatile("{\n\t.reg .b128 t;\n\tld.relaxed.gpu.global.b128 t, [%2];\n\tmov.b128 {%0, %1}, t;\n\t}"
+               : "=l"(lo), "=l"(hi)
+               : "l"(p)
+               : "memory");
+}
 __device__ __forceinline__ void st_word(unsigned long long* p, float v, unsigned epoch) {
   const unsigned long long w = ((unsigned long long)epoch << 32) | __float_as_uint(v);
   asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
@@ -244,6 +260,45 @@ __device__ __forceinline__ void raise_abort(const PArgs& a) {
 __device__ __forceinline__ bool stage_ok(const PArgs& a, bool mine) {
   if (!mine) raise_abort(a);
   return __syncthreads_and(mine ? 1 : 0) != 0;
+}
+
+// Every thread: poll 16-byte words w = threadIdx.x + k*kPT < nw (nw <= 4 kPT) of three
+// values each until they carry this launch's epoch; value 3w + j (< n) goes to the
+// swizzled staging. False on timeout/abort.
+__device__ __forceinline__ bool poll3_to_smem(const PArgs& a, const unsigned long long* src, int nw, int n,
+                                              unsigned epoch, float* xs) {
+  constexpr int K = 4;
+  unsigned long long lo[K], hi[K];
+  unsigned need = 0;
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    const int w = threadIdx.x + k * kPT;
+    lo[k] = hi[k] = 0ull;
+    if (w < nw) {
+      ld_word3(src + 2 * w, lo[k], hi[k]);
+      need |= 1u << k;
+    }
+  }
+  unsigned long long t0 = 0;
+  for (unsigned it = 0;; ++it) {
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      if (((need >> k) & 1u) && (unsigned)(hi[k] >> 32) == epoch) {
+        need &= ~(1u << k);
+        const int e = 3 * (threadIdx.x + k * kPT);
+        xs_store(xs, e, __uint_as_float((unsigned)lo[k]));
+        if (e + 1 < n) xs_store(xs, e + 1, __uint_as_float((unsigned)(lo[k] >> 32)));
+        if (e + 2 < n) xs_store(xs, e + 2, __uint_as_float((unsigned)hi[k]));
+      }
+    }
+    if (!need) return true;
+    if (it == 0) t0 = gtimer();
+    else if ((it & 15) == 0 && (aborted(a) || gtimer() - t0 > kWaitNs)) return false;
+    __nanosleep(kPollBackoffNs);
+#pragma unroll
+    for (int k = 0; k < K; ++k)
+      if ((need >> k) & 1u) ld_word3(src + 2 * (threadIdx.x + k * kPT), lo[k], hi[k]);
+  }
 }
 
 // ---- counted fixed-point sums ------------------------------------------------------
@@ -750,7 +805,13 @@ __global__ void __launch_bounds__(kPT, 1) k_decode_persistent(const __grid_const
   Ranges rg;
   range_of(R, cta, ng, rg.qkv_lo, rg.qkv_hi);
   range_of(H, cta, ng, rg.h_lo, rg.h_hi);
-  range_of(I, cta, ng, rg.i_lo, rg.i_hi);
+  {  // gate/up rows in whole activation words
+    const int words = (I + kActPer - 1) / kActPer;
+    int w_lo, w_hi;
+    range_of(words, cta, ng, w_lo, w_hi);
+    rg.i_lo = min(I, w_lo * kActPer);
+    rg.i_hi = min(I, w_hi * kActPer);
+  }
   range_of(a.vocab, cta, ng, rg.v_lo, rg.v_hi);
   rg.att = cta < a.NKV * a.OS;
   rg.ag = rg.att ? cta / a.OS : 0;
@@ -853,9 +914,17 @@ __global__ void __launch_bounds__(kPT, 1) k_decode_persistent(const __grid_const
       const int n = rg.i_hi - rg.i_lo;
       stage_dots(S.ring + (chunk % kSlots) * kSlotBytes, n, 2, (int)a.rec_h, H / kBlockCols, 1, S.xs, S.res);
       __syncthreads();
+      float* act = S.res + kMaxRes / 2;  // this CTA's activations, then three to a word
       if (threadIdx.x < n) {
         const float gt = S.res[2 * threadIdx.x], upv = S.res[2 * threadIdx.x + 1];
-        st_word(xact + rg.i_lo + threadIdx.x, (gt / (1.0f + expf(-gt))) * upv, epoch);
+        act[threadIdx.x] = (gt / (1.0f + expf(-gt))) * upv;
+      }
+      __syncthreads();
+      const int w0 = rg.i_lo / kActPer, n_words = (n + kActPer - 1) / kActPer;
+      if (threadIdx.x < n_words) {
+        const int j = kActPer * threadIdx.x;
+        st_word3(xact + 2 * (w0 + threadIdx.x), act[j], j + 1 < n ? act[j + 1] : 0.0f, j + 2 < n ? act[j + 2] : 0.0f,
+                 epoch);
       }
       __syncthreads();
       stamp(tl, ev + 7);
@@ -865,7 +934,7 @@ __global__ void __launch_bounds__(kPT, 1) k_decode_persistent(const __grid_const
 
     // 5. down projection + residual
     {
-      QD_FAIL_IF(!stage_ok(a, poll_to_smem(a, xact, I, epoch, S.xs, true)));
+      QD_FAIL_IF(!stage_ok(a, poll3_to_smem(a, xact, (I + kActPer - 1) / kActPer, I, epoch, S.xs)));
       stamp(tl, ev + 8);
       QD_FAIL_IF(!stage_ok(a, wait_chunk(a, S, chunk)));
       stamp(tl, ev + 13);
