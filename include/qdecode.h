@@ -94,6 +94,36 @@ int qd_engine_profile(const qd_engine* e, qd_profile* out);
 int qd_generate_greedy(qd_engine* e, const int32_t* input_ids, int n_prompt, int max_new_tokens,
                        int32_t* out_ids, qd_token_cb on_token, void* user, qd_stats* stats);
 
+/* Sampling beyond greedy (no counterpart in the reference, which decodes greedily only,
+ * README.md:172-173): the token of each step is drawn from the LM head's logits.
+ *  - candidates: the top_k largest logits (1..64; 0 or more than 64: the 64 largest),
+ *    ordered by value with ties to the lower index, NaN below every number;
+ *  - p_i = exp((v_i - v_max) / temperature) over the candidates;
+ *  - top_p in (0, 1]: the shortest prefix of candidates whose sum reaches top_p of the
+ *    candidates' sum is kept (with top_k = 0 this is top-p over the 64 most likely
+ *    tokens, the same as full-vocabulary top-p whenever that nucleus has <= 64 tokens);
+ *  - u = (splitmix64(seed ^ (step * 0xD1B54A32D192ED03)) >> 40) * 2^-24, step = the index
+ *    of the generated token; the first kept candidate whose running sum exceeds
+ *    u * (kept sum) is the token.
+ * temperature <= 0 or top_k == 1 is greedy decoding (qd_generate_greedy's ids).
+ * QD_E_INVALID for top_p outside (0, 1], top_k < 0 or a non-finite temperature. */
+typedef struct qd_sampling {
+  float temperature;
+  int top_k;
+  float top_p;
+  uint64_t seed;
+} qd_sampling;
+/* runCustomQwenGreedyPrompt's flow (prompt, then max_new_tokens generated) with the
+ * tokens drawn as above; arguments and stats as qd_generate_greedy. */
+int qd_generate_sample(qd_engine* e, const int32_t* input_ids, int n_prompt, int max_new_tokens,
+                       const qd_sampling* sampling, int32_t* out_ids, qd_token_cb on_token, void* user,
+                       qd_stats* stats);
+/* Kernel level: one draw from logits[vocab] (device) at RNG step `step`; the id goes to
+ * token[0] (device). workspace: qd_sample_workspace_bytes(vocab) bytes of device memory. */
+size_t qd_sample_workspace_bytes(uint32_t vocab);
+int qd_sample_logits(const float* logits, uint32_t vocab, const qd_sampling* sampling, uint32_t step,
+                     void* workspace, int32_t* token, void* stream);
+
 /* Parity and inspection helpers. */
 int qd_engine_logits(qd_engine* e, float* host_logits);       /* logits of the last generated step */
 int qd_engine_hidden(qd_engine* e, float* host_hidden);       /* residual stream after the last layer */

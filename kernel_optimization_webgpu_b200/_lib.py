@@ -37,6 +37,7 @@ EXPORTS = (
     "qd_batch_set_vocab_shard", "qd_batch_step_layers", "qd_batch_step_lm_slice", "qd_batch_step_merge",
     "qd_batch_shard_sync", "qd_engine_inject_stall", "qd_batch_inject_stall",
     "qd_run_kernel_benchmarks", "qd_run_full_decoder_stack_benchmark",
+    "qd_generate_sample", "qd_sample_workspace_bytes", "qd_sample_logits",
 )
 
 
@@ -56,6 +57,10 @@ class QdStats(C.Structure):
     _fields_ = [("generate_ms", C.c_double), ("first_token_ms", C.c_double),
                 ("steady_ms_per_token", C.c_double), ("generated_tokens", C.c_int),
                 ("prompt_tokens", C.c_int)]
+
+
+class QdSampling(C.Structure):
+    _fields_ = [("temperature", C.c_float), ("top_k", C.c_int), ("top_p", C.c_float), ("seed", C.c_uint64)]
 
 
 class QdKernelBench(C.Structure):
@@ -188,6 +193,13 @@ def load(build_if_stale: bool = True):
         getattr(L, name).restype = i32
     L.qd_batch_shard_sync.argtypes = [vp, i32, vp]
     L.qd_batch_shard_sync.restype = i32
+    L.qd_generate_sample.argtypes = [vp, vp, i32, i32, C.POINTER(QdSampling), vp, TOKEN_CB, vp,
+                                     C.POINTER(QdStats)]
+    L.qd_generate_sample.restype = i32
+    L.qd_sample_workspace_bytes.argtypes = [u32]
+    L.qd_sample_workspace_bytes.restype = C.c_size_t
+    L.qd_sample_logits.argtypes = [vp, u32, C.POINTER(QdSampling), u32, vp, vp, vp]
+    L.qd_sample_logits.restype = i32
     L.qd_run_kernel_benchmarks.argtypes = [vp, C.POINTER(QdKernelBench)]
     L.qd_run_kernel_benchmarks.restype = i32
     L.qd_run_full_decoder_stack_benchmark.argtypes = [vp, C.POINTER(QdStackBench)]

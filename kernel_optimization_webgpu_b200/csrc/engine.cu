@@ -906,6 +906,7 @@ void free_engine(qd_engine* e) {
   if (e->c_cnt) cudaFree(e->c_cnt);
   if (e->d_players) cudaFree(e->d_players);
   if (e->oslices) cudaFree(e->oslices);
+  if (e->sample_ws) cudaFree(e->sample_ws);
   if (e->oacc) cudaFree(e->oacc);
   if (e->timeline) cudaFree(e->timeline);
   if (e->out_host) cudaFreeHost(e->out_host);
@@ -1122,10 +1123,14 @@ int qd_engine_profile(const qd_engine* e, qd_profile* out) {
   return QD_OK;
 }
 
-int qd_generate_greedy(qd_engine* e, const int32_t* input_ids, int n_prompt, int max_new_tokens,
-                       int32_t* out_ids, qd_token_cb on_token, void* user, qd_stats* stats) {
+namespace {
+
+int generate(qd_engine* e, const int32_t* input_ids, int n_prompt, int max_new_tokens, const qd_sampling* sampling,
+             int32_t* out_ids, qd_token_cb on_token, void* user, qd_stats* stats) {
   if (!e) return fail(nullptr, QdError{QD_E_INVALID, "engine is NULL"});
   try {
+    if (sampling) check_sampling(*sampling);
+    const bool sample = sampling && !sampling_is_greedy(*sampling);
     if (!input_ids || n_prompt < 1) throw QdError{QD_E_INVALID, "the prompt needs at least one token"};
     if (max_new_tokens < 0 || (max_new_tokens > 0 && !out_ids)) throw QdError{QD_E_INVALID, "bad max_new_tokens or out_ids"};
     // Positions written: 0 .. n_prompt + max_new - 2 (the last token is never fed back).
@@ -1145,6 +1150,7 @@ int qd_generate_greedy(qd_engine* e, const int32_t* input_ids, int n_prompt, int
     bool stop = false;
     for (int step = 0; step < max_new_tokens && !stop; ++step) {
       run_token(e, true);
+      if (sample) enqueue_engine_sample(e, *sampling);
       QD_CK(cudaEventRecord(e->ev[step & 1], e->stream));
       if (step > 0) {  // deliver the previous token while this one runs
         QD_CK(cudaEventSynchronize(e->ev[(step - 1) & 1]));
@@ -1177,6 +1183,20 @@ int qd_generate_greedy(qd_engine* e, const int32_t* input_ids, int n_prompt, int
     return fail(e, err);
   }
   return QD_OK;
+}
+
+}  // namespace
+
+int qd_generate_greedy(qd_engine* e, const int32_t* input_ids, int n_prompt, int max_new_tokens,
+                       int32_t* out_ids, qd_token_cb on_token, void* user, qd_stats* stats) {
+  return generate(e, input_ids, n_prompt, max_new_tokens, nullptr, out_ids, on_token, user, stats);
+}
+
+int qd_generate_sample(qd_engine* e, const int32_t* input_ids, int n_prompt, int max_new_tokens,
+                       const qd_sampling* sampling, int32_t* out_ids, qd_token_cb on_token, void* user,
+                       qd_stats* stats) {
+  if (!sampling) return fail(e, QdError{QD_E_INVALID, "sampling parameters are NULL"});
+  return generate(e, input_ids, n_prompt, max_new_tokens, sampling, out_ids, on_token, user, stats);
 }
 
 int qd_engine_logits(qd_engine* e, float* host_logits) {

@@ -96,6 +96,11 @@ int gemm_plan_splits(int K, int want, int* kt_split);
 // one decoder layer whose input is the engine's hidden vector (layer 0 included,
 // no embedding gather); the decode position the layer kernels read; the device
 // status check after a run; a q4 matvec over row records (row r at base + r * row_stride).
+// Sampling (sample.cu): validation, the greedy cases, and the sampling kernels after an
+// engine's LM head (reads its logits, overwrites the token the head chose).
+void check_sampling(const qd_sampling& s);
+bool sampling_is_greedy(const qd_sampling& s);
+void enqueue_engine_sample(qd_engine* e, const qd_sampling& s);
 void bench_layer_from_hidden(qd_engine* e, int l, cudaStream_t s);
 void bench_set_position(qd_engine* e, int pos);
 void bench_check_state(qd_engine* e);
@@ -156,6 +161,7 @@ struct qd_engine {
   size_t persist_smem = 0;
   int lm_rows = 0;
   unsigned long long* timeline = nullptr;  // stage stamps of the last persistent launch (opt-in)
+  void* sample_ws = nullptr;               // sampling candidates (allocated on first use)
   char* oslices = nullptr;                 // O rows x KV-head columns, packed per attention CTA
   unsigned long long* oacc = nullptr;      // [2][L][H] counted fixed-point O sums
   int os = 0;                              // attention CTAs per KV head

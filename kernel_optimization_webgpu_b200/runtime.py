@@ -107,6 +107,32 @@ class Engine:
         stats = {f: getattr(st, f) for f, _ in QdStats._fields_}
         return out[:st.generated_tokens].tolist(), stats
 
+    def generate_sample(self, ids: Sequence[int], max_new: int, temperature: float = 1.0, top_k: int = 0,
+                        top_p: float = 1.0, seed: int = 0, on_token: Optional[Callable[[int], object]] = None):
+        """qd_generate_sample: the greedy flow with each token drawn by top-k / top-p
+        sampling (temperature <= 0 or top_k == 1: greedy)."""
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        out = np.zeros(max(max_new, 1), np.int32)
+        st = QdStats()
+        err: list = []
+
+        def _cb(tok, _user):
+            try:
+                return 1 if (on_token and on_token(int(tok)) is False) else 0
+            except BaseException as ex:
+                err.append(ex)
+                return 1
+
+        cb = _lib.TOKEN_CB(_cb)
+        sp = _lib.QdSampling(float(temperature), int(top_k), float(top_p), int(seed) & 0xFFFFFFFFFFFFFFFF)
+        rc = _lib.load().qd_generate_sample(self._h, ids.ctypes.data, int(ids.size), int(max_new), C.byref(sp),
+                                            out.ctypes.data, cb, None, C.byref(st))
+        check(rc, self._h)
+        if err:
+            raise err[0]
+        stats = {f: getattr(st, f) for f, _ in QdStats._fields_}
+        return out[:st.generated_tokens].tolist(), stats
+
     # stepping interface (enqueue only)
     def set_stream(self, stream=None) -> None:
         """Enqueue on a torch.cuda.Stream (None: the engine's own stream). The legacy
@@ -541,6 +567,18 @@ def lm_head_argmax(hidden, embed_f16, norm_weight=None, eps: float = 1e-6, logit
     check(_lib.load().qd_lm_head_argmax(hidden.data_ptr(), nw, eps, embed_f16.data_ptr(), lp,
                                         result.data_ptr(), hs, vocab, ws.buf.data_ptr(), _stream(stream)))
     return result
+
+
+def sample_logits(logits, temperature: float, top_k: int, top_p: float, seed: int, step: int, stream=None) -> int:
+    """One draw from device logits (qd_sample_logits); returns the id."""
+    import torch
+    vocab = logits.numel()
+    ws = torch.empty(_lib.load().qd_sample_workspace_bytes(vocab), dtype=torch.uint8, device=logits.device)
+    tok = torch.zeros(1, dtype=torch.int32, device=logits.device)
+    sp = _lib.QdSampling(float(temperature), int(top_k), float(top_p), int(seed) & 0xFFFFFFFFFFFFFFFF)
+    check(_lib.load().qd_sample_logits(logits.data_ptr(), vocab, C.byref(sp), int(step), ws.data_ptr(),
+                                       tok.data_ptr(), _stream(stream)))
+    return int(tok.item())
 
 
 def gqa_decode(q, k_cache, v_cache, seq_len: int, q_heads: int, kv_heads: int, y=None, stream=None):

@@ -575,3 +575,91 @@ int qo_greedy(qo_session* s, const int32_t* ids, int n_prompt, int max_new, int3
   }
   return 0;
 }
+
+/* ---- sampling beyond greedy (the library's definition, not the reference's: the
+ * reference decodes greedily only, README.md:172-173) ------------------------------ */
+
+static uint64_t qo_splitmix64(uint64_t x) {
+  x += 0x9E3779B97F4A7C15ull;
+  x = (x ^ (x >> 30)) * 0xBF58476D1CE4E5B9ull;
+  x = (x ^ (x >> 27)) * 0x94D049BB133111EBull;
+  return x ^ (x >> 31);
+}
+
+/* value order of the sampler: larger first, NaN below every number, ties to the lower index */
+static int qo_better(float a, uint32_t ia, float b, uint32_t ib) {
+  const int na = a != a, nb = b != b;
+  if (na != nb) return nb;
+  if (!na && a != b) return a > b;
+  return ia < ib;
+}
+
+/* One draw from logits[vocab]: top_k candidates (1..64, else 64), p_i = exp((v_i -
+ * v_0) / temperature) summed in candidate order in f32, the shortest prefix reaching
+ * top_p of the sum, u = (splitmix64(seed ^ step * 0xD1B54A32D192ED03) >> 40) * 2^-24,
+ * the first kept candidate whose running sum exceeds u * (kept sum).
+ * temperature <= 0 or top_k == 1: the argmax. */
+int32_t qo_sample(const float* logits, uint32_t vocab, float temperature, int top_k, float top_p, uint64_t seed,
+                  uint32_t step) {
+  if (vocab == 0) return -1;
+  const int greedy = !(temperature > 0.0f) || top_k == 1;
+  int K = greedy ? 1 : ((top_k >= 1 && top_k <= 64) ? top_k : 64);
+  if ((uint32_t)K > vocab) K = (int)vocab;
+  if (greedy) temperature = 1.0f;
+  float cv[64];
+  uint32_t ci[64];
+  int n = 0;
+  for (uint32_t i = 0; i < vocab; ++i) {  /* insertion into a sorted list of the K best */
+    const float v = logits[i];
+    if (n == K && !qo_better(v, i, cv[n - 1], ci[n - 1])) continue;
+    int j = n < K ? n++ : K - 1;
+    while (j > 0 && qo_better(v, i, cv[j - 1], ci[j - 1])) {
+      cv[j] = cv[j - 1];
+      ci[j] = ci[j - 1];
+      --j;
+    }
+    cv[j] = v;
+    ci[j] = i;
+  }
+  const float v0 = cv[0];
+  float cum[64] = {0.0f};
+  float s = 0.0f;
+  for (int i = 0; i < n; ++i) {
+    const float v = cv[i];
+    const float p = (v == v && v0 == v0) ? expf((v - v0) / temperature) : (i == 0 ? 1.0f : 0.0f);
+    s += p;
+    cum[i] = s;
+  }
+  int m = n - 1;
+  if (top_p < 1.0f)
+    for (int i = 0; i < n; ++i)
+      if (cum[i] >= top_p * s) { m = i; break; }
+  const uint64_t h = qo_splitmix64(seed ^ ((uint64_t)step * 0xD1B54A32D192ED03ull));
+  const float u = (float)(h >> 40) * 5.9604644775390625e-08f;
+  const float target = u * cum[m];
+  int pick = m;
+  for (int i = 0; i <= m; ++i)
+    if (cum[i] > target) { pick = i; break; }
+  return (int32_t)ci[pick];
+}
+
+/* qo_greedy's flow with each generated token drawn by qo_sample (step = its index). */
+int qo_generate_sample(qo_session* s, const int32_t* ids, int n_prompt, int max_new, float temperature, int top_k,
+                       float top_p, uint64_t seed, int32_t* out_ids) {
+  if (n_prompt <= 0 || max_new < 0) return -4;
+  if (n_prompt + max_new > s->max_seq + 1) return -2;
+  for (int i = 0; i < n_prompt; ++i) {
+    const int rc = qo_forward(s, ids[i], i);
+    if (rc) return rc;
+  }
+  for (int step = 0; step < max_new; ++step) {
+    if (step > 0) {
+      const int rc = qo_forward(s, out_ids[step - 1], n_prompt + step - 1);
+      if (rc) return rc;
+    }
+    const qo_model* m = s->m;
+    qo_lm_head_f16(s->final_out, m->embed, s->logits, (uint32_t)m->hidden, (uint32_t)m->vocab);
+    out_ids[step] = qo_sample(s->logits, (uint32_t)m->vocab, temperature, top_k, top_p, seed, (uint32_t)step);
+  }
+  return 0;
+}

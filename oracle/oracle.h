@@ -79,6 +79,10 @@ const float* qo_session_hidden(const qo_session* s);
 /* LM head + argmax on the last forward's final hidden (greedyNextTokenResident). */
 int qo_next_token(qo_session* s, float* logits_out, uint32_t result[2], float* top2_margin);
 /* runCustomQwenGreedyPrompt's token flow. Returns 0 or a negative error. */
+int32_t qo_sample(const float* logits, uint32_t vocab, float temperature, int top_k, float top_p, uint64_t seed,
+                  uint32_t step);
+int qo_generate_sample(qo_session* s, const int32_t* ids, int n_prompt, int max_new, float temperature, int top_k,
+                       float top_p, uint64_t seed, int32_t* out_ids);
 int qo_greedy(qo_session* s, const int32_t* ids, int n_prompt, int max_new, int32_t* out_ids,
               float* top2_margins);
 

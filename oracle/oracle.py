@@ -32,7 +32,8 @@ def build() -> str:
 def lib():
     global _lib
     if _lib is None:
-        if not os.path.exists(LIB_PATH):
+        srcs = [os.path.join(HERE, f) for f in ("oracle.c", "oracle.h")]
+        if not os.path.exists(LIB_PATH) or any(os.path.getmtime(f) > os.path.getmtime(LIB_PATH) for f in srcs):
             build()
         L = C.CDLL(LIB_PATH)
         u32, i32, f32, vp = C.c_uint32, C.c_int, C.c_float, C.c_void_p
@@ -63,6 +64,10 @@ def lib():
         L.qo_session_hidden.argtypes = [vp]; L.qo_session_hidden.restype = C.POINTER(f32)
         L.qo_next_token.argtypes = [vp, vp, _u32p, vp]; L.qo_next_token.restype = i32
         L.qo_greedy.argtypes = [vp, vp, i32, i32, vp, vp]; L.qo_greedy.restype = i32
+        L.qo_sample.argtypes = [vp, C.c_uint32, C.c_float, i32, C.c_float, C.c_uint64, C.c_uint32]
+        L.qo_sample.restype = C.c_int32
+        L.qo_generate_sample.argtypes = [vp, vp, i32, i32, C.c_float, i32, C.c_float, C.c_uint64, vp]
+        L.qo_generate_sample.restype = i32
         L.qo_num_threads.restype = i32
         L.qo_set_num_threads.argtypes = [i32]
         _lib = L
@@ -136,6 +141,13 @@ def lm_head_f16(hidden, table_f16):
     logits = np.zeros(rows, np.float32)
     lib().qo_lm_head_f16(_c(hidden, np.float32), t.view(np.uint16).reshape(-1), logits, hs, rows)
     return logits
+
+
+def sample(logits, temperature: float, top_k: int, top_p: float, seed: int, step: int) -> int:
+    """qo_sample: one draw from logits with the library's top-k / top-p definition."""
+    logits = _c(logits, np.float32)
+    return int(lib().qo_sample(logits.ctypes.data, logits.size, temperature, top_k, top_p,
+                               seed & 0xFFFFFFFFFFFFFFFF, step))
 
 
 def argmax(logits):
@@ -250,6 +262,16 @@ class Session:
         margin = C.c_float()
         lib().qo_next_token(self._h, logits.ctypes.data, r, C.addressof(margin))
         return int(r[0]), logits, float(margin.value)
+
+    def sample(self, ids, max_new: int, temperature: float, top_k: int, top_p: float, seed: int):
+        """qo_generate_sample: the greedy flow with each token drawn by sample()."""
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        out = np.zeros(max(max_new, 1), np.int32)
+        rc = lib().qo_generate_sample(self._h, ids.ctypes.data, ids.size, max_new, temperature, top_k, top_p,
+                                      seed & 0xFFFFFFFFFFFFFFFF, out.ctypes.data)
+        if rc:
+            raise ValueError(f"oracle sample failed: {rc}")
+        return out[:max_new].tolist()
 
     def greedy(self, ids, max_new: int):
         ids = np.ascontiguousarray(ids, dtype=np.int32)
