@@ -303,10 +303,21 @@ def kernel_rooflines(torch, R, peak):
     run = lambda i: R.q4_matvec(xs, wcs[i % copies], scs[i % copies], ys[i % copies], stream=stream)  # noqa: E731
     _timed_chain(torch, stream, run, copies)
     t = _timed_chain(torch, stream, run, 4 * copies)
+    # the same kernel and launch path on a 1-row matvec (576 bytes): the per-launch floor
+    x1, w1, s1 = synth.matvec_case(1, 1024, seed=0)
+    w1d = torch.from_numpy(w1.view(np.int32)).cuda()
+    s1d = torch.from_numpy(s1.astype(np.float16)).cuda()
+    y1 = torch.empty(1, device="cuda")
+    run1 = lambda i: R.q4_matvec(xs, w1d, s1d, y1, stream=stream)  # noqa: E731
+    _timed_chain(torch, stream, run1, copies)
+    t1 = _timed_chain(torch, stream, run1, 4 * copies)
     out["q4_matvec_gate_1024x3072"] = {"us_per_launch": round(t * 1e6, 3), "bytes": per,
                                        "achieved_gbs": round(per / t / 1e9, 1),
                                        "frac": round(per / t / 1e9 / peak, 4),
-                                       "note": "isolated launches back to back (PDL), distinct weights"}
+                                       "launch_floor_us": round(t1 * 1e6, 3),
+                                       "frac_above_floor": round(per / max(t - t1, 1e-9) / 1e9 / peak, 4),
+                                       "note": "isolated launches back to back (PDL), distinct weights; "
+                                               "launch_floor_us: the same launches of a 1-row matvec"}
     del wcs, scs
     table, xh, eps = synth.lm_head_case()
     tb = torch.from_numpy(table.view(np.uint16)).cuda().view(torch.float16)
