@@ -242,7 +242,7 @@ PArgs persist_args(qd_engine* e, bool with_head) {
   a.logits = e->logits; a.part_v = e->lm_pv; a.part_i = e->lm_pi; a.counter = e->lm_counter;
   a.with_head = with_head ? 1 : 0; a.lm_rows = e->lm_rows; a.timeline = e->timeline;
   a.rec_h = rec_bytes(p.hidden); a.rec_q = rec_bytes(p.heads * kHeadDim); a.rec_i = rec_bytes(p.intermediate);
-  a.OS = e->os; a.rec_og = e->rec_og; a.oslice_rows = e->oslice_rows; a.oacc = e->oacc;
+  a.OS = e->os; a.rec_og = e->rec_og; a.oslice_rows = e->oslice_rows; a.oacc = e->oacc; a.n_mlp = e->n_mlp;
   return a;
 }
 
@@ -283,6 +283,30 @@ __global__ void k_pack_oslices(const char* o, char* dst, int H, int NKV, int OS,
   }
 }
 
+// Packs, for one layer, the down-projection slices of the fused MLP stage: CTA c of g
+// owns intermediate columns [I c / g, I (c+1) / g) (at most kDMaxCols, so within two
+// q4 blocks); its slice holds, per hidden row, those columns' nibbles from nibble 0
+// (unused ones 8) and the f16 scales of the first block and the next one.
+__global__ void k_pack_dslices(const char* d, char* dst, int H, int I, int g, long long rec_i) {
+  const int nb = I / kBlockCols;
+  const long long n = (long long)g * H;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const int c = (int)(i / H), r = (int)(i % H);
+    const int lo = (int)((unsigned)I * (unsigned)c / (unsigned)g), hi = (int)((unsigned)I * (unsigned)(c + 1) / (unsigned)g);
+    const unsigned char* row = reinterpret_cast<const unsigned char*>(d + (long long)r * rec_i);
+    const unsigned short* scl = reinterpret_cast<const unsigned short*>(row + (long long)nb * 16);
+    uint32_t w[3] = {0x88888888u, 0x88888888u, 0x88888888u};
+    for (int j = 0; j < hi - lo && j < kDMaxCols; ++j) {
+      const int col = lo + j, blk = col / kBlockCols, cc = col % kBlockCols;
+      const uint32_t nib = (row[blk * 16 + cc / 2] >> (4 * (cc & 1))) & 15u;
+      w[j >> 3] = (w[j >> 3] & ~(15u << (4 * (j & 7)))) | (nib << (4 * (j & 7)));
+    }
+    const int b0 = lo / kBlockCols;
+    const uint32_t sa = hi > lo ? scl[b0] : 0u, sb = hi > lo && b0 + 1 < nb ? scl[b0 + 1] : 0u;
+    reinterpret_cast<uint4*>(dst)[i] = make_uint4(w[0], w[1], w[2], sa | (sb << 16));
+  }
+}
+
 // Decide whether the persistent kernel fits this shape and device; set it up if so.
 void setup_persist(qd_engine* e) {
   const qd_profile& p = e->p;
@@ -296,12 +320,12 @@ void setup_persist(qd_engine* e) {
   // attention CTAs per KV head: each owns H / OS rows of the O projection
   const int OS = std::min(16, g / std::max(1, p.kv_heads));
   const long long rec_og = rec_bytes(G * kHeadDim), oslice_rows = OS > 0 ? (H + OS - 1) / OS : 0;
-  // gate/up rows per CTA: whole words of three activations
-  const long long rows_i = 3 * (((I + 2) / 3 + g - 1) / g);
+  // intermediate columns per CTA (gate/up pairs, then their down partial)
+  const long long cols_i = (I + g - 1) / g;
   bool ok = e->opt.persistent && coop && G <= 2 && H <= 1024 && QS <= 2048 && I <= 3072 && p.kv_heads <= g &&
-            rows_i * 2 * rec_h <= kSlotBytes && 2 * rows_i <= kMaxRes / 2 && (I + 2) / 3 <= 4 * kPT &&
+            cols_i <= kDMaxCols && 2 * cols_i <= kMaxRes / 2 && (long long)H * kDRec <= kSlotBytes &&
             OS >= 1 && oslice_rows <= kMaxRes && oslice_rows * rec_og <= kSlotBytes &&
-            per_cta(R, rec_h) <= kSlotBytes && per_cta(I, 2 * rec_h) <= kSlotBytes && per_cta(H, rec_i) <= kSlotBytes &&
+            per_cta(R, rec_h) <= kSlotBytes && per_cta(I, 2 * rec_h) <= kSlotBytes &&
             2LL * H <= kSlotBytes;
   if (!ok) return;
   const int maxk = std::max(std::max(H, QS), I);
@@ -339,14 +363,24 @@ void setup_persist(qd_engine* e) {
                                               p.kv_heads, OS, G, rec_q, QS / kBlockCols, rec_og, oslice_rows);
   QD_CK(cudaGetLastError());
   QD_CK(cudaStreamSynchronize(e->stream));
-  const size_t acc_bytes = (size_t)2 * p.layers * H * 8;
-  if (cudaMalloc(&e->oacc, acc_bytes) != cudaSuccess) throw QdError{QD_E_NOMEM, "cannot allocate the O sums"};
+  // down slices of the fused MLP stage (one per CTA of the launch)
+  e->n_mlp = std::min(g, I);
+  const long long dslice_per_layer = (long long)g * H * kDRec;
+  if (cudaMalloc(&e->dslices, (size_t)dslice_per_layer * p.layers) != cudaSuccess)
+    throw QdError{QD_E_NOMEM, "cannot allocate the packed down slices"};
+  for (int l = 0; l < p.layers; ++l)
+    k_pack_dslices<<<148, 256, 0, e->stream>>>(e->layers[l].d, e->dslices + (size_t)dslice_per_layer * l, H, I, g,
+                                               rec_i);
+  QD_CK(cudaGetLastError());
+  QD_CK(cudaStreamSynchronize(e->stream));
+  const size_t acc_bytes = (size_t)2 * p.layers * 2 * H * 8;
+  if (cudaMalloc(&e->oacc, acc_bytes) != cudaSuccess) throw QdError{QD_E_NOMEM, "cannot allocate the O / down sums"};
   QD_CK(cudaMemset(e->oacc, 0, acc_bytes));
   std::vector<PLayer> pl(p.layers);
   for (int l = 0; l < p.layers; ++l) {
     const LayerDev& L = e->layers[l];
     pl[l] = PLayer{L.qkv, L.o, L.gu, L.d, L.n_in, L.n_q, L.n_k, L.n_post, L.kc, L.vc,
-                   e->oslices + (size_t)slices_per_layer * l};
+                   e->oslices + (size_t)slices_per_layer * l, e->dslices + (size_t)dslice_per_layer * l};
   }
   if (cudaMalloc(&e->d_players, sizeof(PLayer) * p.layers) != cudaSuccess)
     throw QdError{QD_E_NOMEM, "cannot allocate the layer table"};
@@ -906,6 +940,7 @@ void free_engine(qd_engine* e) {
   if (e->c_cnt) cudaFree(e->c_cnt);
   if (e->d_players) cudaFree(e->d_players);
   if (e->oslices) cudaFree(e->oslices);
+  if (e->dslices) cudaFree(e->dslices);
   if (e->sample_ws) cudaFree(e->sample_ws);
   if (e->oacc) cudaFree(e->oacc);
   if (e->timeline) cudaFree(e->timeline);
@@ -945,8 +980,8 @@ void check_state(qd_engine* e) {
     e->pinned_state->stall_epoch = 0;
     QD_CK(cudaMemcpyAsync(e->st, e->pinned_state, sizeof(DevState), cudaMemcpyHostToDevice, e->stream));
     QD_CK(cudaMemsetAsync(e->lm_counter, 0, 4, e->stream));
-    if (e->oacc)  // a failed launch may leave partial O sums in its parity
-      QD_CK(cudaMemsetAsync(e->oacc, 0, (size_t)2 * e->p.layers * e->p.hidden * 8, e->stream));
+    if (e->oacc)  // a failed launch may leave partial O / down sums in its parity
+      QD_CK(cudaMemsetAsync(e->oacc, 0, (size_t)2 * e->p.layers * 2 * e->p.hidden * 8, e->stream));
     if (e->clus) {  // a failed launch may leave partial sums and counts in either parity
       QD_CK(cudaMemsetAsync(e->c_acc, 0, (size_t)2 * e->p.layers * 2 * e->p.hidden * 8, e->stream));
       QD_CK(cudaMemsetAsync(e->c_cnt, 0, (size_t)2 * e->p.layers * 2 * 32 * 4, e->stream));

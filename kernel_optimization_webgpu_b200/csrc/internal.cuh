@@ -163,7 +163,9 @@ struct qd_engine {
   unsigned long long* timeline = nullptr;  // stage stamps of the last persistent launch (opt-in)
   void* sample_ws = nullptr;               // sampling candidates (allocated on first use)
   char* oslices = nullptr;                 // O rows x KV-head columns, packed per attention CTA
-  unsigned long long* oacc = nullptr;      // [2][L][H] counted fixed-point O sums
+  char* dslices = nullptr;                 // down rows x one CTA's intermediate columns, packed per CTA
+  int n_mlp = 0;                           // CTAs that contribute to the down sums
+  unsigned long long* oacc = nullptr;      // [2][L][O | down][H] counted fixed-point sums
   int os = 0;                              // attention CTAs per KV head
   long long rec_og = 0, oslice_rows = 0;
   // cluster decode kernel (cluster.cuh)

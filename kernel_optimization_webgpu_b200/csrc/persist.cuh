@@ -19,7 +19,11 @@
 // 64-bit counted fixed-point words (2^56 + round(v * 2^28) per contribution:
 // the top byte counts contributions, the rest is their exact sum, so the sum
 // does not depend on arrival order), and consumers poll those words until the
-// count reaches the number of KV heads. The accumulators are double-buffered
+// count reaches the number of KV heads. The MLP is one stage the same way:
+// every CTA owns a run of <= 24 intermediate columns, computes their gate/up
+// rows and silu(gate) * up, multiplies them by its slice of the down columns
+// (packed per CTA, 16 bytes per down row) and adds the partial down sums to
+// counted words that the next layer polls. The accumulators are double-buffered
 // by launch parity; each launch zeroes the other parity for the next one.
 // Every wait has a deadline (globaltimer) and an abort flag: on expiry the
 // kernel sets an error bit, waits for its own copies in flight and returns.
@@ -57,7 +61,13 @@ struct PLayer {
   // O rows x one KV head's columns, packed per attention CTA: slice (g, s) at
   // oslice + (g * OS + s) * oslice_rows * rec_og, rows of s's range as row records
   const char* oslice;
+  // down rows x one CTA's intermediate columns, packed per CTA: CTA c's slice at
+  // dslice + c * H * kDRec; row record = 3 words of 8 nibbles (its <= 24 columns
+  // from nibble 0, unused ones 8) and the f16 scales of the two blocks they span
+  const char* dslice;
 };
+constexpr int kDRec = 16;      // bytes of one packed down row
+constexpr int kDMaxCols = 24;  // intermediate columns per CTA at most
 
 struct PArgs {
   const PLayer* layers;
@@ -79,7 +89,8 @@ struct PArgs {
   long long rec_h, rec_q, rec_i;           // row record bytes for K = H, NH*128, I
   int OS;                                  // attention CTAs per KV head (each owns a slice of O rows)
   long long rec_og, oslice_rows;           // O slice row record bytes (K = G*128), rows per slice (max)
-  unsigned long long* oacc;                // [2 parities][L][H] counted fixed-point O sums
+  unsigned long long* oacc;                // [2 parities][L][O | down][H] counted fixed-point sums
+  int n_mlp;                               // CTAs that own intermediate columns (contributors to the down sums)
 };
 
 // ---- small PTX helpers --------------------------------------------------------
@@ -95,22 +106,6 @@ __device__ __forceinline__ unsigned long long ld_word(const unsigned long long* 
   unsigned long long v;
   asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
-}
-// The gate/up stage's activations travel three to a 16-byte word {a, b, c, epoch},
-// stored and loaded as single 128-bit accesses: a third of the words to poll.
-constexpr int kActPer = 3;
-__device__ __forceinline__ void st_word3(unsigned long long* p, float a, float b, float c, unsigned epoch) {
-  const unsigned long long lo = ((unsigned long long)__float_as_uint(b) << 32) | __float_as_uint(a);
-  const unsigned long long hi = ((unsigned long long)epoch << 32) | __float_as_uint(c);
-  asm volatile("{\n\t.reg .b128 t;\n\tmov.b128 t, {%1, %2};\n\tst.relaxed.gpu.global.b128 [%0], t;\n\t}" ::"l"(p),
-               "l"(lo), "l"(hi)
-               : "memory");
-}
-__device__ __forceinline__ void ld_word3(const unsigned long long* p, unsigned long long& lo, unsigned long long& hi) {
-  asm volatile("{\n\t.reg .b128 t;\n\tld.relaxed.gpu.global.b128 t, [%2];\n\tmov.b128 {%0, %1}, t;\n\t}"
-               : "=l"(lo), "=l"(hi)
-               : "l"(p)
-               : "memory");
 }
 __device__ __forceinline__ void st_word(unsigned long long* p, float v, unsigned epoch) {
   const unsigned long long w = ((unsigned long long)epoch << 32) | __float_as_uint(v);
@@ -193,7 +188,10 @@ __device__ __forceinline__ void chunk_src(const PArgs& a, const Ranges& rg, int 
       bytes = rg.att ? (unsigned)((rg.o_hi - rg.o_lo) * a.rec_og) : 0u;
       break;
     case 2: src = P.gu + rg.i_lo * 2 * a.rec_h; bytes = (unsigned)((rg.i_hi - rg.i_lo) * 2 * a.rec_h); break;
-    default: src = P.d + rg.h_lo * a.rec_i; bytes = (unsigned)((rg.h_hi - rg.h_lo) * a.rec_i); break;
+    default:  // this CTA's packed down columns
+      src = P.dslice + (long long)blockIdx.x * a.H * kDRec;
+      bytes = rg.i_hi > rg.i_lo ? (unsigned)(a.H * kDRec) : 0u;
+      break;
   }
 }
 
@@ -262,49 +260,10 @@ __device__ __forceinline__ bool stage_ok(const PArgs& a, bool mine) {
   return __syncthreads_and(mine ? 1 : 0) != 0;
 }
 
-// Every thread: poll 16-byte words w = threadIdx.x + k*kPT < nw (nw <= 4 kPT) of three
-// values each until they carry this launch's epoch; value 3w + j (< n) goes to the
-// swizzled staging. False on timeout/abort.
-__device__ __forceinline__ bool poll3_to_smem(const PArgs& a, const unsigned long long* src, int nw, int n,
-                                              unsigned epoch, float* xs) {
-  constexpr int K = 4;
-  unsigned long long lo[K], hi[K];
-  unsigned need = 0;
-#pragma unroll
-  for (int k = 0; k < K; ++k) {
-    const int w = threadIdx.x + k * kPT;
-    lo[k] = hi[k] = 0ull;
-    if (w < nw) {
-      ld_word3(src + 2 * w, lo[k], hi[k]);
-      need |= 1u << k;
-    }
-  }
-  unsigned long long t0 = 0;
-  for (unsigned it = 0;; ++it) {
-#pragma unroll
-    for (int k = 0; k < K; ++k) {
-      if (((need >> k) & 1u) && (unsigned)(hi[k] >> 32) == epoch) {
-        need &= ~(1u << k);
-        const int e = 3 * (threadIdx.x + k * kPT);
-        xs_store(xs, e, __uint_as_float((unsigned)lo[k]));
-        if (e + 1 < n) xs_store(xs, e + 1, __uint_as_float((unsigned)(lo[k] >> 32)));
-        if (e + 2 < n) xs_store(xs, e + 2, __uint_as_float((unsigned)hi[k]));
-      }
-    }
-    if (!need) return true;
-    if (it == 0) t0 = gtimer();
-    else if ((it & 15) == 0 && (aborted(a) || gtimer() - t0 > kWaitNs)) return false;
-    __nanosleep(kPollBackoffNs);
-#pragma unroll
-    for (int k = 0; k < K; ++k)
-      if ((need >> k) & 1u) ld_word3(src + 2 * (threadIdx.x + k * kPT), lo[k], hi[k]);
-  }
-}
-
 // ---- counted fixed-point sums ------------------------------------------------------
 constexpr float kFxScale = 268435456.0f;              // 2^28
 constexpr float kFxInv = 3.7252902984619140625e-9f;   // 2^-28
-constexpr float kFxMax = 4194304.0f;                  // 2^22: 16 such partials still fit 55 bits
+constexpr float kFxMax = 524288.0f;                   // 2^19: 148 such partials still fit 55 bits
 
 __device__ __forceinline__ void red_fx(const PArgs& a, unsigned long long* p, float v) {
   if (!(fabsf(v) < kFxMax)) {  // also catches NaN
@@ -747,6 +706,39 @@ __device__ __forceinline__ bool attn_o_stage(const PArgs& a, const PShared& S, c
   return true;
 }
 
+// This CTA's partial of the down projection: rows r = tid, tid + kPT (< H) over its n
+// intermediate columns (act[0..kDMaxCols), shared memory, zero past n; 16-byte
+// aligned; the first `split` columns lie in
+// the scale of the record's first block, the rest in the second), added to the
+// counted sums acc[r]. Nibbles become floats through the 2^23 + n bit pattern.
+__device__ __forceinline__ void down_partial(const PArgs& a, const char* slot, int n, int split, const float* act,
+                                             unsigned long long* acc, int H) {
+#pragma unroll 1
+  for (int k = 0; k < 2; ++k) {
+    const int r = threadIdx.x + k * kPT;
+    if (r >= H) break;
+    const uint4 rec = reinterpret_cast<const uint4*>(slot)[r];
+    const uint32_t w[3] = {rec.x, rec.y, rec.z};
+    float pa = 0.0f, pb = 0.0f;
+#pragma unroll
+    for (int q = 0; q < kDMaxCols / 4; ++q) {
+      const float4 x4 = reinterpret_cast<const float4*>(act)[q];  // same address in every lane
+      const float x[4] = {x4.x, x4.y, x4.z, x4.w};
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const int j = 4 * q + t;
+        const uint32_t nib = (w[j >> 3] >> (4 * (j & 7))) & 15u;
+        const float v = __int_as_float(0x4B000000 | (int)nib) - 8388616.0f;  // nib - 8
+        if (j < split) pa = fmaf(v, x[t], pa);
+        else pb = fmaf(v, x[t], pb);
+      }
+    }
+    const float sa = __half2float(__ushort_as_half((unsigned short)(rec.w & 0xFFFFu)));
+    const float sb = __half2float(__ushort_as_half((unsigned short)(rec.w >> 16)));
+    red_fx(a, acc + r, sa * pa + sb * pb);
+  }
+}
+
 // RMSNorm of v[e] (shared memory, e = tid, tid + kPT) with the thread's
 // prefetched weights w into the swizzled staging; all threads must call it.
 __device__ __forceinline__ void rms_own(const float* v, const float (&w)[2], int n, float eps, float* xs,
@@ -770,6 +762,21 @@ __device__ __forceinline__ void rms_own(const float* v, const float (&w)[2], int
     const int e = threadIdx.x + k * kPT;
     if (e < n) xs_store(xs, e, x[k] * inv * w[k]);
   }
+}
+
+// Every thread: the final hidden state = h_attn of the last layer + its down sums
+// into S.hs, and this CTA's rows of it out as words (read back by the host). H <= 2 kPT.
+__device__ __forceinline__ bool final_hidden(const PArgs& a, const Ranges& rg, unsigned epoch, int H,
+                                             const PShared& S) {
+  const unsigned long long* acc_d = a.oacc + ((long long)(epoch & 1u) * a.L + (a.L - 1)) * 2 * H + H;
+  if (!poll_fx(a, acc_d, H, (unsigned)a.n_mlp, S.has, S.hs)) return false;
+  unsigned long long* xf = a.xb + (long long)a.L * a.xstride;
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {  // the elements this thread polled itself (no barrier needed)
+    const int e = threadIdx.x + k * kPT;
+    if (e >= rg.h_lo && e < rg.h_hi) st_word(xf + e, S.hs[e], epoch);
+  }
+  return true;
 }
 
 // ---- the kernel -------------------------------------------------------------------
@@ -805,13 +812,7 @@ __global__ void __launch_bounds__(kPT, 1) k_decode_persistent(const __grid_const
   Ranges rg;
   range_of(R, cta, ng, rg.qkv_lo, rg.qkv_hi);
   range_of(H, cta, ng, rg.h_lo, rg.h_hi);
-  {  // gate/up rows in whole activation words
-    const int words = (I + kActPer - 1) / kActPer;
-    int w_lo, w_hi;
-    range_of(words, cta, ng, w_lo, w_hi);
-    rg.i_lo = min(I, w_lo * kActPer);
-    rg.i_hi = min(I, w_hi * kActPer);
-  }
+  range_of(I, cta, ng, rg.i_lo, rg.i_hi);
   range_of(a.vocab, cta, ng, rg.v_lo, rg.v_hi);
   rg.att = cta < a.NKV * a.OS;
   rg.ag = rg.att ? cta / a.OS : 0;
@@ -821,7 +822,7 @@ __global__ void __launch_bounds__(kPT, 1) k_decode_persistent(const __grid_const
   const int n_chunks = 4 * a.L;
   // The next launch's O sums start at zero: clear the other parity's words.
   {
-    const long long words = (long long)a.L * H;
+    const long long words = (long long)a.L * 2 * H;
     unsigned long long* other = a.oacc + (long long)((epoch + 1u) & 1u) * words;
     const long long lo = words * cta / ng, hi = words * (cta + 1) / ng;
     for (long long i = lo + threadIdx.x; i < hi; i += kPT) other[i] = 0ull;
@@ -857,17 +858,18 @@ __global__ void __launch_bounds__(kPT, 1) k_decode_persistent(const __grid_const
   }
   for (int l = 0; l < a.L; ++l) {
     const PLayer& P = a.layers[l];
-    unsigned long long* X = a.xb + (long long)l * a.xstride;
-    unsigned long long *xh = X, *xq = X + H, *xact = X + H + R + QS + H;
-    unsigned long long* xnext = a.xb + (long long)(l + 1) * a.xstride;
+    unsigned long long* xq = a.xb + (long long)l * a.xstride + H;
+    unsigned long long* acc_o = a.oacc + ((long long)(epoch & 1u) * a.L + l) * 2 * H;  // O sums
+    unsigned long long* acc_d = acc_o + H;                                              // down sums
     const int ev = 1 + l * kTimelinePerLayer;
 
-    // 1. input RMSNorm + QKV rows
+    // 1. layer input (the embedding row, or h_attn + the down sums of the previous
+    //    layer), RMSNorm, QKV rows
     {
       float nw[2];
 #pragma unroll
       for (int k = 0; k < 2; ++k) nw[k] = threadIdx.x + k * kPT < H ? P.n_in[threadIdx.x + k * kPT] : 0.0f;
-      if (l > 0) QD_FAIL_IF(!stage_ok(a, poll_to_smem(a, xh, H, epoch, S.hs, false)));
+      if (l > 0) QD_FAIL_IF(!stage_ok(a, poll_fx(a, acc_o - H, H, (unsigned)a.n_mlp, S.has, S.hs)));
       stamp(tl, ev + 0);
       rms_own(S.hs, nw, H, a.eps, S.xs, S.red);
       stamp(tl, ev + 10);
@@ -886,9 +888,8 @@ __global__ void __launch_bounds__(kPT, 1) k_decode_persistent(const __grid_const
     // 2. attention + O slice (the attention CTAs; every CTA passes chunk 4l+1, empty for
     //    the others), then 3. h_attn = h + the O sums (every CTA)
     {
-      unsigned long long* acc = a.oacc + ((long long)(epoch & 1u) * a.L + l) * H;
       if (rg.att) {
-        QD_FAIL_IF((!attn_o_stage<G, KVT>(a, S, rg, l, pos, epoch, xq, acc, chunk, xs_floats, tl, ev)));
+        QD_FAIL_IF((!attn_o_stage<G, KVT>(a, S, rg, l, pos, epoch, xq, acc_o, chunk, xs_floats, tl, ev)));
       } else {
         QD_FAIL_IF(!stage_ok(a, wait_chunk(a, S, chunk)));
       }
@@ -896,13 +897,14 @@ __global__ void __launch_bounds__(kPT, 1) k_decode_persistent(const __grid_const
       stamp(tl, ev + 3);
       if (threadIdx.x == 0) issue_chunk(a, S, rg, chunk + kSlots, n_chunks);
       ++chunk;
-      QD_FAIL_IF(!stage_ok(a, poll_fx(a, acc, H, (unsigned)a.NKV, S.hs, S.has)));
+      QD_FAIL_IF(!stage_ok(a, poll_fx(a, acc_o, H, (unsigned)a.NKV, S.hs, S.has)));
       stamp(tl, ev + 4);
       stamp(tl, ev + 11);
       stamp(tl, ev + 5);
     }
 
-    // 4. post-attention RMSNorm + gate/up + silu * up
+    // 4. post-attention RMSNorm, gate/up rows of this CTA's intermediate columns,
+    //    silu(gate) * up, and their partial of the down projection into the down sums
     {
       float nw[2];
 #pragma unroll
@@ -914,38 +916,25 @@ __global__ void __launch_bounds__(kPT, 1) k_decode_persistent(const __grid_const
       const int n = rg.i_hi - rg.i_lo;
       stage_dots(S.ring + (chunk % kSlots) * kSlotBytes, n, 2, (int)a.rec_h, H / kBlockCols, 1, S.xs, S.res);
       __syncthreads();
-      float* act = S.res + kMaxRes / 2;  // this CTA's activations, then three to a word
-      if (threadIdx.x < n) {
-        const float gt = S.res[2 * threadIdx.x], upv = S.res[2 * threadIdx.x + 1];
-        act[threadIdx.x] = (gt / (1.0f + expf(-gt))) * upv;
-      }
-      __syncthreads();
-      const int w0 = rg.i_lo / kActPer, n_words = (n + kActPer - 1) / kActPer;
-      if (threadIdx.x < n_words) {
-        const int j = kActPer * threadIdx.x;
-        st_word3(xact + 2 * (w0 + threadIdx.x), act[j], j + 1 < n ? act[j + 1] : 0.0f, j + 2 < n ? act[j + 2] : 0.0f,
-                 epoch);
+      float* act = S.res + kMaxRes / 2;  // this CTA's activations
+      if (threadIdx.x < kDMaxCols) {  // zero past n: the down partial reads all kDMaxCols
+        float v = 0.0f;
+        if (threadIdx.x < n) {
+          const float gt = S.res[2 * threadIdx.x], upv = S.res[2 * threadIdx.x + 1];
+          v = (gt / (1.0f + expf(-gt))) * upv;
+        }
+        act[threadIdx.x] = v;
       }
       __syncthreads();
       stamp(tl, ev + 7);
       if (threadIdx.x == 0) issue_chunk(a, S, rg, chunk + kSlots, n_chunks);
       ++chunk;
-    }
-
-    // 5. down projection + residual
-    {
-      QD_FAIL_IF(!stage_ok(a, poll3_to_smem(a, xact, (I + kActPer - 1) / kActPer, I, epoch, S.xs)));
-      stamp(tl, ev + 8);
       QD_FAIL_IF(!stage_ok(a, wait_chunk(a, S, chunk)));
+      stamp(tl, ev + 8);
       stamp(tl, ev + 13);
-      const int n = rg.h_hi - rg.h_lo;
-      stage_dots(S.ring + (chunk % kSlots) * kSlotBytes, n, 1, (int)a.rec_i, I / kBlockCols, 3, S.xs, S.res);
-      __syncthreads();
-      if (threadIdx.x < n) {
-        const int r = rg.h_lo + threadIdx.x;
-        st_word(xnext + r, S.has[r] + ((S.res[threadIdx.x] + S.res[n + threadIdx.x]) + S.res[2 * n + threadIdx.x]),
-                epoch);
-      }
+      if (n > 0)
+        down_partial(a, S.ring + (chunk % kSlots) * kSlotBytes, n, min(n, kBlockCols - rg.i_lo % kBlockCols), act,
+                     acc_d, H);
       __syncthreads();
       stamp(tl, ev + 9);
       if (threadIdx.x == 0) issue_chunk(a, S, rg, chunk + kSlots, n_chunks);
@@ -983,8 +972,7 @@ __global__ void __launch_bounds__(kPT, 1) k_decode_persistent(const __grid_const
     float fw[2];
 #pragma unroll
     for (int k = 0; k < 2; ++k) fw[k] = threadIdx.x + k * kPT < H ? a.final_norm[threadIdx.x + k * kPT] : 0.0f;
-    unsigned long long* xf = a.xb + (long long)a.L * a.xstride;
-    if (!stage_ok(a, poll_to_smem(a, xf, H, epoch, S.hs, false))) return;
+    if (!stage_ok(a, final_hidden(a, rg, epoch, H, S))) return;
     float fv[2];
 #pragma unroll
     for (int k = 0; k < 2; ++k) fv[k] = threadIdx.x + k * kPT < H ? S.hs[threadIdx.x + k * kPT] : 0.0f;
@@ -1048,6 +1036,7 @@ __global__ void __launch_bounds__(kPT, 1) k_decode_persistent(const __grid_const
       if (am_better(ov, oi, bv, bi)) { bv = ov; bi = oi; }
     }
   }
+  if (!a.with_head && !stage_ok(a, final_hidden(a, rg, epoch, H, S))) return;
   stamp(tl, 2 + kTimelinePerLayer * a.L);
 
   // CTA partial -> last CTA merges, emits the token and advances the state.
