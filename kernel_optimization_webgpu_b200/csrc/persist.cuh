@@ -739,29 +739,29 @@ __device__ __forceinline__ void down_partial(const PArgs& a, const char* slot, i
   }
 }
 
-// RMSNorm of v[e] (shared memory, e = tid, tid + kPT) with the thread's
-// prefetched weights w into the swizzled staging; all threads must call it.
-__device__ __forceinline__ void rms_own(const float* v, const float (&w)[2], int n, float eps, float* xs,
-                                        float* red) {
-  float x[2] = {0.0f, 0.0f}, ss = 0.0f;
-#pragma unroll
-  for (int k = 0; k < 2; ++k)
-    if (threadIdx.x + k * kPT < n) {
-      x[k] = v[threadIdx.x + k * kPT];
-      ss += x[k] * x[k];
-    }
-  ss = warp_sum(ss);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
-  __syncthreads();
-  float t = 0.0f;
-#pragma unroll
-  for (int k = 0; k < kPW; ++k) t += red[k];
-  const float inv = rsqrtf(t / (float)n + eps);
+// RMSNorm folded into the dots that follow it: xs holds v[e] * w[e] (e = tid,
+// tid + kPT), red[warp] the warps' sums of squares; the dots over xs times
+// rms_inv(red) are the dots over the normalised vector, so no barrier sits between
+// the input and the dots. The caller's next barrier publishes both.
+__device__ __forceinline__ void weigh_own(const float* v, const float (&w)[2], int n, float* xs, float* red) {
+  float ss = 0.0f;
 #pragma unroll
   for (int k = 0; k < 2; ++k) {
     const int e = threadIdx.x + k * kPT;
-    if (e < n) xs_store(xs, e, x[k] * inv * w[k]);
+    if (e < n) {
+      const float x = v[e];
+      ss += x * x;
+      xs_store(xs, e, x * w[k]);
+    }
   }
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+}
+__device__ __forceinline__ float rms_inv(const float* red, int n, float eps) {
+  float t = 0.0f;
+#pragma unroll
+  for (int k = 0; k < kPW; ++k) t += red[k];
+  return rsqrtf(t / (float)n + eps);
 }
 
 // Every thread: the final hidden state = h_attn of the last layer + its down sums
@@ -871,14 +871,15 @@ __global__ void __launch_bounds__(kPT, 1) k_decode_persistent(const __grid_const
       for (int k = 0; k < 2; ++k) nw[k] = threadIdx.x + k * kPT < H ? P.n_in[threadIdx.x + k * kPT] : 0.0f;
       if (l > 0) QD_FAIL_IF(!stage_ok(a, poll_fx(a, acc_o - H, H, (unsigned)a.n_mlp, S.has, S.hs)));
       stamp(tl, ev + 0);
-      rms_own(S.hs, nw, H, a.eps, S.xs, S.red);
+      weigh_own(S.hs, nw, H, S.xs, S.red);
       stamp(tl, ev + 10);
       QD_FAIL_IF(!stage_ok(a, wait_chunk(a, S, chunk)));
       stamp(tl, ev + 1);
       const int n = rg.qkv_hi - rg.qkv_lo;
       stage_dots(S.ring + (chunk % kSlots) * kSlotBytes, n, 1, (int)a.rec_h, H / kBlockCols, 1, S.xs, S.res);
       __syncthreads();
-      if (threadIdx.x < n && !(stall && l == 0)) st_word(xq + rg.qkv_lo + threadIdx.x, S.res[threadIdx.x], epoch);
+      if (threadIdx.x < n && !(stall && l == 0))
+        st_word(xq + rg.qkv_lo + threadIdx.x, S.res[threadIdx.x] * rms_inv(S.red, H, a.eps), epoch);
       __syncthreads();
       stamp(tl, ev + 2);
       if (threadIdx.x == 0) issue_chunk(a, S, rg, chunk + kSlots, n_chunks);
@@ -910,7 +911,7 @@ __global__ void __launch_bounds__(kPT, 1) k_decode_persistent(const __grid_const
 #pragma unroll
       for (int k = 0; k < 2; ++k) nw[k] = threadIdx.x + k * kPT < H ? P.n_post[threadIdx.x + k * kPT] : 0.0f;
       stamp(tl, ev + 6);
-      rms_own(S.has, nw, H, a.eps, S.xs, S.red);
+      weigh_own(S.has, nw, H, S.xs, S.red);
       stamp(tl, ev + 12);
       QD_FAIL_IF(!stage_ok(a, wait_chunk(a, S, chunk)));
       const int n = rg.i_hi - rg.i_lo;
@@ -920,7 +921,8 @@ __global__ void __launch_bounds__(kPT, 1) k_decode_persistent(const __grid_const
       if (threadIdx.x < kDMaxCols) {  // zero past n: the down partial reads all kDMaxCols
         float v = 0.0f;
         if (threadIdx.x < n) {
-          const float gt = S.res[2 * threadIdx.x], upv = S.res[2 * threadIdx.x + 1];
+          const float inv = rms_inv(S.red, H, a.eps);
+          const float gt = S.res[2 * threadIdx.x] * inv, upv = S.res[2 * threadIdx.x + 1] * inv;
           v = (gt / (1.0f + expf(-gt))) * upv;
         }
         act[threadIdx.x] = v;
