@@ -282,7 +282,7 @@ __device__ __forceinline__ float fx_value(unsigned long long w) {
 
 // Every thread: poll counted words src[e], e = threadIdx.x + k*kPT < n (n <= 4 kPT),
 // until each holds `need` contributions; dst[e] = base[e] + sum. False on timeout/abort.
-__device__ __forceinline__ bool poll_fx(const PArgs& a, const unsigned long long* src, int n, unsigned need,
+static __device__ __noinline__ bool poll_fx(const PArgs& a, const unsigned long long* src, int n, unsigned need,
                                         const float* base, float* dst) {
   constexpr int K = 4;
   unsigned long long v[K];
@@ -350,7 +350,7 @@ __device__ __forceinline__ float reduce4(float p0, float p1, float p2, float p3)
 // (kPW / kc warps per chunk, each holding only that chunk's activations) and
 // process 4 items at a time, so four independent dot chains overlap and share
 // one 6-shuffle reduction.
-__device__ __forceinline__ void stage_dots(const char* slot, int n_rows, int nw, int rec, int nb, int kc,
+static __device__ __noinline__ void stage_dots(const char* slot, int n_rows, int nw, int rec, int nb, int kc,
                                         const float* xs, float* res) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int wpc = kPW / kc;
@@ -589,6 +589,7 @@ __device__ __forceinline__ bool attn_o_stage(const PArgs& a, const PShared& S, c
         for (int h = 0; h < G; ++h) scs[h * 64 + p] = d[h] * a.scale;
     }
     __syncthreads();
+    stamp(tl, ev + 11);
     // softmax of each head (warp h): probabilities in place
     if (warp < G) {
       const float s0 = lane <= pos ? scs[warp * 64 + lane] : -INFINITY;
@@ -600,6 +601,7 @@ __device__ __forceinline__ bool attn_o_stage(const PArgs& a, const PShared& S, c
       if (lane + 32 <= pos) scs[warp * 64 + lane + 32] = e1 * inv;
     }
     __syncthreads();
+    stamp(tl, ev + 5);
     // weighted sum of the V rows: thread e -> (head e / 128, dim e % 128)
     for (int e = threadIdx.x; e < G * kHeadDim; e += kPT) {
       const int h = e / kHeadDim, d = e % kHeadDim;
@@ -900,8 +902,6 @@ __global__ void __launch_bounds__(kPT, 1) k_decode_persistent(const __grid_const
       ++chunk;
       QD_FAIL_IF(!stage_ok(a, poll_fx(a, acc_o, H, (unsigned)a.NKV, S.hs, S.has)));
       stamp(tl, ev + 4);
-      stamp(tl, ev + 11);
-      stamp(tl, ev + 5);
     }
 
     // 4. post-attention RMSNorm, gate/up rows of this CTA's intermediate columns,
