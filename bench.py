@@ -37,8 +37,9 @@ from kernel_optimization_webgpu_b200 import synth  # noqa: E402
 
 PROMPT_LEN, NEW_TOKENS = 8, 24
 # DRAM bytes (read + write) of one k_decode_persistent token launch, measured by ncu
-# on the default workload (560.96 MB read + 3.94 MB written).
-B1_TRAFFIC = 564897280
+# on the default workload (579.45 MB read + 4.77 MB written; the per-CTA packed O and
+# down slices read ~18 MB more than the row records they are packed from).
+B1_TRAFFIC = 584217088
 WORKLOAD = ("batch-1 greedy decode, Qwen3-0.6B shape (28 layers, hidden 1024, 16q/8kv heads x 128, "
             "SwiGLU 3072, q4 MatMulNBits block 32 with f16 scales, tied f16 LM head 151936x1024, f16 KV), "
             "8-token prompt + 24 generated, seed 2")

@@ -149,8 +149,11 @@ __device__ __forceinline__ void bulk_load_hint(void* dst, const void* src, unsig
       : "memory");
 }
 
+// All of warp 0 stores the same word: a store by one lane leaves the warp diverged,
+// and its next warp-collective step then pays ~800 cycles to reconverge (measured),
+// which the stamps would report as that step's own time.
 __device__ __forceinline__ void stamp(unsigned long long* tl, int ev) {
-  if (tl && threadIdx.x == 0) tl[ev] = gtimer();
+  if (tl && threadIdx.x < 32) tl[ev] = gtimer();
 }
 
 // Contiguous split of n rows over g CTAs (n * g < 2^31 for every shape served).
