@@ -353,8 +353,10 @@ __device__ __forceinline__ float reduce4(float p0, float p1, float p2, float p3)
 // (kPW / kc warps per chunk, each holding only that chunk's activations) and
 // process 4 items at a time, so four independent dot chains overlap and share
 // one 6-shuffle reduction.
-static __device__ __noinline__ void stage_dots(const char* slot, int n_rows, int nw, int rec, int nb, int kc,
-                                        const float* xs, float* res) {
+template <int NW>
+__device__ __forceinline__ void stage_dots(const char* slot, int n_rows, int rec, int nb, int kc, const float* xs,
+                                           float* res) {
+  constexpr int nw = NW;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int wpc = kPW / kc;
   const int c = warp / wpc, u = warp - c * wpc;
@@ -881,7 +883,7 @@ __global__ void __launch_bounds__(kPT, 1) k_decode_persistent(const __grid_const
       QD_FAIL_IF(!stage_ok(a, wait_chunk(a, S, chunk)));
       stamp(tl, ev + 1);
       const int n = rg.qkv_hi - rg.qkv_lo;
-      stage_dots(S.ring + (chunk % kSlots) * kSlotBytes, n, 1, (int)a.rec_h, H / kBlockCols, 1, S.xs, S.res);
+      stage_dots<1>(S.ring + (chunk % kSlots) * kSlotBytes, n, (int)a.rec_h, H / kBlockCols, 1, S.xs, S.res);
       __syncthreads();
       if (threadIdx.x < n && !(stall && l == 0))
         st_word(xq + rg.qkv_lo + threadIdx.x, S.res[threadIdx.x] * rms_inv(S.red, H, a.eps), epoch);
@@ -918,7 +920,7 @@ __global__ void __launch_bounds__(kPT, 1) k_decode_persistent(const __grid_const
       stamp(tl, ev + 12);
       QD_FAIL_IF(!stage_ok(a, wait_chunk(a, S, chunk)));
       const int n = rg.i_hi - rg.i_lo;
-      stage_dots(S.ring + (chunk % kSlots) * kSlotBytes, n, 2, (int)a.rec_h, H / kBlockCols, 1, S.xs, S.res);
+      stage_dots<2>(S.ring + (chunk % kSlots) * kSlotBytes, n, (int)a.rec_h, H / kBlockCols, 1, S.xs, S.res);
       __syncthreads();
       float* act = S.res + kMaxRes / 2;  // this CTA's activations
       if (threadIdx.x < kDMaxCols) {  // zero past n: the down partial reads all kDMaxCols
