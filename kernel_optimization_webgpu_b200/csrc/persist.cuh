@@ -360,7 +360,8 @@ __device__ __forceinline__ void stage_dots(const char* slot, int n_rows, int rec
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int wpc = kPW / kc;
   const int c = warp / wpc, u = warp - c * wpc;
-  if (c >= kc) return;
+  const int n_items = n_rows * nw;
+  if (c >= kc || u * 4 >= n_items) return;  // idle warps skip the activation loads
   const int b = c * 32 + lane;
   const bool live = b < nb;
   float2 xr[16];
@@ -374,7 +375,6 @@ __device__ __forceinline__ void stage_dots(const char* slot, int n_rows, int rec
   // A warp takes 4 consecutive items at a time: the activation chunk each warp
   // loads from shared memory (4 KB) is the dominant cost, so few warps with more
   // items each beat many warps with one item each.
-  const int n_items = n_rows * nw;
   for (int i0 = u * 4; i0 < n_items; i0 += wpc * 4) {
     uint4 w[4];
     float s[4];
