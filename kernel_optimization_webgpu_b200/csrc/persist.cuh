@@ -198,7 +198,8 @@ __device__ __forceinline__ void chunk_src(const PArgs& a, const Ranges& rg, int 
   }
 }
 
-// Thread 0 only: put chunk i in flight into its slot.
+// One thread: put chunk i in flight into its slot (after a barrier that ends the
+// slot's last reads).
 __device__ __forceinline__ void issue_chunk(const PArgs& a, const PShared& S, const Ranges& rg, int i, int n) {
   if (i >= n) return;
   const char* src;
@@ -887,9 +888,10 @@ __global__ void __launch_bounds__(kPT, 1) k_decode_persistent(const __grid_const
       __syncthreads();
       if (threadIdx.x < n && !(stall && l == 0))
         st_word(xq + rg.qkv_lo + threadIdx.x, S.res[threadIdx.x] * rms_inv(S.red, H, a.eps), epoch);
-      __syncthreads();
+      // The slot's weights are consumed; the last thread (never a result row: n <= kMaxRes)
+      // refills it, so the refill does not hold back the stores and needs no barrier.
+      if (threadIdx.x == kPT - 1) issue_chunk(a, S, rg, chunk + kSlots, n_chunks);
       stamp(tl, ev + 2);
-      if (threadIdx.x == 0) issue_chunk(a, S, rg, chunk + kSlots, n_chunks);
       ++chunk;
     }
 
