@@ -924,6 +924,9 @@ __global__ void __launch_bounds__(kPT, 1) k_decode_persistent(const __grid_const
       const int n = rg.i_hi - rg.i_lo;
       stage_dots<2>(S.ring + (chunk % kSlots) * kSlotBytes, n, (int)a.rec_h, H / kBlockCols, 1, S.xs, S.res);
       __syncthreads();
+      // The gate/up weights are consumed: the last thread (no activation to write) refills the slot.
+      if (threadIdx.x == kPT - 1) issue_chunk(a, S, rg, chunk + kSlots, n_chunks);
+      ++chunk;
       float* act = S.res + kMaxRes / 2;  // this CTA's activations
       if (threadIdx.x < kDMaxCols) {  // zero past n: the down partial reads all kDMaxCols
         float v = 0.0f;
@@ -934,10 +937,8 @@ __global__ void __launch_bounds__(kPT, 1) k_decode_persistent(const __grid_const
         }
         act[threadIdx.x] = v;
       }
-      __syncthreads();
       stamp(tl, ev + 7);
-      if (threadIdx.x == 0) issue_chunk(a, S, rg, chunk + kSlots, n_chunks);
-      ++chunk;
+      // the down slice's wait ends in a barrier, which also publishes the activations
       QD_FAIL_IF(!stage_ok(a, wait_chunk(a, S, chunk)));
       stamp(tl, ev + 8);
       stamp(tl, ev + 13);
