@@ -167,10 +167,12 @@ struct SampleOut {
   int step;              // kernel-level entry: the RNG step
 };
 
-// Second level: the K best candidates, sorted; the sampled id.
+// Second level: the K best candidates, sorted; the sampled id. n_real = min(K, vocab)
+// of them are tokens: a chunk shorter than K pads its candidates with (key 0, index
+// 0x7fffffff) entries, which sort after every token and are never drawn.
 __global__ void __launch_bounds__(kSampleThreads) k_sample_final(const uint32_t* cand_key, const int* cand_idx,
-                                                                 int n_cand, int K, float temperature, float top_p,
-                                                                 unsigned long long seed, SampleOut o) {
+                                                                 int n_cand, int K, int n_real, float temperature,
+                                                                 float top_p, unsigned long long seed, SampleOut o) {
   extern __shared__ uint32_t dyn[];
   uint32_t* key = dyn;                                   // [n_cand]
   __shared__ uint32_t sm[264];
@@ -181,17 +183,18 @@ __global__ void __launch_bounds__(kSampleThreads) k_sample_final(const uint32_t*
   pdl_wait();
   for (int i = threadIdx.x; i < n_cand; i += blockDim.x) key[i] = cand_key[i];
   __syncthreads();
-  const int k = min(K, n_cand);
+  int k = min(K, n_cand);
   cta_select(key, n_cand, k, sm, sk, sp);
-  // rank sort: larger key first, ties to the lower vocabulary index
+  // rank sort: larger key first, ties to the lower vocabulary index, then to the lower
+  // candidate position (padding entries repeat one key and index): a permutation of 0..k-1
   if (threadIdx.x < k) {
     const uint32_t mk = sk[threadIdx.x];
-    const int mi = cand_idx[sp[threadIdx.x]];
+    const int mp = sp[threadIdx.x], mi = cand_idx[mp];
     int r = 0;
     for (int j = 0; j < k; ++j) {
       const uint32_t ok = sk[j];
-      const int oi = cand_idx[sp[j]];
-      r += ok > mk || (ok == mk && oi < mi);
+      const int op = sp[j], oi = cand_idx[op];
+      r += ok > mk || (ok == mk && (oi < mi || (oi == mi && op < mp)));
     }
     rk[r] = mk;
     ri[r] = mi;
@@ -203,6 +206,7 @@ __global__ void __launch_bounds__(kSampleThreads) k_sample_final(const uint32_t*
     const float v0 = okey_value(rk[0]);
     float cum[kSampleK];
     float s = 0.0f;
+    k = min(k, n_real);  // the tokens among the candidates
     for (int i = 0; i < k; ++i) {
       const float v = okey_value(rk[i]);
       const float p = (v == v && v0 == v0) ? expf((v - v0) / temperature) : (i == 0 ? 1.0f : 0.0f);
@@ -257,7 +261,7 @@ void enqueue_sample(const float* logits, int vocab, const qd_sampling& s, void* 
   launch_ex(k_sample_partial, dim3(chunks), dim3(kSampleThreads), 0, stream, logits, vocab, K, ck, ci);
   const size_t smem = (size_t)chunks * K * 4;  // within the default 48 KB (checked by the callers)
   launch_ex(k_sample_final, dim3(1), dim3(kSampleThreads), smem, stream, (const uint32_t*)ck, (const int*)ci,
-            chunks * K, K, temperature, s.top_p, (unsigned long long)s.seed, o);
+            chunks * K, K, std::min(K, vocab), temperature, s.top_p, (unsigned long long)s.seed, o);
 }
 
 void enqueue_engine_sample(qd_engine* e, const qd_sampling& s) {

@@ -109,6 +109,23 @@ def _cuda():
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("vocab", [1, 3, 7, 63])
+def test_cuda_sampler_vocab_below_the_candidate_count(vocab):
+    """Fewer tokens than candidates (K = 64): the padding candidates of the short chunk
+    are never drawn and the draw matches the oracle, whatever the seed."""
+    torch = _cuda()
+    from kernel_optimization_webgpu_b200 import runtime as R
+    rng = np.random.default_rng(100 + vocab)
+    for case in range(60):
+        logits = (rng.standard_normal(vocab) * 2.0).astype(np.float32)
+        params = (float(rng.choice([0.5, 1.0, 3.0])), int(rng.choice([0, 64, 100])), float(rng.choice([0.5, 1.0])),
+                  int(rng.integers(0, 2**63)), int(rng.integers(0, 10**6)))
+        got = R.sample_logits(torch.from_numpy(logits).cuda(), *params)
+        assert 0 <= got < vocab, (vocab, case, params, got)
+        assert got == O.sample(logits, *params), (vocab, case, params)
+
+
+@pytest.mark.gpu
 @pytest.mark.parametrize("vocab", [7, 1000, 4099, 151936])
 def test_cuda_sampler_matches_the_oracle(vocab):
     torch = _cuda()
