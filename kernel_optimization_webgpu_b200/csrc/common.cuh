@@ -65,6 +65,12 @@ __device__ __forceinline__ uint4 ld_stream(const uint4* p) {
   return r;
 }
 
+__device__ __forceinline__ uint2 ld_stream2(const uint2* p) {
+  uint2 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(r.x), "=r"(r.y) : "l"(p));
+  return r;
+}
+
 // (value, index) argmax order: larger value wins, ties go to the lower index,
 // NaN never wins (every comparison with NaN is false). argmax_stage1.wgsl:51-52.
 __device__ __forceinline__ bool am_better(float v, uint32_t i, float bv, uint32_t bi) {
@@ -103,6 +109,23 @@ __device__ __forceinline__ float2 f16x8_dot(uint4 w, const float2* x, float2 acc
     const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&ws[k]));
     acc = __ffma2_rn(f, x[k], acc);
   }
+  return acc;
+}
+
+// Eight int8 table entries stored biased (q + 128, one uint2) against eight
+// activations (4 float2 pairs), the same column order as f16x8_dot. A byte permute
+// builds the float 2^23 + u and one packed subtract of 2^23 + 128 leaves q exactly.
+__device__ __forceinline__ float2 q8x8_dot(uint2 w, const float2* x, float2 acc) {
+  const float2 bias = make_float2(-8388736.0f, -8388736.0f);
+  const uint32_t ws[2] = {w.x, w.y};
+#pragma unroll
+  for (int h = 0; h < 2; ++h)
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const float a = __int_as_float(__byte_perm(ws[h], 0x4B000000u, 0x7540u + 2 * j));
+      const float b = __int_as_float(__byte_perm(ws[h], 0x4B000000u, 0x7540u + 2 * j + 1));
+      acc = __ffma2_rn(__fadd2_rn(make_float2(a, b), bias), x[2 * h + j], acc);
+    }
   return acc;
 }
 

@@ -229,7 +229,8 @@ void launch_persist_t(qd_engine* e, const PArgs& a, cudaStream_t s) {
   QD_CK(cudaLaunchKernelEx(&cfg, k_decode_persistent<G, KVT>, a));
 }
 
-PArgs persist_args(qd_engine* e, bool with_head) {
+PArgs persist_args(qd_engine* e, int head) {
+  const bool with_head = head != kHeadNone;
   const qd_profile& p = e->p;
   PArgs a{};
   a.layers = e->d_players;
@@ -243,11 +244,13 @@ PArgs persist_args(qd_engine* e, bool with_head) {
   a.with_head = with_head ? 1 : 0; a.lm_rows = e->lm_rows; a.timeline = e->timeline;
   a.rec_h = rec_bytes(p.hidden); a.rec_q = rec_bytes(p.heads * kHeadDim); a.rec_i = rec_bytes(p.intermediate);
   a.OS = e->os; a.rec_og = e->rec_og; a.oslice_rows = e->oslice_rows; a.oacc = e->oacc; a.n_mlp = e->n_mlp;
+  a.pruned = head == kHeadArgmax && e->lm_q8 ? 1 : 0;
+  a.lm_q8 = reinterpret_cast<const uint2*>(e->lm_q8); a.lm_scale = e->lm_scale; a.lm_bound = e->lm_bound;
   return a;
 }
 
-void launch_persist(qd_engine* e, bool with_head, cudaStream_t s) {
-  const PArgs a = persist_args(e, with_head);
+void launch_persist(qd_engine* e, int head, cudaStream_t s) {
+  const PArgs a = persist_args(e, head);
   const int group = e->p.heads / e->p.kv_heads;
   if (e->opt.kv_dtype == QD_KV_F32) {
     if (group == 1) launch_persist_t<1, float>(e, a, s); else launch_persist_t<2, float>(e, a, s);
@@ -305,6 +308,52 @@ __global__ void k_pack_dslices(const char* d, char* dst, int H, int I, int g, lo
     const uint32_t sa = hi > lo ? scl[b0] : 0u, sb = hi > lo && b0 + 1 < nb ? scl[b0 + 1] : 0u;
     reinterpret_cast<uint4*>(dst)[i] = make_uint4(w[0], w[1], w[2], sa | (sb << 16));
   }
+}
+
+// The LM head table as int8 for the argmax-only head: row r holds q = rint(E / s_r),
+// s_r = max|E_r| / 127, stored biased (q + 128), and a bound coefficient b_r such that
+// every fp32 evaluation of the f16 logit E_r . x and of the int8 logit s_r (q . x)
+// (dots of depth <= H) differ by at most b_r ||x||_1: the largest elementwise
+// |E - s q| (measured), the rounding of both dots ((H + 2) 2^-24 each, relative to
+// max|E_r| ||x||_1) and of this arithmetic. Rows with a non-finite entry get b_r = inf
+// (always recomputed exactly).
+__global__ void k_prep_lm_q8(const __half* E, int V, int H, uint8_t* q8, float* scale, float* bound) {
+  const int lane = threadIdx.x & 31, wpb = blockDim.x / 32;
+  const float gamma = (float)(H + 2) * 5.9604645e-08f * 1.01f;
+  for (long long r = (long long)blockIdx.x * wpb + (threadIdx.x >> 5); r < V; r += (long long)gridDim.x * wpb) {
+    const __half* row = E + r * H;
+    float m = 0.0f;
+    bool fin = true;
+    for (int j = lane; j < H; j += 32) {
+      const float v = __half2float(row[j]);
+      fin = fin && isfinite(v);
+      m = fmaxf(m, fabsf(v));
+    }
+    m = warp_max(m);
+    fin = __all_sync(0xffffffffu, fin);
+    const float sc = (fin && m > 0.0f) ? m / 127.0f : 0.0f;
+    const float inv = sc > 0.0f ? 127.0f / m : 0.0f;
+    float err = 0.0f;
+    for (int j = lane; j < H; j += 32) {
+      const float v = __half2float(row[j]);
+      const float q = fminf(fmaxf(rintf(v * inv), -127.0f), 127.0f);
+      q8[r * H + j] = (uint8_t)(int)(q + 128.0f);
+      if (fin) err = fmaxf(err, fabsf(v - sc * q));
+    }
+    err = warp_max(err);
+    if (lane == 0) {
+      scale[r] = sc;
+      bound[r] = fin ? (err + m * (2.1f * gamma + 4.8e-7f)) * (1.0f + 3.0f * gamma) : INFINITY;
+    }
+  }
+}
+
+// The final hidden state from the persistent kernel's exchange words (value bits in the low half).
+__global__ void k_words_to_f32(const unsigned long long* w, float* h, int n) {
+  pdl_wait();
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) h[i] = __uint_as_float((uint32_t)w[i]);
+  pdl_trigger();
 }
 
 // Decide whether the persistent kernel fits this shape and device; set it up if so.
@@ -385,6 +434,16 @@ void setup_persist(qd_engine* e) {
   if (cudaMalloc(&e->d_players, sizeof(PLayer) * p.layers) != cudaSuccess)
     throw QdError{QD_E_NOMEM, "cannot allocate the layer table"};
   QD_CK(cudaMemcpy(e->d_players, pl.data(), sizeof(PLayer) * p.layers, cudaMemcpyHostToDevice));
+  // the int8 LM head table of the argmax-only head
+  {
+    const size_t tb = (size_t)p.vocab * H;
+    if (cudaMalloc(&e->lm_q8, tb) != cudaSuccess || cudaMalloc(&e->lm_scale, (size_t)p.vocab * 4) != cudaSuccess ||
+        cudaMalloc(&e->lm_bound, (size_t)p.vocab * 4) != cudaSuccess)
+      throw QdError{QD_E_NOMEM, "cannot allocate the int8 LM head table"};
+    k_prep_lm_q8<<<4 * e->sms, 256, 0, e->stream>>>(e->embed, p.vocab, H, e->lm_q8, e->lm_scale, e->lm_bound);
+    QD_CK(cudaGetLastError());
+    QD_CK(cudaStreamSynchronize(e->stream));
+  }
   if (e->opt.timeline) {
     const size_t tb = (size_t)e->sms * timeline_events(p.layers) * 8;
     if (cudaMalloc(&e->timeline, tb) != cudaSuccess) throw QdError{QD_E_NOMEM, "cannot allocate the timeline"};
@@ -477,25 +536,25 @@ void launch_cluster(qd_engine* e, bool with_head, cudaStream_t s) {
   }
 }
 
-void enqueue_token(qd_engine* e, bool with_head, cudaStream_t s) {
+void enqueue_token(qd_engine* e, int head, cudaStream_t s) {
   if (e->clus) {
-    launch_cluster(e, with_head, s);
+    launch_cluster(e, head != kHeadNone, s);
     return;
   }
   if (e->persist) {
-    launch_persist(e, with_head, s);
+    launch_persist(e, head, s);
     return;
   }
   for (int l = 0; l < e->p.layers; ++l) enqueue_layer(e, l, s);
-  if (with_head) enqueue_lmhead(e, s);
+  if (head != kHeadNone) enqueue_lmhead(e, s);
   else launch(k_advance, dim3(1), s, e->st);
 }
 
-cudaGraphExec_t capture(qd_engine* e, bool with_head) {
+cudaGraphExec_t capture(qd_engine* e, int head) {
   cudaGraph_t g = nullptr;
   QD_CK(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal));
   try {
-    enqueue_token(e, with_head, e->stream);
+    enqueue_token(e, head, e->stream);
   } catch (...) {
     cudaStreamEndCapture(e->stream, &g);
     if (g) cudaGraphDestroy(g);
@@ -509,9 +568,17 @@ cudaGraphExec_t capture(qd_engine* e, bool with_head) {
   return ex;
 }
 
-void run_token(qd_engine* e, bool with_head) {
-  if (e->opt.use_graph) QD_CK(cudaGraphLaunch(with_head ? e->g_full : e->g_layers, e->stream));
-  else enqueue_token(e, with_head, e->stream);
+// One token: kHeadNone (layers only), kHeadFull (logits + argmax) or kHeadArgmax
+// (the argmax only, where the persistent kernel prunes the LM head; the logits are
+// then recomputed from the final hidden state if asked for).
+void run_token(qd_engine* e, int head) {
+  if (e->opt.use_graph) {
+    cudaGraphExec_t g = head == kHeadNone ? e->g_layers : head == kHeadFull ? e->g_full : e->g_argmax;
+    QD_CK(cudaGraphLaunch(g, e->stream));
+  } else {
+    enqueue_token(e, head, e->stream);
+  }
+  if (head != kHeadNone) e->logits_stale = head == kHeadArgmax && e->persist && e->lm_q8;
 }
 
 int dims_of(const Json& entry, size_t i) { return (int)entry.at("dims").at(i).as_int(); }
@@ -910,8 +977,9 @@ void load_engine(qd_engine* e, const std::string& dir, const Json& m) {
   QD_CK(cudaEventCreateWithFlags(&e->ev[0], cudaEventDisableTiming));
   QD_CK(cudaEventCreateWithFlags(&e->ev[1], cudaEventDisableTiming));
   if (o.use_graph) {
-    e->g_layers = capture(e, false);
-    e->g_full = capture(e, true);
+    e->g_layers = capture(e, kHeadNone);
+    e->g_full = capture(e, kHeadFull);
+    e->g_argmax = capture(e, kHeadArgmax);
   }
   QD_CK(cudaStreamSynchronize(e->stream));
 }
@@ -926,6 +994,10 @@ void free_engine(qd_engine* e) {
   if (e->stream) cudaStreamSynchronize(e->stream);
   if (e->g_layers) cudaGraphExecDestroy(e->g_layers);
   if (e->g_full) cudaGraphExecDestroy(e->g_full);
+  if (e->g_argmax) cudaGraphExecDestroy(e->g_argmax);
+  if (e->lm_q8) cudaFree(e->lm_q8);
+  if (e->lm_scale) cudaFree(e->lm_scale);
+  if (e->lm_bound) cudaFree(e->lm_bound);
   for (auto& ev : e->ev)
     if (ev) cudaEventDestroy(ev);
   if (e->blob) cudaFree(e->blob);
@@ -1179,12 +1251,12 @@ int generate(qd_engine* e, const int32_t* input_ids, int n_prompt, int max_new_t
     QD_CK(cudaMemcpyAsync(e->tokens, e->pinned_ids, (size_t)n_prompt * 4, cudaMemcpyHostToDevice, e->stream));
     set_state(e, 0, max_new_tokens);
     const int n_layers_only = max_new_tokens > 0 ? n_prompt - 1 : n_prompt;
-    for (int i = 0; i < n_layers_only; ++i) run_token(e, false);
+    for (int i = 0; i < n_layers_only; ++i) run_token(e, kHeadNone);
     double first_ms = 0.0;
     int produced = 0;
     bool stop = false;
     for (int step = 0; step < max_new_tokens && !stop; ++step) {
-      run_token(e, true);
+      run_token(e, sample ? kHeadFull : kHeadArgmax);  // the sampler reads the logits
       if (sample) enqueue_engine_sample(e, *sampling);
       QD_CK(cudaEventRecord(e->ev[step & 1], e->stream));
       if (step > 0) {  // deliver the previous token while this one runs
@@ -1238,6 +1310,17 @@ int qd_engine_logits(qd_engine* e, float* host_logits) {
   if (!e || !host_logits) return fail(e, QdError{QD_E_INVALID, "NULL argument"});
   try {
     QD_CK(cudaSetDevice(e->dev));
+    if (e->logits_stale) {  // the last token computed the argmax only: logits from its final hidden state
+      launch(k_words_to_f32, dim3((e->p.hidden + kThreads - 1) / kThreads), e->stream,
+             (const unsigned long long*)(e->xbuf + (long long)e->p.layers * e->xstride), e->h, e->p.hidden);
+      LmArgs a{};
+      a.h = e->h; a.norm_w = e->final_norm; a.eps = e->p.eps;
+      a.table = reinterpret_cast<const uint4*>(e->embed); a.vocab = e->p.vocab; a.H = e->p.hidden;
+      a.logits = e->logits; a.part_v = e->lm_pv; a.part_i = e->lm_pi; a.counter = e->lm_counter;
+      a.result = e->result;  // no token state: st stays null
+      launch_lmhead(a, e->lm_grid, e->stream);
+      e->logits_stale = false;
+    }
     QD_CK(cudaMemcpyAsync(host_logits, e->logits, (size_t)e->p.vocab * 4, cudaMemcpyDeviceToHost, e->stream));
     QD_CK(cudaStreamSynchronize(e->stream));
   } catch (const QdError& err) {
@@ -1316,7 +1399,7 @@ int qd_decode_begin(qd_engine* e, const int32_t* input_ids, int n_prompt, int ma
     QD_CK(cudaMemcpyAsync(e->tokens, e->pinned_ids, (size_t)n_prompt * 4, cudaMemcpyHostToDevice, e->stream));
     set_state(e, 0, max_new_tokens);
     e->stepping_max_new = max_new_tokens;
-    for (int i = 0; i < n_prompt - 1; ++i) run_token(e, false);
+    for (int i = 0; i < n_prompt - 1; ++i) run_token(e, kHeadNone);
   } catch (const QdError& err) {
     return fail(e, err);
   }
@@ -1326,7 +1409,7 @@ int qd_decode_begin(qd_engine* e, const int32_t* input_ids, int n_prompt, int ma
 int qd_decode_step(qd_engine* e) {
   if (!e) return fail(nullptr, QdError{QD_E_INVALID, "engine is NULL"});
   try {
-    run_token(e, true);
+    run_token(e, kHeadArgmax);
   } catch (const QdError& err) {
     return fail(e, err);
   }

@@ -87,6 +87,8 @@ void set_thread_error(const std::string& msg);
 // tcgen05 GEMM launch (gemm_tc.cuh): q4 weights with split-K partial outputs,
 // or the f16 LM head with the per-CTA (max, index) epilogue.
 enum GemmMode : int { kGemmQ4Store = 0, kGemmF16Argmax = 1, kGemmQ4Silu = 2 };
+// What a decode token launch computes after its layers.
+enum HeadMode : int { kHeadNone = 0, kHeadFull = 1, kHeadArgmax = 2 };
 struct TcArgs;
 void launch_gemm(TcArgs a, int splits, int mode, cudaStream_t s);
 // Splits actually used for K columns when `want` are asked for (no empty split).
@@ -151,7 +153,11 @@ struct qd_engine {
   unsigned* lm_counter = nullptr;
   int32_t* pinned_ids = nullptr;
   qd::DevState* pinned_state = nullptr;
-  cudaGraphExec_t g_layers = nullptr, g_full = nullptr;
+  cudaGraphExec_t g_layers = nullptr, g_full = nullptr, g_argmax = nullptr;
+  bool logits_stale = false;               // the last token launch computed the argmax only
+  // argmax-only LM head of the persistent kernel: the table as int8 + per-row scale / bound
+  uint8_t* lm_q8 = nullptr;
+  float *lm_scale = nullptr, *lm_bound = nullptr;
   cudaEvent_t ev[2] = {nullptr, nullptr};
   // persistent decode kernel
   bool persist = false;

@@ -91,7 +91,14 @@ struct PArgs {
   long long rec_og, oslice_rows;           // O slice row record bytes (K = G*128), rows per slice (max)
   unsigned long long* oacc;                // [2 parities][L][O | down][H] counted fixed-point sums
   int n_mlp;                               // CTAs that own intermediate columns (contributors to the down sums)
+  // argmax-only LM head (pruned = 1): the table as int8 (q + 128, per-row scale) and a
+  // per-row bound coefficient: |f16 logit - int8 logit| <= lm_bound[r] * ||x||_1
+  int pruned;
+  const uint2* lm_q8;                      // [vocab][H / 8]
+  const float *lm_scale, *lm_bound;        // [vocab]
 };
+constexpr int kLmCand = 64;                // candidate rows per warp of the pruned head
+constexpr int kLmRows = 16;                // int8 rows per ring chunk of the pruned head (4 warps x 4)
 
 // ---- small PTX helpers --------------------------------------------------------
 __device__ __forceinline__ unsigned smem_u32(const void* p) {
@@ -960,35 +967,34 @@ __global__ void __launch_bounds__(kPT, 1) k_decode_persistent(const __grid_const
   uint32_t bi = 0;
   if (a.with_head) {
     // This warp streams rows v_lo + (i*kPW + warp)*4 + k (k < 4): 4 rows at once,
-    // lane holding uint4 c*32 + lane of each row. The first batch is loaded
-    // before waiting for the final hidden state.
+    // lane holding chunk c*32 + lane (columns 8 (c*32 + lane) .. +7) of each row. The
+    // first batch is loaded before waiting for the final hidden state.
     const int kc8 = H / 256;
     const int n_rows = rg.v_hi - rg.v_lo;
     const uint4* tab = reinterpret_cast<const uint4*>(a.embed);
     const int rpr = H / 8;
-    uint4 cur[4][4];
     int i0 = warp * 4;
-    auto load_batch = [&](int first) {
+    auto load_batch = [&](uint4 (&dst)[4][4], int first) {
 #pragma unroll
       for (int k = 0; k < 4; ++k)
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           const int rr = first + k;
-          cur[k][c] = (c < kc8 && rr < n_rows) ? ld_stream(tab + (long long)(rg.v_lo + rr) * rpr + c * 32 + lane)
+          dst[k][c] = (c < kc8 && rr < n_rows) ? ld_stream(tab + (long long)(rg.v_lo + rr) * rpr + c * 32 + lane)
                                                : make_uint4(0u, 0u, 0u, 0u);
         }
     };
-    load_batch(i0);
-    float fw[2];
+    // The final hidden state, its RMSNorm into plain staging and this lane's columns
+    // (c*32+lane)*8 .. +7 of it; false on timeout/abort.
+    auto normed_x = [&](float2 (&xr)[4][4]) -> bool {
+      float fw[2];
 #pragma unroll
-    for (int k = 0; k < 2; ++k) fw[k] = threadIdx.x + k * kPT < H ? a.final_norm[threadIdx.x + k * kPT] : 0.0f;
-    if (!stage_ok(a, final_hidden(a, rg, epoch, H, S))) return;
-    float fv[2];
+      for (int k = 0; k < 2; ++k) fw[k] = threadIdx.x + k * kPT < H ? a.final_norm[threadIdx.x + k * kPT] : 0.0f;
+      if (!stage_ok(a, final_hidden(a, rg, epoch, H, S))) return false;
+      float fv[2];
 #pragma unroll
-    for (int k = 0; k < 2; ++k) fv[k] = threadIdx.x + k * kPT < H ? S.hs[threadIdx.x + k * kPT] : 0.0f;
-    stamp(tl, 1 + kTimelinePerLayer * a.L);
-    // final RMSNorm into plain staging; lane holds columns (c*32+lane)*8 .. +7
-    {
+      for (int k = 0; k < 2; ++k) fv[k] = threadIdx.x + k * kPT < H ? S.hs[threadIdx.x + k * kPT] : 0.0f;
+      stamp(tl, 1 + kTimelinePerLayer * a.L);
       float ss = 0.0f;
 #pragma unroll
       for (int k = 0; k < 2; ++k)
@@ -1004,38 +1010,207 @@ __global__ void __launch_bounds__(kPT, 1) k_decode_persistent(const __grid_const
       for (int k = 0; k < 2; ++k)
         if (threadIdx.x + k * kPT < H) S.xs[threadIdx.x + k * kPT] = fv[k] * inv * fw[k];
       __syncthreads();
-    }
-    float2 xr[4][4];
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      if (c < kc8) {
-        const float4* p = reinterpret_cast<const float4*>(S.xs + (c * 32 + lane) * 8);
-        const float4 v0 = p[0], v1 = p[1];
-        xr[c][0] = make_float2(v0.x, v0.y);
-        xr[c][1] = make_float2(v0.z, v0.w);
-        xr[c][2] = make_float2(v1.x, v1.y);
-        xr[c][3] = make_float2(v1.z, v1.w);
-      } else {
+      for (int c = 0; c < 4; ++c) {
+        if (c < kc8) {
+          const float4* p = reinterpret_cast<const float4*>(S.xs + (c * 32 + lane) * 8);
+          const float4 v0 = p[0], v1 = p[1];
+          xr[c][0] = make_float2(v0.x, v0.y);
+          xr[c][1] = make_float2(v0.z, v0.w);
+          xr[c][2] = make_float2(v1.x, v1.y);
+          xr[c][3] = make_float2(v1.z, v1.w);
+        } else {
 #pragma unroll
-        for (int k = 0; k < 4; ++k) xr[c][k] = make_float2(0.f, 0.f);
+          for (int k = 0; k < 4; ++k) xr[c][k] = make_float2(0.f, 0.f);
+        }
       }
-    }
-    for (; i0 < n_rows; i0 += kPW * 4) {
+      return true;
+    };
+    // Exact f16 logits of 4 rows (row offsets rk[k] in this CTA's range, < 0: none);
+    // the same arithmetic for every row wherever it is computed.
+    auto exact4 = [&](const float2 (&xr)[4][4], const int (&rk)[4]) {
+      uint4 w[4][4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          w[k][c] = (c < kc8 && rk[k] >= 0) ? ld_stream(tab + (long long)(rg.v_lo + rk[k]) * rpr + c * 32 + lane)
+                                            : make_uint4(0u, 0u, 0u, 0u);
       float p[4];
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
         float2 acc = make_float2(0.f, 0.f);
 #pragma unroll
-        for (int c = 0; c < 4; ++c) acc = f16x8_dot(cur[k][c], xr[c], acc);
+        for (int c = 0; c < 4; ++c) acc = f16x8_dot(w[k][c], xr[c], acc);
         p[k] = acc.x + acc.y;
       }
-      if (i0 + kPW * 4 < n_rows) load_batch(i0 + kPW * 4);
       const float v = reduce4(p[0], p[1], p[2], p[3]);
-      const int rr = i0 + (lane >> 3);
-      if ((lane & 7) == 0 && rr < n_rows) {
+      const int m = lane >> 3, rr = m == 0 ? rk[0] : m == 1 ? rk[1] : m == 2 ? rk[2] : rk[3];
+      if ((lane & 7) == 0 && rr >= 0) {
         const int r = rg.v_lo + rr;
-        a.logits[r] = v;
         if (am_better(v, (uint32_t)r, bv, bi)) { bv = v; bi = (uint32_t)r; }
+      }
+    };
+    if (!a.pruned) {
+      uint4 cur[4][4];
+      load_batch(cur, i0);
+      float2 xr[4][4];
+      if (!normed_x(xr)) return;
+      for (; i0 < n_rows; i0 += kPW * 4) {
+        float p[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          float2 acc = make_float2(0.f, 0.f);
+#pragma unroll
+          for (int c = 0; c < 4; ++c) acc = f16x8_dot(cur[k][c], xr[c], acc);
+          p[k] = acc.x + acc.y;
+        }
+        if (i0 + kPW * 4 < n_rows) load_batch(cur, i0 + kPW * 4);
+        const float v = reduce4(p[0], p[1], p[2], p[3]);
+        const int rr = i0 + (lane >> 3);
+        if ((lane & 7) == 0 && rr < n_rows) {
+          const int r = rg.v_lo + rr;
+          a.logits[r] = v;
+          if (am_better(v, (uint32_t)r, bv, bi)) { bv = v; bi = (uint32_t)r; }
+        }
+      }
+    } else {
+      // The int8 rows stream through the (now idle) weight ring by bulk copies: chunk j
+      // = rows [16 j, 16 j + 16) goes to ring index n_chunks + j; warp group g (warps
+      // 4g .. 4g+3) takes chunks g, g + 4, ... (its two slots) and refills each slot
+      // with the chunk 8 ahead once its four warps are done with it.
+      const int n_lc = (n_rows + kLmRows - 1) / kLmRows;
+      auto lc_issue = [&](int j) {
+        const int gi = n_chunks + j, slot = gi % kSlots;
+        const int rows = min(kLmRows, n_rows - j * kLmRows);
+        const unsigned bytes = (unsigned)(rows * H);
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        mbar_arrive_tx(&S.mbar[slot], bytes);
+        bulk_load_hint(S.ring + slot * kSlotBytes, reinterpret_cast<const char*>(a.lm_q8) + (long long)(rg.v_lo + j * kLmRows) * H,
+                       bytes, &S.mbar[slot], policy_evict_first());
+      };
+      // bounded wait for chunk j (ignoring the abort flag: these are this CTA's own copies)
+      auto lc_wait = [&](int j) -> bool {
+        const int gi = n_chunks + j;
+        const unsigned parity = (unsigned)(gi / kSlots) & 1u;
+        const unsigned long long t0 = gtimer();
+        while (!mbar_test(&S.mbar[gi % kSlots], parity))
+          if (gtimer() - t0 > kWaitNs) return false;
+        return true;
+      };
+      if (threadIdx.x == 0)
+        for (int j = 0; j < min(kSlots, n_lc); ++j) lc_issue(j);
+      float2 xr[4][4];
+      if (!normed_x(xr)) {
+        for (int j = 0; j < min(kSlots, n_lc); ++j) (void)lc_wait(j);
+        return;
+      }
+      // Argmax only. (1) Coarse logits from the int8 table, each within
+      // lm_bound[r] * ||x||_1 (+ a rounding margin) of the row's f16 logit; the
+      // warps keep the rows whose upper bound reaches the best lower bound seen so
+      // far. (2) The rows whose upper bound reaches the CTA's best lower bound get
+      // their exact f16 logits; no other row of the CTA can be its argmax (its
+      // logit is below that of the row holding the best lower bound), so the
+      // result is the full head's, ties and NaN rules included. A warp whose list
+      // overflows, or a non-finite ||x||_1, takes the exact path for all its rows.
+      // per-warp scalars in the misc area; the candidate lists in the activation
+      // staging, which is free once ||x||_1 is summed (the ring carries the int8 rows)
+      int* cnt = reinterpret_cast<int*>(S.misc);                  // [kPW]
+      float* wlb = S.misc + kPW;                                  // [kPW]
+      float* l1s = S.misc + 2 * kPW;                              // [kPW]
+      int2* cand = reinterpret_cast<int2*>(S.xs);                 // [kPW][kLmCand] (row offset, ub bits)
+      static_assert(kPW * kLmCand * 2 <= kPW * kHeadDim, "the lists fit the staging area (at least kPW * 128 floats)");
+      float l1 = 0.0f;
+#pragma unroll
+      for (int k = 0; k < 2; ++k)
+        if (threadIdx.x + k * kPT < H) l1 += fabsf(S.xs[threadIdx.x + k * kPT]);
+      l1 = warp_sum(l1);
+      if (lane == 0) {
+        l1s[warp] = l1;
+        cnt[warp] = 0;
+      }
+      __syncthreads();
+      float L1 = 0.0f;
+#pragma unroll
+      for (int k = 0; k < kPW; ++k) L1 += l1s[k];
+      const bool bounded = isfinite(L1);  // the same in every CTA
+      float lane_lb = -INFINITY;
+      // 4 rows of a landed chunk (rows `first` .. +3 of the CTA's range, chunk row
+      // offset `local`): coarse logits, bounds, candidates
+      auto coarse4 = [&](const char* chunk, int local, int first) {
+          float p[4];
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const char* row = chunk + (local + k) * H;
+            float2 acc = make_float2(0.f, 0.f);
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              const uint2 w = (c < kc8 && first + k < n_rows) ? reinterpret_cast<const uint2*>(row)[c * 32 + lane]
+                                                              : make_uint2(0x80808080u, 0x80808080u);
+              acc = q8x8_dot(w, xr[c], acc);
+            }
+            p[k] = acc.x + acc.y;
+          }
+          const float t = reduce4(p[0], p[1], p[2], p[3]);
+          const int rr = first + (lane >> 3);
+          if ((lane & 7) == 0 && rr < n_rows) {
+            const int r = rg.v_lo + rr;
+            const float coarse = a.lm_scale[r] * t;
+            const float bnd = fmaf(fabsf(coarse), 1e-6f, a.lm_bound[r] * L1);
+            const float lb = coarse - bnd, ub = coarse + bnd;
+            if (lb > lane_lb) lane_lb = lb;
+            if (!(ub < lane_lb)) {  // NaN bounds stay candidates
+              const int slot = atomicAdd(&cnt[warp], 1);
+              if (slot < kLmCand) cand[warp * kLmCand + slot] = make_int2(rr, __float_as_int(ub));
+            }
+          }
+      };
+      {
+        const int g = warp >> 2, wq = warp & 3;
+        bool lc_ok = true;
+        for (int j = g; j < n_lc; j += 4) {
+          lc_ok = lc_wait(j) && lc_ok;
+          if (bounded) coarse4(S.ring + ((n_chunks + j) % kSlots) * kSlotBytes, wq * 4, j * kLmRows + wq * 4);
+          asm volatile("bar.sync %0, %1;" ::"r"(1 + g), "r"(128) : "memory");  // the group is done with the slot
+          if ((threadIdx.x & 127) == 0 && j + kSlots < n_lc) lc_issue(j + kSlots);
+        }
+        if (!lc_ok) {  // a copy never landed: the token is void (QD_E_TIMEOUT)
+          raise_abort(a);
+          // wait once more for the group's last chunk in each of its two slots (only
+          // those can still be in flight; older phases of a slot are not waited on again)
+          const int last = g + (n_lc - 1 - g) / 4 * 4;
+          if (last >= g) (void)lc_wait(last);
+          if (last - 4 >= g) (void)lc_wait(last - 4);
+        }
+      }
+      const float wmax = warp_max(lane_lb);
+      if (lane == 0) wlb[warp] = wmax;
+      __syncthreads();
+      float LB = -INFINITY;
+#pragma unroll
+      for (int k = 0; k < kPW; ++k) LB = fmaxf(LB, wlb[k]);
+      const int nc = cnt[warp];
+      if (!bounded || nc > kLmCand) {
+        for (int j0 = warp * 4; j0 < n_rows; j0 += kPW * 4) {
+          int rk[4];
+#pragma unroll
+          for (int k = 0; k < 4; ++k) rk[k] = j0 + k < n_rows ? j0 + k : -1;
+          exact4(xr, rk);
+        }
+      } else {
+        // this warp's candidates that reach the CTA's best lower bound, 4 at a time
+        int j = 0;
+        while (true) {
+          int rk[4];
+          int got = 0;
+          for (; j < nc && got < 4; ++j) {
+            const int2 e = cand[warp * kLmCand + j];
+            if (!(__int_as_float(e.y) < LB)) rk[got++] = e.x;
+          }
+          if (got == 0) break;
+          for (int k = got; k < 4; ++k) rk[k] = -1;
+          exact4(xr, rk);
+        }
       }
     }
     // warp argmax (total order: larger value, then lower index)

@@ -393,3 +393,37 @@ def test_engine_rope_row_stride_option(tiny_runtime, tiny_model, persistent):
     # the option changes the math: the default stride gives other logits
     _, default_logits, _ = _oracle_step_logits(tiny_model, prompt, 8, max_seq=64, kv_f16=True)
     assert any(rel(a, b) > 1e-3 for a, b in zip(want_logits, default_logits))
+
+
+# ---- the argmax-only LM head (int8 coarse pass + exact recompute of candidates) ------
+
+def test_argmax_head_ties_and_nan_rows(tiny_runtime, tmp_path):
+    """Every embedding row present twice (exact ties at every logit) plus NaN rows: the
+    argmax-only head picks the lower index of the best pair and never a NaN row, the
+    same ids as the oracle and as the full head (greedy through the sampler); the logits
+    asked for afterwards are the oracle's."""
+    import shutil
+    d = str(tmp_path / "ties")
+    shutil.copytree(tiny_runtime, d)
+    path = os.path.join(d, "shared", "embed_tokens.f16")
+    s = synth.TINY
+    emb = np.fromfile(path, dtype=np.float16).reshape(s.vocab, s.hidden)
+    half = s.vocab // 2
+    emb[half:2 * half] = emb[:half]
+    emb[[7, 7 + half, s.vocab - 1]] = np.nan
+    emb.tofile(path)
+    prompt = [5, 77, 1000, 3]
+    sess = O.Model(d).session(max_seq=64, kv_f16=True)
+    want, margins = sess.greedy(prompt, 12)
+    _, want_logits, _ = sess.next_token()
+    with R.Engine(d, max_seq=64, persistent=1) as eng:
+        assert eng.token_kernel == 1
+        ids, _ = eng.generate_greedy(prompt, 12)
+        logits = eng.logits()
+        full, _ = eng.generate_sample(prompt, 12, temperature=1.0, top_k=1)
+    assert ids == want, (ids, want, margins)
+    assert full == want
+    assert all(i < half and i != 7 for i in ids)
+    nan = np.isnan(want_logits)
+    assert np.array_equal(np.isnan(logits), nan)
+    assert rel(logits[~nan], want_logits[~nan]) < TOL
