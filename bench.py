@@ -124,32 +124,41 @@ class ClockSampler:
 
     def __init__(self, index: int):
         self.index, self.rows, self.proc = index, [], None
+        self.t0 = self.t1 = None
 
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
-                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
+            # the sampler is running before the timed region starts (its first row takes ~0.1-0.3 s)
+            deadline = time.monotonic() + 5.0
+            while not self.rows and time.monotonic() < deadline:
+                time.sleep(0.01)
         except (OSError, FileNotFoundError):
             self.proc = None
+        self.t0 = time.monotonic()
         return self
 
     def _read(self):
         for line in self.proc.stdout:
             parts = [p.strip() for p in line.split(",")]
             if len(parts) >= 9:
-                self.rows.append(parts)
+                self.rows.append((time.monotonic(), parts))
 
     def __exit__(self, *exc):
+        self.t1 = time.monotonic()
         if self.proc:
-            time.sleep(0.25)
+            time.sleep(0.06)
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
+        # the rows read inside the timed region (plus one sampling interval of delivery lag)
+        self.rows = [r for t, r in self.rows if self.t0 <= t <= self.t1 + 0.05]
 
     def summary(self):
         if not self.rows:
@@ -771,7 +780,7 @@ def time_cpu_prefill(rt, ids, n_tokens=256):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=None, help="timed steps (b1: 480, b64: 128)")
+    ap.add_argument("--steps", type=int, default=None, help="timed steps (b1: 1000, b64: 128)")
     ap.add_argument("--warmup", type=int, default=None, help="untimed steps (b1: 24, b64: 3)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-steps", type=int, default=24)
@@ -786,7 +795,7 @@ def main():
                     help="prefill + warm-up + timed decode steps only (for profiler launch lists)")
     args = ap.parse_args()
     if args.steps is None:
-        args.steps = {"b64": 128, "prefill": 10}.get(args.workload, 480)
+        args.steps = {"b64": 128, "prefill": 10}.get(args.workload, 1000)
     if args.warmup is None:
         args.warmup = 24 if args.workload == "b1" else 3
     world, rank, local = dist_setup()
