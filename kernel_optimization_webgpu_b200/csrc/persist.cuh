@@ -721,36 +721,45 @@ __device__ __forceinline__ bool attn_o_stage(const PArgs& a, const PShared& S, c
   return true;
 }
 
-// This CTA's partial of the down projection: rows r = tid, tid + kPT (< H) over its n
-// intermediate columns (act[0..kDMaxCols), shared memory, zero past n; 16-byte
-// aligned; the first `split` columns lie in
-// the scale of the record's first block, the rest in the second), added to the
-// counted sums acc[r]. Nibbles become floats through the 2^23 + n bit pattern.
-__device__ __forceinline__ void down_partial(const PArgs& a, const char* slot, int n, int split, const float* act,
+// This CTA's partial of the down projection: rows r = tid, tid + kPT (< H) over its
+// intermediate columns, added to the counted sums acc[r]. act[0, kDMaxCols) holds the
+// activations of the columns in the record's first q4 block (zero elsewhere) and
+// act[kDMaxCols, 2 kDMaxCols) those in its second (shared memory, 16-byte aligned),
+// so both scale segments accumulate without per-column selects. The nibbles become
+// floats two at a time through the 2^23 + n bit pattern (one packed subtract).
+__device__ __forceinline__ void down_partial(const PArgs& a, const char* slot, const float* act,
                                              unsigned long long* acc, int H) {
+  static_assert(kDMaxCols == 24, "three words of eight nibbles per record");
+  const float4* xa4 = reinterpret_cast<const float4*>(act);
+  const float4* xb4 = reinterpret_cast<const float4*>(act + kDMaxCols);
+  const float2 bias = make_float2(-8388616.0f, -8388616.0f);
 #pragma unroll 1
   for (int k = 0; k < 2; ++k) {
     const int r = threadIdx.x + k * kPT;
     if (r >= H) break;
     const uint4 rec = reinterpret_cast<const uint4*>(slot)[r];
     const uint32_t w[3] = {rec.x, rec.y, rec.z};
-    float pa = 0.0f, pb = 0.0f;
+    float2 pa = make_float2(0.0f, 0.0f), pb = pa;
 #pragma unroll
-    for (int q = 0; q < kDMaxCols / 4; ++q) {
-      const float4 x4 = reinterpret_cast<const float4*>(act)[q];  // same address in every lane
-      const float x[4] = {x4.x, x4.y, x4.z, x4.w};
+    for (int q = 0; q < 3; ++q) {  // word q: columns 8q .. 8q + 7 (nibble i = column 8q + i)
+      const uint32_t lo = w[q] & 0x0F0F0F0Fu, hi = (w[q] >> 4) & 0x0F0F0F0Fu;  // even / odd columns
+      const float4 a0 = xa4[2 * q], a1 = xa4[2 * q + 1], b0 = xb4[2 * q], b1 = xb4[2 * q + 1];  // broadcast
+      const float2 xa[4] = {make_float2(a0.x, a0.y), make_float2(a0.z, a0.w), make_float2(a1.x, a1.y),
+                            make_float2(a1.z, a1.w)};
+      const float2 xb[4] = {make_float2(b0.x, b0.y), make_float2(b0.z, b0.w), make_float2(b1.x, b1.y),
+                            make_float2(b1.z, b1.w)};
 #pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        const int j = 4 * q + t;
-        const uint32_t nib = (w[j >> 3] >> (4 * (j & 7))) & 15u;
-        const float v = __int_as_float(0x4B000000 | (int)nib) - 8388616.0f;  // nib - 8
-        if (j < split) pa = fmaf(v, x[t], pa);
-        else pb = fmaf(v, x[t], pb);
+      for (int m = 0; m < 4; ++m) {  // columns 8q + 2m, 8q + 2m + 1
+        const float2 v = __fadd2_rn(make_float2(__int_as_float(__byte_perm(lo, 0x4B000000u, 0x7540u + m)),
+                                                __int_as_float(__byte_perm(hi, 0x4B000000u, 0x7540u + m))),
+                                    bias);
+        pa = __ffma2_rn(v, xa[m], pa);
+        pb = __ffma2_rn(v, xb[m], pb);
       }
     }
     const float sa = __half2float(__ushort_as_half((unsigned short)(rec.w & 0xFFFFu)));
     const float sb = __half2float(__ushort_as_half((unsigned short)(rec.w >> 16)));
-    red_fx(a, acc + r, sa * pa + sb * pb);
+    red_fx(a, acc + r, sa * (pa.x + pa.y) + sb * (pb.x + pb.y));
   }
 }
 
@@ -934,24 +943,27 @@ __global__ void __launch_bounds__(kPT, 1) k_decode_persistent(const __grid_const
       // The gate/up weights are consumed: the last thread (no activation to write) refills the slot.
       if (threadIdx.x == kPT - 1) issue_chunk(a, S, rg, chunk + kSlots, n_chunks);
       ++chunk;
-      float* act = S.res + kMaxRes / 2;  // this CTA's activations
-      if (threadIdx.x < kDMaxCols) {  // zero past n: the down partial reads all kDMaxCols
+      // this CTA's activations, split by the q4 block of the down record they fall in:
+      // act[j] for the first block's columns, act[kDMaxCols + j] for the second's (zero past n)
+      float* act = S.res + kMaxRes / 2;
+      static_assert(kMaxRes / 2 + 2 * kDMaxCols <= kMaxRes, "both halves fit the result buffer");
+      if (threadIdx.x < kDMaxCols) {
         float v = 0.0f;
         if (threadIdx.x < n) {
           const float inv = rms_inv(S.red, H, a.eps);
           const float gt = S.res[2 * threadIdx.x] * inv, upv = S.res[2 * threadIdx.x + 1] * inv;
           v = (gt / (1.0f + expf(-gt))) * upv;
         }
-        act[threadIdx.x] = v;
+        const bool first = (int)threadIdx.x < kBlockCols - rg.i_lo % kBlockCols;
+        act[threadIdx.x] = first ? v : 0.0f;
+        act[kDMaxCols + threadIdx.x] = first ? 0.0f : v;
       }
       stamp(tl, ev + 7);
       // the down slice's wait ends in a barrier, which also publishes the activations
       QD_FAIL_IF(!stage_ok(a, wait_chunk(a, S, chunk)));
       stamp(tl, ev + 8);
       stamp(tl, ev + 13);
-      if (n > 0)
-        down_partial(a, S.ring + (chunk % kSlots) * kSlotBytes, n, min(n, kBlockCols - rg.i_lo % kBlockCols), act,
-                     acc_d, H);
+      if (n > 0) down_partial(a, S.ring + (chunk % kSlots) * kSlotBytes, act, acc_d, H);
       __syncthreads();
       stamp(tl, ev + 9);
       if (threadIdx.x == 0) issue_chunk(a, S, rg, chunk + kSlots, n_chunks);
