@@ -37,11 +37,11 @@ from kernel_optimization_webgpu_b200 import synth  # noqa: E402
 
 PROMPT_LEN, NEW_TOKENS = 8, 24
 # DRAM bytes (read + write) of one k_decode_persistent token launch, measured by ncu
-# on the default workload (428.75 MB read + 4.65 MB written): the layers' weights (the
+# on the default workload (428.79 MB read + 4.31 MB written): the layers' weights (the
 # packed O and down slices carry ~18 MB more than the row records they come from) and,
 # for a greedy token, the int8 copy of the LM head table (156 MB) in place of the f16
 # table (311 MB) plus the f16 rows of the few candidates.
-B1_TRAFFIC = 433397248
+B1_TRAFFIC = 433105408
 WORKLOAD = ("batch-1 greedy decode, Qwen3-0.6B shape (28 layers, hidden 1024, 16q/8kv heads x 128, "
             "SwiGLU 3072, q4 MatMulNBits block 32 with f16 scales, tied f16 LM head 151936x1024, f16 KV), "
             "8-token prompt + 24 generated, seed 2")
