@@ -360,7 +360,6 @@ def run_ours(args, world, rank, local):
     step_kernels = eng.step_kernels
     eng_kernel = eng.token_kernel
     token_kernel_desc = {
-        2: "decode token: k_decode_cluster, one launch per token (28 layers + LM head/argmax)",
         1: "decode token: k_decode_persistent, one launch per token (28 layers + LM head/argmax)",
     }.get(eng.token_kernel, f"decode token: one CUDA graph of {step_kernels} kernels (28 layers + LM head/argmax)")
     stream = torch.cuda.Stream()

@@ -54,12 +54,8 @@ typedef struct qd_options {
   int rope_row_stride;   /* cos/sin offset = position * stride + pair; 0 = head_dim (reference) */
   const char* variant;   /* "optimized" | "mixed" | "original": accepted, one B200 path */
   int use_graph;         /* 1 (default): each token is one CUDA graph launch */
-  int persistent;        /* 1 (default): one persistent kernel per token, one CTA per SM, where
-                            the shape allows;
-                            2: one launch per token on thread-block clusters of 8 CTAs (the
-                            q/k/v -> attention and gate/up -> down exchanges stay inside a
-                            cluster) where the shape and device allow, else as 1;
-                            0: one kernel per fused stage */
+  int persistent;        /* nonzero (default 1): one persistent kernel per token, one CTA per
+                            SM, where the shape allows; 0: one kernel per fused stage */
   int timeline;          /* 1: record per-CTA stage timestamps of each persistent launch */
 } qd_options;
 
@@ -127,25 +123,18 @@ int qd_sample_logits(const float* logits, uint32_t vocab, const qd_sampling* sam
 /* Parity and inspection helpers. */
 int qd_engine_logits(qd_engine* e, float* host_logits);       /* logits of the last generated step */
 int qd_engine_hidden(qd_engine* e, float* host_hidden);       /* residual stream after the last layer */
-/* Token kernel in use: 2 = cluster kernel, 1 = single-CTA-ring persistent kernel,
- * 0 = one kernel per stage. */
+/* Token kernel in use: 1 = the persistent kernel, 0 = one kernel per stage. */
 int qd_engine_uses_persistent(const qd_engine* e);
 /* Stage timestamps (ns, globaltimer) of the last persistent launch: host_out[cta][event]
- * (needs qd_options.timeline = 1). Pass host_out NULL to query the sizes.
- * Cluster kernel, per CTA: start; per layer 11 events (layer input ready, q/k/v weights
- * ready, q/k/v rows done, group rows exchanged, attention partial done, partials
- * exchanged, O partial added, O sums ready, gate/up done, activations exchanged, down
- * partial added; attention-only events stay 0 in the other clusters); LM-head input
- * ready, LM head done, merged (last CTA only).
- * Single-CTA-ring kernel, per CTA: start; per layer 14 events (QKV input ready, QKV
- * weights ready, QKV stored, attention done, O input ready, O stored, gate/up input
- * ready, gate/up stored, down input ready, down stored, QKV norm done, O weights ready,
- * gate/up norm done, down weights ready); LM-head input ready, LM head done, merged. */
+ * (needs qd_options.timeline = 1). Pass host_out NULL to query the sizes. Per CTA: start;
+ * per layer 19 events (0 layer input ready, 1 QKV weights ready, 2 QKV stored, 3 attention
+ * + O stage done, 4 h_attn ready, 5 attention softmax done, 6 gate/up stage start, 7
+ * gate/up done, 8 down weights ready, 9 down partial issued, 10 QKV input weighted, 11
+ * attention scores done, 12 gate/up input weighted, 13 down partial start, 14 q/k/v
+ * arrived, 15 head norm + RoPE done, 16 weighted sum done, 17 O weights ready, 18 O slice
+ * dots done; events 5, 11 and 14-18 only in the attention CTAs); LM-head input ready, LM
+ * head done, merged. */
 int qd_engine_timeline(qd_engine* e, uint64_t* host_out, int* ctas, int* events_per_cta);
-/* SM clock (clock64) stamps inside every layer of the last cluster-kernel launch:
- * host_out[cta][layer][event], events_per_layer per layer (needs qd_options.timeline = 1
- * and the cluster kernel). For stage-by-stage cycle counts within one CTA. */
-int qd_engine_timeline_fine(qd_engine* e, uint64_t* host_out, int* ctas, int* events_per_layer);
 /* One token through the layers at `position` (no LM head), with the residual
  * stream after every layer copied to host_trace[layers][hidden]. */
 int qd_engine_forward_trace(qd_engine* e, int32_t token, int position, float* host_trace);

@@ -25,7 +25,7 @@ QD_KV_F32 = 1
 EXPORTS = (
     "qd_options_default", "qd_engine_create", "qd_engine_destroy", "qd_last_error",
     "qd_engine_profile", "qd_generate_greedy", "qd_engine_logits", "qd_engine_hidden",
-    "qd_engine_forward_trace", "qd_engine_uses_persistent", "qd_engine_timeline", "qd_engine_timeline_fine",
+    "qd_engine_forward_trace", "qd_engine_uses_persistent", "qd_engine_timeline",
     "qd_q4_matvec",
     "qd_q4_gemm_workspace_bytes", "qd_q4_gemm", "qd_lm_head_argmax_workspace_bytes",
     "qd_lm_head_argmax", "qd_gqa_decode_workspace_bytes", "qd_gqa_decode",
@@ -127,8 +127,6 @@ def load(build_if_stale: bool = True):
     L.qd_engine_uses_persistent.restype = i32
     L.qd_engine_timeline.argtypes = [vp, vp, C.POINTER(C.c_int), C.POINTER(C.c_int)]
     L.qd_engine_timeline.restype = i32
-    L.qd_engine_timeline_fine.argtypes = [vp, vp, C.POINTER(C.c_int), C.POINTER(C.c_int)]
-    L.qd_engine_timeline_fine.restype = i32
     L.qd_engine_set_stream.argtypes = [vp, vp]
     L.qd_engine_set_stream.restype = i32
     L.qd_decode_begin.argtypes = [vp, vp, i32, i32]

@@ -15,7 +15,7 @@ ROOT = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
 LIB = os.path.join(PKG, "libqdecode.so")
 SOURCES = ["engine.cu", "batch.cu", "noalloc.cu", "bench_api.cu", "sample.cu"]
-DEPS = SOURCES + ["kernels.cuh", "persist.cuh", "cluster.cuh", "gemm_tc.cuh", "batch.cuh", "internal.cuh", "tma.cuh", "common.cuh", "json.hpp"]
+DEPS = SOURCES + ["kernels.cuh", "persist.cuh", "gemm_tc.cuh", "batch.cuh", "internal.cuh", "tma.cuh", "common.cuh", "json.hpp"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -18,7 +18,6 @@
 #include "internal.cuh"
 #include "kernels.cuh"
 #include "persist.cuh"
-#include "cluster.cuh"
 
 using namespace qd;
 
@@ -452,95 +451,7 @@ void setup_persist(qd_engine* e) {
   e->persist = true;
 }
 
-// Device tables and exchange buffers of the cluster kernel (after the weights are resident).
-void setup_cluster(qd_engine* e) {
-  if (!e->ncl || !e->cblob) return;
-  const qd_profile& p = e->p;
-  const int grid = e->ncl * kCC;
-  // norm table [L][input | post-attention | q head | k head], copied from the weight arena
-  const int ns = cnorm_stride(p.hidden);
-  const size_t acc_bytes = (size_t)2 * p.layers * 2 * p.hidden * 8, cnt_bytes = (size_t)2 * p.layers * 2 * 32 * 4;
-  if (cudaMalloc(&e->c_norms, sizeof(float) * ns * p.layers) != cudaSuccess ||
-      cudaMalloc(&e->c_d_cta_off, sizeof(long long) * grid) != cudaSuccess ||
-      cudaMalloc(&e->c_acc, acc_bytes) != cudaSuccess || cudaMalloc(&e->c_cnt, cnt_bytes) != cudaSuccess)
-    throw QdError{QD_E_NOMEM, "cannot allocate the cluster decode tables"};
-  for (int l = 0; l < p.layers; ++l) {
-    const LayerDev& L = e->layers[l];
-    float* d = e->c_norms + (size_t)l * ns;
-    QD_CK(cudaMemcpy(d, L.n_in, sizeof(float) * p.hidden, cudaMemcpyDeviceToDevice));
-    QD_CK(cudaMemcpy(d + p.hidden, L.n_post, sizeof(float) * p.hidden, cudaMemcpyDeviceToDevice));
-    QD_CK(cudaMemcpy(d + 2 * p.hidden, L.n_q, sizeof(float) * kHeadDim, cudaMemcpyDeviceToDevice));
-    QD_CK(cudaMemcpy(d + 2 * p.hidden + kHeadDim, L.n_k, sizeof(float) * kHeadDim, cudaMemcpyDeviceToDevice));
-  }
-  QD_CK(cudaMemcpy(e->c_d_cta_off, e->c_cta_off.data(), sizeof(long long) * grid, cudaMemcpyHostToDevice));
-  QD_CK(cudaMemset(e->c_acc, 0, acc_bytes));
-  QD_CK(cudaMemset(e->c_cnt, 0, cnt_bytes));
-  if (e->opt.timeline) {
-    const size_t tb = (size_t)grid * ctimeline_events(p.layers) * 8;
-    if (cudaMalloc(&e->timeline, tb) != cudaSuccess) throw QdError{QD_E_NOMEM, "cannot allocate the timeline"};
-    QD_CK(cudaMemset(e->timeline, 0, tb));
-    const size_t fb = (size_t)grid * p.layers * kCFine * 8;
-    if (cudaMalloc(&e->c_fine, fb) != cudaSuccess) throw QdError{QD_E_NOMEM, "cannot allocate the timeline"};
-    QD_CK(cudaMemset(e->c_fine, 0, fb));
-  }
-  e->clus = true;
-}
-
-template <int G, typename KVT>
-void launch_cluster_t(qd_engine* e, const CArgs& a, cudaStream_t s) {
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(e->ncl * kCC);
-  cfg.blockDim = dim3(kCT);
-  cfg.dynamicSmemBytes = e->c_smem;
-  cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = kCC;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  QD_CK(cudaLaunchKernelEx(&cfg, k_decode_cluster<G, KVT>, a));
-}
-
-void launch_cluster(qd_engine* e, bool with_head, cudaStream_t s) {
-  const qd_profile& p = e->p;
-  CArgs a{};
-  a.norms = e->c_norms;
-  a.kv = static_cast<char*>(e->kv);
-  a.kv_layer_bytes = (long long)e->opt.max_seq * p.kv_heads * kHeadDim * (e->opt.kv_dtype == QD_KV_F32 ? 4 : 2);
-  a.wblob = static_cast<const char*>(e->cblob);
-  a.layer_bytes = e->c_layer_bytes;
-  a.cta_off = e->c_d_cta_off;
-  a.L = p.layers; a.H = p.hidden; a.I = p.intermediate; a.NH = p.heads; a.NKV = p.kv_heads;
-  a.vocab = p.vocab; a.max_seq = e->opt.max_seq; a.row_stride = e->opt.rope_row_stride; a.ncl = e->ncl;
-  a.eps = p.eps; a.scale = 1.0f / std::sqrt((float)kHeadDim);
-  a.embed = e->embed; a.cos_t = e->cos_t; a.sin_t = e->sin_t; a.final_norm = e->final_norm;
-  a.acc = e->c_acc; a.cnt = e->c_cnt; a.st = e->st;
-  a.tokens = e->tokens; a.out_dev = e->out_dev; a.out_host = e->out_host_dev;
-  a.logits = e->logits; a.hidden = e->h;
-  a.part_v = e->lm_pv; a.part_i = e->lm_pi; a.counter = e->lm_counter;
-  a.with_head = with_head ? 1 : 0;
-  a.slot_bytes = e->c_slot; a.n_slots = e->c_nslots; a.lm_rows = e->c_lmrows;
-  a.timeline = e->timeline;
-  a.fine = e->c_fine;
-  const int G = p.heads / p.kv_heads;
-  if (e->opt.kv_dtype == QD_KV_F32) {
-    if (G == 1) launch_cluster_t<1, float>(e, a, s);
-    else if (G == 2) launch_cluster_t<2, float>(e, a, s);
-    else launch_cluster_t<4, float>(e, a, s);
-  } else {
-    if (G == 1) launch_cluster_t<1, __half>(e, a, s);
-    else if (G == 2) launch_cluster_t<2, __half>(e, a, s);
-    else launch_cluster_t<4, __half>(e, a, s);
-  }
-}
-
 void enqueue_token(qd_engine* e, int head, cudaStream_t s) {
-  if (e->clus) {
-    launch_cluster(e, head != kHeadNone, s);
-    return;
-  }
   if (e->persist) {
     launch_persist(e, head, s);
     return;
@@ -654,140 +565,6 @@ Json parse_manifest(qd_engine* e, const std::string& dir) {
   return m;
 }
 
-// ---- the cluster decode kernel (cluster.cuh) -----------------------------------
-
-template <int G, typename KVT>
-cudaError_t cluster_capacity_t(size_t smem, int* clusters) {
-  cudaError_t rc = cudaFuncSetAttribute(k_decode_cluster<G, KVT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (rc != cudaSuccess) return rc;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(kCC);
-  cfg.blockDim = dim3(kCT);
-  cfg.dynamicSmemBytes = smem;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = kCC;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaOccupancyMaxActiveClusters(clusters, k_decode_cluster<G, KVT>, &cfg);
-}
-
-cudaError_t cluster_capacity(int G, int kv_dtype, size_t smem, int* clusters) {
-  if (kv_dtype == QD_KV_F32) {
-    if (G == 1) return cluster_capacity_t<1, float>(smem, clusters);
-    if (G == 2) return cluster_capacity_t<2, float>(smem, clusters);
-    return cluster_capacity_t<4, float>(smem, clusters);
-  }
-  if (G == 1) return cluster_capacity_t<1, __half>(smem, clusters);
-  if (G == 2) return cluster_capacity_t<2, __half>(smem, clusters);
-  return cluster_capacity_t<4, __half>(smem, clusters);
-}
-
-// Decide whether the cluster kernel serves this shape and device, and its
-// geometry: clusters, ring slots, LM-head rows per chunk, each CTA's slice
-// offset inside a packed layer. Leaves e->ncl = 0 when it does not.
-void plan_cluster(qd_engine* e) {
-  e->ncl = 0;
-  const qd_profile& p = e->p;
-  if (e->opt.persistent != 2) return;
-  const int G = p.heads / p.kv_heads, H = p.hidden, I = p.intermediate, nbI = I / 32;
-  if (!(G == 1 || G == 2 || G == 4) || H % 256 || H > 1024) return;
-  int cl_launch = 0, optin = 0;
-  cudaDeviceGetAttribute(&cl_launch, cudaDevAttrClusterLaunch, e->dev);
-  cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, e->dev);
-  if (!cl_launch) return;
-  int ncl = std::min(e->sms / kCC, nbI);
-  for (int iter = 0; iter < 4; ++iter) {
-    if (ncl < p.kv_heads || ncl <= 0) return;
-    const int grid = ncl * kCC;
-    int chunk_max = 0;
-    std::vector<long long> off(grid);
-    long long total = 0;
-    for (int c = 0; c < grid; ++c) {
-      CGeo g;
-      cgeo(c, ncl, H, I, p.heads, p.kv_heads, g);
-      for (int k = 0; k < 4; ++k) chunk_max = std::max(chunk_max, g.sz[k]);
-      // per-stage row limits of the kernel's buffers (res / exports hold kCT rows)
-      if (g.qkv_rows > kCT || 2 * (g.p_hi - g.p_lo) > kCT || g.o_hi - g.o_lo > kCT || g.p_hi == g.p_lo) return;
-      if ((g.cb_hi - g.cb_lo) * 32 > 1024) return;  // one block per lane in the down stage
-      off[c] = total;
-      total += g.bytes;
-    }
-    const int slot = (std::max(chunk_max, kCW * 2 * H) + 127) / 128 * 128;
-    const int cp_max = (nbI + ncl - 1) / ncl * 32;
-    const size_t fixed = cluster_smem_bytes(H, G, cp_max, 0, 0);
-    const int n_slots = std::min<long long>(kCMaxSlots, ((long long)optin - (long long)fixed) / slot);
-    if (n_slots < 3) return;
-    const size_t smem = cluster_smem_bytes(H, G, cp_max, slot, n_slots);
-    int fit = 0;
-    if (cluster_capacity(G, e->opt.kv_dtype, smem, &fit) != cudaSuccess) {
-      cudaGetLastError();
-      return;
-    }
-    if (fit < ncl) {
-      ncl = fit;
-      continue;
-    }
-    e->ncl = ncl;
-    e->c_slot = slot;
-    e->c_nslots = n_slots;
-    e->c_lmrows = slot / (2 * H) / kCW * kCW;
-    e->c_smem = smem;
-    e->c_layer_bytes = total;
-    e->c_cta_off = off;
-    return;
-  }
-}
-
-// One layer's packed slices for the cluster kernel, from the layer's record
-// matrices (row records of q|k|v, o, gate/up pairs, down).
-void pack_cluster_layer(const qd_engine* e, const std::vector<char>* mats, std::vector<char>& out) {
-  const qd_profile& p = e->p;
-  const int H = p.hidden, I = p.intermediate, QS = p.heads * kHeadDim, KVS = p.kv_heads * kHeadDim;
-  const int G = p.heads / p.kv_heads;
-  const long long rec_h = rec_bytes(H), rec_q = rec_bytes(QS), rec_i = rec_bytes(I);
-  const int nbQ = QS / 32, nbI = I / 32;
-  out.assign((size_t)e->c_layer_bytes, 0);
-  const int grid = e->ncl * kCC;
-  for (int c = 0; c < grid; ++c) {
-    CGeo g;
-    cgeo(c, e->ncl, H, I, p.heads, p.kv_heads, g);
-    char* base = out.data() + e->c_cta_off[c];
-    if (g.attn) {
-      const int kv = g.cl;
-      for (int i = 0; i < g.qkv_rows; ++i) {
-        const int gi = g.r * g.qkv_rows + i;
-        const int row = gi < G * kHeadDim ? kv * G * kHeadDim + gi
-                      : gi < (G + 1) * kHeadDim ? QS + kv * kHeadDim + (gi - G * kHeadDim)
-                                                : QS + KVS + kv * kHeadDim + (gi - (G + 1) * kHeadDim);
-        std::memcpy(base + g.off[0] + (size_t)i * rec_h, mats[0].data() + (size_t)row * rec_h, (size_t)rec_h);
-      }
-      const int nblk = G * kHeadDim / 32, b0 = kv * nblk, rec_o = crec(G * kHeadDim);
-      for (int j = g.o_lo; j < g.o_hi; ++j) {
-        const char* src = mats[1].data() + (size_t)j * rec_q;
-        char* d = base + g.off[1] + (size_t)(j - g.o_lo) * rec_o;
-        std::memcpy(d, src + (size_t)b0 * 16, (size_t)nblk * 16);
-        std::memcpy(d + (size_t)nblk * 16, src + (size_t)nbQ * 16 + (size_t)b0 * 2, (size_t)nblk * 2);
-      }
-    }
-    const int np = g.p_hi - g.p_lo;
-    for (int i = 0; i < np; ++i) {
-      const char* pr = mats[2].data() + (size_t)(g.p_lo + i) * 2 * rec_h;
-      std::memcpy(base + g.off[2] + (size_t)i * rec_h, pr, (size_t)rec_h);
-      std::memcpy(base + g.off[2] + (size_t)(np + i) * rec_h, pr + rec_h, (size_t)rec_h);
-    }
-    const int nblk = g.cb_hi - g.cb_lo, rec_d = crec(nblk * 32);
-    for (int j = g.o_lo; j < g.o_hi; ++j) {
-      const char* src = mats[3].data() + (size_t)j * rec_i;
-      char* d = base + g.off[3] + (size_t)(j - g.o_lo) * rec_d;
-      std::memcpy(d, src + (size_t)g.cb_lo * 16, (size_t)nblk * 16);
-      std::memcpy(d + (size_t)nblk * 16, src + (size_t)nbI * 16 + (size_t)g.cb_lo * 2, (size_t)nblk * 2);
-    }
-  }
-}
-
 void load_engine(qd_engine* e, const std::string& dir, const Json& m) {
   const qd_profile& p = e->p;
   const qd_options& o = e->opt;
@@ -817,14 +594,6 @@ void load_engine(qd_engine* e, const std::string& dir, const Json& m) {
   if (cudaMalloc(&e->blob, ar.off) != cudaSuccess)
     throw QdError{QD_E_NOMEM, "cannot allocate " + std::to_string(ar.off) + " bytes of weights"};
   char* base = static_cast<char*>(e->blob);
-  plan_cluster(e);
-  if (e->ncl) {
-    const size_t cb = (size_t)e->c_layer_bytes * p.layers;
-    if (cudaMalloc(&e->cblob, cb) != cudaSuccess) {
-      cudaGetLastError();
-      e->ncl = 0;  // the other decode paths serve the engine
-    }
-  }
   auto up = [&](size_t off, const void* src, size_t bytes) {
     QD_CK(cudaMemcpy(base + off, src, bytes, cudaMemcpyHostToDevice));
   };
@@ -899,12 +668,6 @@ void load_engine(qd_engine* e, const std::string& dir, const Json& m) {
       }
       const size_t m_off[4] = {lo[l].qkv, lo[l].o, lo[l].gu, lo[l].d};
       for (int k = 0; k < 4; ++k) up(m_off[k], mats[k].data(), m_bytes[k]);
-      if (e->ncl) {
-        std::vector<char> packed;
-        pack_cluster_layer(e, mats, packed);
-        QD_CK(cudaMemcpy(static_cast<char*>(e->cblob) + (size_t)l * e->c_layer_bytes, packed.data(), packed.size(),
-                         cudaMemcpyHostToDevice));
-      }
     }
   } catch (const std::runtime_error& ex) {
     throw QdError{QD_E_IO, ex.what()};
@@ -972,8 +735,7 @@ void load_engine(qd_engine* e, const std::string& dir, const Json& m) {
   if (cudaHostAlloc(reinterpret_cast<void**>(&e->pinned_ids), (size_t)(o.max_seq + 1) * 4, cudaHostAllocDefault) != cudaSuccess ||
       cudaHostAlloc(reinterpret_cast<void**>(&e->pinned_state), sizeof(DevState), cudaHostAllocDefault) != cudaSuccess)
     throw QdError{QD_E_NOMEM, "cannot allocate pinned host memory"};
-  setup_cluster(e);
-  if (!e->clus) setup_persist(e);
+  setup_persist(e);
   QD_CK(cudaEventCreateWithFlags(&e->ev[0], cudaEventDisableTiming));
   QD_CK(cudaEventCreateWithFlags(&e->ev[1], cudaEventDisableTiming));
   if (o.use_graph) {
@@ -1004,12 +766,6 @@ void free_engine(qd_engine* e) {
   if (e->kv) cudaFree(e->kv);
   if (e->scratch) cudaFree(e->scratch);
   if (e->xbuf) cudaFree(e->xbuf);
-  if (e->cblob) cudaFree(e->cblob);
-  if (e->c_d_cta_off) cudaFree(e->c_d_cta_off);
-  if (e->c_norms) cudaFree(e->c_norms);
-  if (e->c_fine) cudaFree(e->c_fine);
-  if (e->c_acc) cudaFree(e->c_acc);
-  if (e->c_cnt) cudaFree(e->c_cnt);
   if (e->d_players) cudaFree(e->d_players);
   if (e->oslices) cudaFree(e->oslices);
   if (e->dslices) cudaFree(e->dslices);
@@ -1054,10 +810,6 @@ void check_state(qd_engine* e) {
     QD_CK(cudaMemsetAsync(e->lm_counter, 0, 4, e->stream));
     if (e->oacc)  // a failed launch may leave partial O / down sums in its parity
       QD_CK(cudaMemsetAsync(e->oacc, 0, (size_t)2 * e->p.layers * 2 * e->p.hidden * 8, e->stream));
-    if (e->clus) {  // a failed launch may leave partial sums and counts in either parity
-      QD_CK(cudaMemsetAsync(e->c_acc, 0, (size_t)2 * e->p.layers * 2 * e->p.hidden * 8, e->stream));
-      QD_CK(cudaMemsetAsync(e->c_cnt, 0, (size_t)2 * e->p.layers * 2 * 32 * 4, e->stream));
-    }
     QD_CK(cudaStreamSynchronize(e->stream));
   }
   if (err & kErrTimeout) throw QdError{QD_E_TIMEOUT, "device: a persistent-kernel wait expired; the launch was abandoned"};
@@ -1333,7 +1085,7 @@ int qd_engine_hidden(qd_engine* e, float* host_hidden) {
   if (!e || !host_hidden) return fail(e, QdError{QD_E_INVALID, "NULL argument"});
   try {
     QD_CK(cudaSetDevice(e->dev));
-    if (e->persist && !e->clus) {  // the persistent kernel leaves it in the exchange words after the last layer
+    if (e->persist) {  // the persistent kernel leaves it in the exchange words after the last layer
       std::vector<unsigned long long> w(e->p.hidden);
       QD_CK(cudaMemcpyAsync(w.data(), e->xbuf + (long long)e->p.layers * e->xstride, w.size() * 8,
                             cudaMemcpyDeviceToHost, e->stream));
@@ -1443,7 +1195,7 @@ int qd_decode_sync(qd_engine* e, int32_t* out_ids, int n) {
 int qd_engine_inject_stall(qd_engine* e) {
   if (!e) return fail(nullptr, QdError{QD_E_INVALID, "engine is NULL"});
   try {
-    if (!e->persist || e->clus) throw QdError{QD_E_INVALID, "the stall hook needs the persistent decode kernel"};
+    if (!e->persist) throw QdError{QD_E_INVALID, "the stall hook needs the persistent decode kernel"};
     QD_CK(cudaSetDevice(e->dev));
     // The next launch tags its words with the device's epoch + 1.
     QD_CK(cudaMemcpyAsync(e->pinned_state, e->st, sizeof(DevState), cudaMemcpyDeviceToHost, e->stream));
@@ -1458,14 +1210,14 @@ int qd_engine_inject_stall(qd_engine* e) {
   return QD_OK;
 }
 
-int qd_engine_uses_persistent(const qd_engine* e) { return e ? (e->clus ? 2 : e->persist ? 1 : 0) : 0; }
+int qd_engine_uses_persistent(const qd_engine* e) { return e ? (e->persist ? 1 : 0) : 0; }
 
 int qd_engine_timeline(qd_engine* e, uint64_t* host_out, int* ctas, int* events_per_cta) {
   if (!e) return fail(nullptr, QdError{QD_E_INVALID, "engine is NULL"});
   try {
     if (!e->timeline) throw QdError{QD_E_INVALID, "timeline not enabled (qd_options.timeline) or no persistent kernel"};
-    const int ev = e->clus ? ctimeline_events(e->p.layers) : timeline_events(e->p.layers);
-    const int nctas = e->clus ? e->ncl * kCC : e->sms;
+    const int ev = timeline_events(e->p.layers);
+    const int nctas = e->sms;
     if (ctas) *ctas = nctas;
     if (events_per_cta) *events_per_cta = ev;
     if (host_out) {
@@ -1479,26 +1231,8 @@ int qd_engine_timeline(qd_engine* e, uint64_t* host_out, int* ctas, int* events_
   return QD_OK;
 }
 
-int qd_engine_timeline_fine(qd_engine* e, uint64_t* host_out, int* ctas, int* events_per_layer) {
-  if (!e) return fail(nullptr, QdError{QD_E_INVALID, "engine is NULL"});
-  try {
-    if (!e->c_fine) throw QdError{QD_E_INVALID, "fine timeline needs the cluster kernel and qd_options.timeline"};
-    const int nctas = e->ncl * kCC;
-    if (ctas) *ctas = nctas;
-    if (events_per_layer) *events_per_layer = kCFine;
-    if (host_out) {
-      QD_CK(cudaSetDevice(e->dev));
-      QD_CK(cudaMemcpyAsync(host_out, e->c_fine, (size_t)nctas * e->p.layers * kCFine * 8, cudaMemcpyDeviceToHost,
-                            e->stream));
-      QD_CK(cudaStreamSynchronize(e->stream));
-    }
-  } catch (const QdError& err) {
-    return fail(e, err);
-  }
-  return QD_OK;
-}
 
-int qd_decode_step_kernels(const qd_engine* e) { return e ? (e->clus || e->persist ? 1 : e->p.layers * 5 + 1) : 0; }
+int qd_decode_step_kernels(const qd_engine* e) { return e ? (e->persist ? 1 : e->p.layers * 5 + 1) : 0; }
 
 // ---- kernel level -------------------------------------------------------------
 

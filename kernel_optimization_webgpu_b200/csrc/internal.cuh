@@ -9,7 +9,6 @@
 
 #include "../../include/qdecode.h"
 #include "common.cuh"
-#include "cluster.cuh"
 #include "persist.cuh"
 
 namespace qd {
@@ -174,17 +173,4 @@ struct qd_engine {
   unsigned long long* oacc = nullptr;      // [2][L][O | down][H] counted fixed-point sums
   int os = 0;                              // attention CTAs per KV head
   long long rec_og = 0, oslice_rows = 0;
-  // cluster decode kernel (cluster.cuh)
-  bool clus = false;
-  int ncl = 0;                       // clusters of kCC CTAs
-  int c_slot = 0, c_nslots = 0, c_lmrows = 0;
-  size_t c_smem = 0;
-  long long c_layer_bytes = 0;
-  std::vector<long long> c_cta_off;  // host copy of each CTA's slice offset inside a layer
-  void* cblob = nullptr;             // packed per-CTA layer slices
-  long long* c_d_cta_off = nullptr;
-  float* c_norms = nullptr;           // [L][input | post | q | k] norm weights
-  unsigned long long* c_fine = nullptr;  // [grid][L][kCFine] SM clock stamps (timeline option)
-  long long* c_acc = nullptr;        // [2][L][2][H] fixed-point sums
-  unsigned* c_cnt = nullptr;         // [2][L][2][32] counters
 };

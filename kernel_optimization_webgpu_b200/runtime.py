@@ -57,8 +57,8 @@ class Engine:
         self._variant = variant.encode()
         opt.variant = self._variant
         opt.use_graph = int(use_graph)
-        # True/1: one persistent kernel per token (one CTA per SM); 2: the cluster kernel;
-        # False/0: one kernel per fused stage.
+        # True/nonzero: one persistent kernel per token (one CTA per SM); False/0: one
+        # kernel per fused stage.
         opt.persistent = int(persistent)
         opt.timeline = int(timeline)
         h = C.c_void_p()
@@ -167,22 +167,13 @@ class Engine:
         check(L.qd_engine_timeline(self._h, out.ctypes.data, None, None), self._h)
         return out
 
-    def timeline_fine(self) -> np.ndarray:
-        """SM clock stamps inside every layer of the last cluster-kernel launch, [ctas][layers][events]."""
-        L = _lib.load()
-        ctas, ev = C.c_int(), C.c_int()
-        check(L.qd_engine_timeline_fine(self._h, None, C.byref(ctas), C.byref(ev)), self._h)
-        out = np.zeros((ctas.value, self.profile["layers"], ev.value), np.uint64)
-        check(L.qd_engine_timeline_fine(self._h, out.ctypes.data, None, None), self._h)
-        return out
-
     @property
     def persistent(self) -> bool:
         return bool(_lib.load().qd_engine_uses_persistent(self._h))
 
     @property
     def token_kernel(self) -> int:
-        """2: the cluster kernel, 1: the single-CTA-ring persistent kernel, 0: one kernel per stage."""
+        """1: the persistent kernel, 0: one kernel per stage."""
         return int(_lib.load().qd_engine_uses_persistent(self._h))
 
     @property

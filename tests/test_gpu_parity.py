@@ -158,8 +158,8 @@ def test_engine_layer_trace_matches_oracle(tiny_runtime, tiny_model, kv):
                 assert rel(got[layer], want[layer]) < TOL, (pos, layer)
 
 
-# persistent: 2 = cluster kernel, 1 = single-CTA-ring kernel, 0 = one kernel per stage
-@pytest.mark.parametrize("use_graph,persistent", [(True, 2), (False, 2), (True, 1), (False, 1), (True, 0), (False, 0)])
+# persistent: 1 = the persistent kernel, 0 = one kernel per stage
+@pytest.mark.parametrize("use_graph,persistent", [(True, 1), (False, 1), (True, 0), (False, 0)])
 def test_engine_greedy_tiny_matches_oracle_f16_kv(tiny_runtime, tiny_model, use_graph, persistent):
     with open(os.path.join(GOLDEN, "tiny_seed2_greedy.json")) as f:
         g = json.load(f)
@@ -176,7 +176,7 @@ def test_engine_greedy_tiny_matches_oracle_f16_kv(tiny_runtime, tiny_model, use_
         assert rel(eng.hidden(), sess.hidden()) < TOL
 
 
-@pytest.mark.parametrize("persistent", [2, 1, 0])
+@pytest.mark.parametrize("persistent", [1, 0])
 def test_engine_greedy_tiny_f32_kv_matches_js_port_golden(tiny_runtime, persistent):
     with open(os.path.join(GOLDEN, "tiny_seed2_greedy.json")) as f:
         g = json.load(f)
@@ -189,10 +189,10 @@ def test_engine_greedy_tiny_f32_kv_matches_js_port_golden(tiny_runtime, persiste
         assert ids == g["generated"]
 
 
-@pytest.mark.parametrize("persistent", [2, 1])
+@pytest.mark.parametrize("persistent", [1, 0])
 def test_engine_long_prompt_matches_oracle(tiny_runtime, tiny_model, persistent):
     """A 300-token prompt: each attention warp walks ~19 cached positions (the K/V
-    prefetch pipeline refills in the loop), the cluster kernel splits them over its 8 CTAs."""
+    prefetch pipeline refills in the loop)."""
     rng = np.random.Generator(np.random.PCG64(8))
     prompt = rng.integers(0, tiny_model.vocab, size=300).tolist()
     with R.Engine(tiny_runtime, max_seq=320, persistent=persistent) as eng:
@@ -240,7 +240,7 @@ def test_reference_api_mirror(tiny_runtime):
     ctx["device"].close()
 
 
-@pytest.mark.parametrize("persistent", [2, 1, 0])
+@pytest.mark.parametrize("persistent", [1, 0])
 def test_engine_qwen_shape_greedy_config2(qwen_runtime, persistent):
     """Config 2: 28 layers, 8 seeded prompt ids, 24 generated tokens, f16 KV."""
     rng = np.random.Generator(np.random.PCG64(2))
