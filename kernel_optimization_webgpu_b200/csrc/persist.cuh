@@ -41,7 +41,7 @@ constexpr unsigned long long kWaitNs = 200ull * 1000 * 1000;  // deadline of any
 constexpr int kErrTimeout = 4;             // DevErr bit: a wait expired (kernel aborted)
 constexpr int kErrOverflow = 16;           // DevErr bit: an O partial beyond the fixed-point range (clamped)
 constexpr int kMaxRes = 256;               // per-CTA row results of one stage (floats)
-constexpr unsigned kPollBackoffNs = 100;   // pause between re-polls of exchange words
+constexpr unsigned kPollBackoffNs = 0;     // pause between re-polls of exchange words (none: measured fastest)
 constexpr int kAttnPf = 2;                 // cached K/V rows each attention warp loads ahead
 
 // Stage timeline (opt-in): per CTA, event 0 = start, then per layer
@@ -239,7 +239,7 @@ __device__ __forceinline__ bool poll_word(const PArgs& a, const unsigned long lo
   for (unsigned it = 0; (unsigned)(v >> 32) != epoch; ++it) {
     if (it == 0) t0 = gtimer();
     else if ((it & 15) == 0 && (aborted(a) || gtimer() - t0 > kWaitNs)) return false;
-    __nanosleep(kPollBackoffNs);
+    if (kPollBackoffNs) __nanosleep(kPollBackoffNs);
     v = ld_word(p);
   }
   out = __uint_as_float((unsigned)v);
@@ -320,7 +320,7 @@ static __device__ __noinline__ bool poll_fx(const PArgs& a, const unsigned long 
     if (!pend) return true;
     if (it == 0) t0 = gtimer();
     else if ((it & 15) == 0 && (aborted(a) || gtimer() - t0 > kWaitNs)) return false;
-    __nanosleep(kPollBackoffNs);
+    if (kPollBackoffNs) __nanosleep(kPollBackoffNs);
 #pragma unroll
     for (int k = 0; k < K; ++k)
       if ((pend >> k) & 1u) v[k] = ld_word(src + threadIdx.x + k * kPT);
@@ -472,7 +472,7 @@ __device__ __forceinline__ bool poll_to_smem(const PArgs& a, const unsigned long
     if (!need) return true;
     if (it == 0) t0 = gtimer();
     else if ((it & 15) == 0 && (aborted(a) || gtimer() - t0 > kWaitNs)) return false;
-    __nanosleep(kPollBackoffNs);
+    if (kPollBackoffNs) __nanosleep(kPollBackoffNs);
 #pragma unroll
     for (int k = 0; k < K; ++k)
       if ((need >> k) & 1u) v[k] = ld_word(src + threadIdx.x + k * kPT);
