@@ -44,7 +44,7 @@ EXPORTS = (
 class QdOptions(C.Structure):
     _fields_ = [("device", C.c_int), ("max_seq", C.c_int), ("kv_dtype", C.c_int),
                 ("rope_row_stride", C.c_int), ("variant", C.c_char_p), ("use_graph", C.c_int),
-                ("persistent", C.c_int), ("timeline", C.c_int)]
+                ("persistent", C.c_int), ("timeline", C.c_int), ("prompt_pass", C.c_int)]
 
 
 class QdProfile(C.Structure):

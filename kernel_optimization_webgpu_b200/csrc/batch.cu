@@ -61,6 +61,10 @@ struct qd_batch {
   uint32_t* shard_pi = nullptr;
   cudaGraphExec_t g_layers = nullptr;   // layers + final norm + copy into the gather buffer
   int shard_steps = 0;                  // merged steps since the last qd_batch_shard_sync
+  // engine prompt pass (B = 1): split-K partials and one graph per prompt length
+  float* pp = nullptr;
+  long long pp_elems = 0;
+  std::vector<std::pair<int, cudaGraphExec_t>> g_prompt;
 };
 
 namespace {
@@ -293,6 +297,8 @@ void drop_graphs(qd_batch* b) {
       cudaGraphExecDestroy(g);
       g = nullptr;
     }
+  for (auto& g : b->g_prompt) cudaGraphExecDestroy(g.second);
+  b->g_prompt.clear();
   if (b->g_layers) {
     cudaGraphExecDestroy(b->g_layers);
     b->g_layers = nullptr;
@@ -326,6 +332,7 @@ void free_batch(qd_batch* b) {
   }
   drop_graphs(b);
   if (b->kv) cudaFree(b->kv);
+  if (b->pp) cudaFree(b->pp);
   if (b->dec) cudaFree(b->dec);
   if (b->logits) cudaFree(b->logits);
   if (b->wide) cudaFree(b->wide);
@@ -490,20 +497,22 @@ void decode(qd_batch* b, int steps, int32_t* out_ids) {
 // Residual (+ one partial) + RMSNorm of `rows` rows into the GEMM operands: one warp
 // per row where the hidden size allows (128 NV columns, NV = 4 or 8), else one CTA
 // per row.
+// `np` split-K partials `stride` floats apart (np = 1 when parts is set and np is 0).
 void rows_norm(qd_batch* b, float* h, const float* parts, const __half* embed, const int* tokens, const float* w,
-               long long rows, cudaStream_t s) {
+               long long rows, cudaStream_t s, int np = 0, long long stride = 0) {
   const Dims d = dims(b->e);
   const unsigned grid = (unsigned)((rows + kNormThreads / 32 - 1) / (kNormThreads / 32));
-  const int np = parts ? 1 : 0;
+  if (!parts) np = 0;
+  else if (np < 1) np = 1;
   if (d.H == 1024)
-    launch_ex(kb_resid_norm_rows<8>, dim3(grid), dim3(kNormThreads), 0, s, h, parts, np, 0LL, embed, tokens, d.V, w,
+    launch_ex(kb_resid_norm_rows<8>, dim3(grid), dim3(kNormThreads), 0, s, h, parts, np, stride, embed, tokens, d.V, w,
               (int)rows, d.eps, b->w_xh, b->w_xl, b->errw);
   else if (d.H == 512)
-    launch_ex(kb_resid_norm_rows<4>, dim3(grid), dim3(kNormThreads), 0, s, h, parts, np, 0LL, embed, tokens, d.V, w,
+    launch_ex(kb_resid_norm_rows<4>, dim3(grid), dim3(kNormThreads), 0, s, h, parts, np, stride, embed, tokens, d.V, w,
               (int)rows, d.eps, b->w_xh, b->w_xl, b->errw);
   else
-    launch_ex(kb_resid_norm, dim3((unsigned)rows), dim3(kNormThreads), 0, s, h, parts, np, 0LL, embed, tokens, d.V, w,
-              d.H, d.eps, b->w_xh, b->w_xl, b->errw);
+    launch_ex(kb_resid_norm, dim3((unsigned)rows), dim3(kNormThreads), 0, s, h, parts, np, stride, embed, tokens, d.V,
+              w, d.H, d.eps, b->w_xh, b->w_xl, b->errw);
 }
 
 // All prompts at once: B * n rows through every layer (GEMMs over the rows,
@@ -567,6 +576,79 @@ void prefill(qd_batch* b, const int32_t* ids, int n, int32_t* first_ids) {
   b->host_pos.assign(B, n);
 }
 
+// ---- engine prompt pass ------------------------------------------------------------
+// The engine's prompt tokens 0..T-1 as T rows of one sequence: per layer the input
+// norm, the QKV GEMM, head norm + RoPE + K/V append, causal prompt attention, the O
+// GEMM, the post-attention norm, gate/up, silu(gate) * up and the down GEMM, with
+// split-K planned for about one CTA per SM (T is small: few row tiles per GEMM). The
+// last layer stops after its K/V append (nothing after it feeds the cache), and the
+// K/V rows are then copied into the engine's cache layout.
+struct PromptPlan {
+  int sq, so, sg, sd, ktq, kto, ktg, ktd;
+  long long parts;  // floats of the largest GEMM's partials
+};
+
+PromptPlan prompt_plan(qd_batch* b, int T) {
+  const Dims d = dims(b->e);
+  const int col_tiles = T <= 128 ? 1 : (T + 255) / 256;
+  auto plan = [&](int n_rows, int K, int* kt) {
+    const int tiles = (n_rows + kTcM - 1) / kTcM * col_tiles;
+    return gemm_plan_splits(K, std::max(1, std::min(kMaxParts, b->e->sms / std::max(1, tiles))), kt);
+  };
+  PromptPlan p{};
+  p.sq = plan(d.R, d.H, &p.ktq);
+  p.so = plan(d.H, d.QS, &p.kto);
+  p.sg = plan(2 * d.I, d.H, &p.ktg);
+  p.sd = plan(d.H, d.I, &p.ktd);
+  p.parts = std::max(std::max((long long)p.sq * d.R, (long long)p.so * d.H),
+                     std::max((long long)p.sg * 2 * d.I, (long long)p.sd * d.H)) *
+            T;
+  return p;
+}
+
+void enqueue_prompt(qd_batch* b, const int* ids, int T, const PromptPlan& pl, cudaStream_t s) {
+  qd_engine* e = b->e;
+  const Dims d = dims(e);
+  const long long sT = T;
+  const float scale = 1.0f / std::sqrt((float)kHeadDim);
+  const long long layer_rows = (long long)d.NKV * b->max_seq;  // one sequence
+  const int qtiles = (T + kPfTile - 1) / kPfTile;
+  const int rope_grid = rope_grid_for(sT * (d.NH + 2 * d.NKV), 4096);
+  const int silu_grid = (int)std::min<long long>((sT * d.I + 255) / 256, 4096);
+  for (int l = 0; l < d.L; ++l) {
+    const LayerDev& L = e->layers[l];
+    if (l == 0)
+      rows_norm(b, b->w_h, nullptr, e->embed, ids, L.n_in, T, s);
+    else
+      rows_norm(b, b->w_h, b->pp, nullptr, nullptr, L.n_in, T, s, pl.sd, sT * d.H);
+    gemm_q4(L.qkv, d.H, d.R, b->w_xh, b->w_xl, T, pl.sq, pl.ktq, b->pp, s, b->errw);
+    launch(kb_rope_cache, dim3(rope_grid), s, (const float*)b->pp, pl.sq, sT * d.R, T, d.NH, d.NKV, L.n_q, L.n_k,
+           d.eps, (const float*)e->cos_t, (const float*)e->sin_t, e->opt.rope_row_stride, (const int*)nullptr, T,
+           0LL, b->max_seq, kc_of(b, l), vc_of(b, l), b->w_q, b->errw);
+    if (l == d.L - 1) break;
+    const long long k_row0 = (long long)l * layer_rows, v_row0 = (long long)(d.L + l) * layer_rows;
+    const dim3 agrid(d.NKV, qtiles, 1);
+    if (d.G == 1) {
+      allow_smem(kb_prefill_attn<1>, pf_smem(1), g_pf_smem_mask);
+      launch_ex(kb_prefill_attn<1>, agrid, dim3(128), pf_smem(1), s, b->kvmap, k_row0, v_row0, (const float*)b->w_q, T,
+                d.NH, d.NKV, b->max_seq, scale, b->w_xh, b->w_xl, b->errw);
+    } else {
+      allow_smem(kb_prefill_attn<2>, pf_smem(2), g_pf_smem_mask2);
+      launch_ex(kb_prefill_attn<2>, agrid, dim3(256), pf_smem(2), s, b->kvmap, k_row0, v_row0, (const float*)b->w_q, T,
+                d.NH, d.NKV, b->max_seq, scale, b->w_xh, b->w_xl, b->errw);
+    }
+    gemm_q4(L.o, d.QS, d.H, b->w_xh, b->w_xl, T, pl.so, pl.kto, b->pp, s, b->errw);
+    rows_norm(b, b->w_h, b->pp, nullptr, nullptr, L.n_post, T, s, pl.so, sT * d.H);
+    gemm_q4(L.gu, d.H, 2 * d.I, b->w_xh, b->w_xl, T, pl.sg, pl.ktg, b->pp, s, b->errw);
+    launch(kb_silu_split, dim3(silu_grid), s, (const float*)b->pp, pl.sg, sT * 2 * d.I, T, d.I, b->w_ah, b->w_al);
+    gemm_q4(L.d, d.I, d.H, b->w_ah, b->w_al, T, pl.sd, pl.ktd, b->pp, s, b->errw);
+  }
+  const long long ekv_layer = (long long)e->opt.max_seq * d.KVS * 2;  // bytes of one layer's K (f16)
+  const long long copies = (long long)d.L * 2 * T * d.NKV * 16;
+  launch(kb_kv_to_engine, dim3((unsigned)std::min<long long>((copies + 255) / 256, 4 * e->sms)), s,
+         (const __half*)b->kv, (long long)b->kv_layer, d.L, d.NKV, b->max_seq, T, static_cast<char*>(e->kv), ekv_layer);
+}
+
 // ---- vocabulary-sharded LM head ------------------------------------------------------
 cudaGraphExec_t capture_layers_to_gather(qd_batch* b) {
   cudaStream_t s = b->e->stream;
@@ -597,6 +679,79 @@ void require_shard(const qd_batch* b) {
 }
 
 }  // namespace
+
+namespace qd {
+
+bool prompt_pass_fits(qd_engine* e, int n) {
+  if (!e->opt.prompt_pass || e->opt.kv_dtype != QD_KV_F16 || e->pbatch_unfit) return false;
+  if (n < kPromptPassMin || n > kPromptPassMax || n > e->opt.max_seq) return false;
+  if (e->pbatch) return true;
+  qd_batch* b = new qd_batch();
+  try {
+    create_batch(e, 1, std::min(kPromptPassMax, e->opt.max_seq), b);
+  } catch (const QdError&) {  // a shape or size the batched path does not take: token by token
+    free_batch(b);
+    e->pbatch_unfit = true;
+    return false;
+  }
+  e->pbatch = b;
+  return true;
+}
+
+void prompt_pass(qd_engine* e, int n) {
+  qd_batch* b = e->pbatch;
+  if (!b || n > b->max_seq) throw QdError{QD_E_INVALID, "prompt pass: no batch for this length"};
+  const PromptPlan pl = prompt_plan(b, n);
+  cudaGraphExec_t x = nullptr;
+  for (auto& g : b->g_prompt)
+    if (g.first == n) x = g.second;
+  if (!x) {
+    // Buffers first (a graph holds their addresses): wide rows for the longest prompt,
+    // partials for this plan.
+    ensure_wide(b, b->max_seq);
+    if (b->pp_elems < pl.parts) {
+      QD_CK(cudaStreamSynchronize(e->stream));
+      for (auto& g : b->g_prompt) cudaGraphExecDestroy(g.second);
+      b->g_prompt.clear();
+      if (b->pp) cudaFree(b->pp);
+      b->pp = nullptr;
+      b->pp_elems = 0;
+      if (cudaMalloc(&b->pp, (size_t)pl.parts * 4) != cudaSuccess)
+        throw QdError{QD_E_NOMEM, "cannot allocate the prompt pass partials"};
+      b->pp_elems = pl.parts;
+    }
+    cudaGraph_t g = nullptr;
+    QD_CK(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal));
+    try {
+      enqueue_prompt(b, e->tokens, n, pl, e->stream);
+    } catch (...) {
+      cudaStreamEndCapture(e->stream, &g);
+      if (g) cudaGraphDestroy(g);
+      throw;
+    }
+    QD_CK(cudaStreamEndCapture(e->stream, &g));
+    const cudaError_t rc = cudaGraphInstantiate(&x, g, 0);
+    cudaGraphDestroy(g);
+    QD_CK(rc);
+    if (b->g_prompt.size() >= 8) {
+      cudaGraphExecDestroy(b->g_prompt.front().second);
+      b->g_prompt.erase(b->g_prompt.begin());
+    }
+    b->g_prompt.emplace_back(n, x);
+  }
+  QD_CK(cudaGraphLaunch(x, e->stream));
+}
+
+void prompt_pass_check(qd_engine* e) {
+  if (e->pbatch) check_err(e->pbatch);
+}
+
+void prompt_pass_free(qd_engine* e) {
+  if (e->pbatch) free_batch(e->pbatch);
+  e->pbatch = nullptr;
+}
+
+}  // namespace qd
 
 extern "C" {
 

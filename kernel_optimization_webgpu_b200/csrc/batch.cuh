@@ -1040,4 +1040,29 @@ __global__ void __launch_bounds__(128 * G) kb_prefill_attn(const __grid_constant
   }
 }
 
+// ---- engine prompt pass: K/V rows into the engine's cache ----------------------------
+// Positions 0..n-1 of sequence 0 of a batch cache (K of every layer, then V; row
+// (g, p) of a layer at (g * max_seq + p) * 128) into an engine cache of f16 rows:
+// layer l's K at ekv + 2l * ekv_layer bytes, its V at (2l + 1) * ekv_layer, row
+// (p, g) at (p * NKV + g) * 256 bytes. One thread per 16 bytes.
+static __global__ void __launch_bounds__(256) kb_kv_to_engine(const __half* kv, long long kv_layer, int L, int NKV,
+                                                            int max_seq, int n, char* ekv, long long ekv_layer) {
+  pdl_wait();
+  const long long total = (long long)L * 2 * n * NKV * 16;
+  for (long long i = (long long)blockIdx.x * 256 + threadIdx.x; i < total; i += (long long)gridDim.x * 256) {
+    const int q = (int)(i & 15);
+    long long r = i >> 4;
+    const int g = (int)(r % NKV);
+    r /= NKV;
+    const int p = (int)(r % n);
+    const int lk = (int)(r / n);  // layer * 2 + (0: K, 1: V)
+    const int l = lk >> 1, kind = lk & 1;
+    const uint4* src = reinterpret_cast<const uint4*>(kv + (long long)(kind * L + l) * kv_layer +
+                                                      ((long long)g * max_seq + p) * kHeadDim) + q;
+    uint4* dst = reinterpret_cast<uint4*>(ekv + (long long)lk * ekv_layer + ((long long)p * NKV + g) * kHeadDim * 2) + q;
+    *dst = *src;
+  }
+  pdl_trigger();
+}
+
 }  // namespace qd

@@ -754,6 +754,7 @@ void free_engine(qd_engine* e) {
   }
   cudaSetDevice(e->dev);
   if (e->stream) cudaStreamSynchronize(e->stream);
+  prompt_pass_free(e);
   if (e->g_layers) cudaGraphExecDestroy(e->g_layers);
   if (e->g_full) cudaGraphExecDestroy(e->g_full);
   if (e->g_argmax) cudaGraphExecDestroy(e->g_argmax);
@@ -796,6 +797,10 @@ void set_state(qd_engine* e, int pos, int max_new) {
 }
 
 void check_state(qd_engine* e) {
+  if (e->pbatch_used) {  // the prompt pass's own status word first
+    e->pbatch_used = false;
+    prompt_pass_check(e);
+  }
   QD_CK(cudaMemcpyAsync(e->pinned_state, e->st, sizeof(DevState), cudaMemcpyDeviceToHost, e->stream));
   QD_CK(cudaStreamSynchronize(e->stream));
   const int err = e->pinned_state->err;
@@ -817,6 +822,15 @@ void check_state(qd_engine* e) {
   if (err & kErrPosition) throw QdError{QD_E_DEVICE, "device: position beyond max_seq"};
   if (err & kErrOverflow)
     throw QdError{QD_E_DEVICE, "device: an attention output projection partial beyond the fixed-point range (2^22)"};
+}
+
+// The first n prompt tokens' K/V in one batched pass where the engine takes it
+// (returns n), else nothing (returns 0: the tokens go through the decode kernel).
+int run_prompt(qd_engine* e, int n) {
+  if (!prompt_pass_fits(e, n)) return 0;
+  prompt_pass(e, n);
+  e->pbatch_used = true;
+  return n;
 }
 
 double ms_since(std::chrono::steady_clock::time_point t0) {
@@ -936,6 +950,7 @@ void qd_options_default(qd_options* opt) {
   opt->use_graph = 1;
   opt->persistent = 1;
   opt->timeline = 0;
+  opt->prompt_pass = 1;
 }
 
 int qd_engine_create(const char* runtime_dir, const qd_options* opt, qd_engine** out) {
@@ -1001,9 +1016,10 @@ int generate(qd_engine* e, const int32_t* input_ids, int n_prompt, int max_new_t
     const auto t0 = std::chrono::steady_clock::now();
     std::memcpy(e->pinned_ids, input_ids, (size_t)n_prompt * 4);
     QD_CK(cudaMemcpyAsync(e->tokens, e->pinned_ids, (size_t)n_prompt * 4, cudaMemcpyHostToDevice, e->stream));
-    set_state(e, 0, max_new_tokens);
     const int n_layers_only = max_new_tokens > 0 ? n_prompt - 1 : n_prompt;
-    for (int i = 0; i < n_layers_only; ++i) run_token(e, kHeadNone);
+    const int first = run_prompt(e, n_layers_only);
+    set_state(e, first, max_new_tokens);
+    for (int i = first; i < n_layers_only; ++i) run_token(e, kHeadNone);
     double first_ms = 0.0;
     int produced = 0;
     bool stop = false;
@@ -1149,9 +1165,10 @@ int qd_decode_begin(qd_engine* e, const int32_t* input_ids, int n_prompt, int ma
     QD_CK(cudaStreamSynchronize(e->stream));  // pinned staging buffers are reused below
     std::memcpy(e->pinned_ids, input_ids, (size_t)n_prompt * 4);
     QD_CK(cudaMemcpyAsync(e->tokens, e->pinned_ids, (size_t)n_prompt * 4, cudaMemcpyHostToDevice, e->stream));
-    set_state(e, 0, max_new_tokens);
+    const int first = run_prompt(e, n_prompt - 1);
+    set_state(e, first, max_new_tokens);
     e->stepping_max_new = max_new_tokens;
-    for (int i = 0; i < n_prompt - 1; ++i) run_token(e, kHeadNone);
+    for (int i = first; i < n_prompt - 1; ++i) run_token(e, kHeadNone);
   } catch (const QdError& err) {
     return fail(e, err);
   }

@@ -108,6 +108,17 @@ void bench_check_state(qd_engine* e);
 void bench_rows_matvec(qd_engine* e, const char* base, long long row_stride, int rows, int k, const float* x,
                        float* y, cudaStream_t s);
 
+// Prompt pass (batch.cu): the first n prompt tokens (e->tokens[0..n)) of the engine's
+// sequence through every layer at once with the batched path's tensor-core GEMMs,
+// leaving their K/V rows at positions 0..n-1 of the engine's cache; no LM head.
+// prompt_pass_fits says whether this engine and length take it (f16 KV, option
+// on, kPromptPassMin <= n <= kPromptPassMax, a shape the batched path supports).
+constexpr int kPromptPassMin = 4, kPromptPassMax = 256;
+bool prompt_pass_fits(qd_engine* e, int n);
+void prompt_pass(qd_engine* e, int n);
+void prompt_pass_check(qd_engine* e);  // raises the pass's device status (synchronises)
+void prompt_pass_free(qd_engine* e);
+
 }  // namespace qd
 
 // Bytes of one q4 row record: nb 16-byte blocks then nb f16 scales, padded to 16.
@@ -173,4 +184,8 @@ struct qd_engine {
   unsigned long long* oacc = nullptr;      // [2][L][O | down][H] counted fixed-point sums
   int os = 0;                              // attention CTAs per KV head
   long long rec_og = 0, oslice_rows = 0;
+  // prompt pass: a one-sequence batch over the engine's weights (created on first use)
+  qd_batch* pbatch = nullptr;
+  bool pbatch_unfit = false;               // the batched path rejected this shape
+  bool pbatch_used = false;                // the current prompt took the pass
 };

@@ -46,7 +46,7 @@ class Engine:
 
     def __init__(self, runtime_dir: str, device: int = 0, max_seq: int = 256, kv_dtype: str = "f16",
                  rope_row_stride: int = 0, variant: str = "optimized", use_graph: bool = True,
-                 persistent: "bool | int" = True, timeline: bool = False):
+                 persistent: "bool | int" = True, timeline: bool = False, prompt_pass: bool = True):
         L = _lib.load()
         opt = QdOptions()
         L.qd_options_default(C.byref(opt))
@@ -61,6 +61,9 @@ class Engine:
         # kernel per fused stage.
         opt.persistent = int(persistent)
         opt.timeline = int(timeline)
+        # True: a prompt's first 4..256 tokens take one batched pass (f16 KV cache);
+        # False: every prompt token goes through the decode kernel.
+        opt.prompt_pass = int(prompt_pass)
         h = C.c_void_p()
         check(L.qd_engine_create(os.fsencode(runtime_dir), C.byref(opt), C.byref(h)))
         self._h = h

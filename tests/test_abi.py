@@ -51,6 +51,7 @@ def test_options_default():
     _lib.load().qd_options_default(C.byref(opt))
     assert opt.max_seq == 256 and opt.kv_dtype == _lib.QD_KV_F16 and opt.use_graph == 1
     assert opt.rope_row_stride == 0 and opt.variant == b"optimized"
+    assert opt.persistent == 1 and opt.timeline == 0 and opt.prompt_pass == 1
 
 
 def _create(runtime_dir, **kw):
