@@ -57,7 +57,7 @@ typedef struct qd_options {
   int persistent;        /* nonzero (default 1): one persistent kernel per token, one CTA per
                             SM, where the shape allows; 0: one kernel per fused stage */
   int timeline;          /* 1: record per-CTA stage timestamps of each persistent launch */
-  int prompt_pass;       /* 1 (default): with an f16 KV cache, a prompt's first 4..256 tokens
+  int prompt_pass;       /* 1 (default): with an f16 KV cache, a prompt's first 5..256 tokens
                             take one batched pass through the layers (tensor-core GEMMs over
                             all of them, causal attention among them) before decoding;
                             0: every prompt token goes through the decode kernel, one at a

@@ -498,13 +498,19 @@ void decode(qd_batch* b, int steps, int32_t* out_ids) {
 // per row where the hidden size allows (128 NV columns, NV = 4 or 8), else one CTA
 // per row.
 // `np` split-K partials `stride` floats apart (np = 1 when parts is set and np is 0).
+// Fewer rows than 4 per SM (a short prompt) take one CTA per row instead: a warp
+// alone would add up to 16 partials of its row one round trip after another
+// (measured 15 us per launch at 7 rows and 16 partials).
 void rows_norm(qd_batch* b, float* h, const float* parts, const __half* embed, const int* tokens, const float* w,
                long long rows, cudaStream_t s, int np = 0, long long stride = 0) {
   const Dims d = dims(b->e);
   const unsigned grid = (unsigned)((rows + kNormThreads / 32 - 1) / (kNormThreads / 32));
   if (!parts) np = 0;
   else if (np < 1) np = 1;
-  if (d.H == 1024)
+  if (rows < 4LL * b->e->sms)
+    launch_ex(kb_resid_norm, dim3((unsigned)rows), dim3(kNormThreads), 0, s, h, parts, np, stride, embed, tokens, d.V,
+              w, d.H, d.eps, b->w_xh, b->w_xl, b->errw);
+  else if (d.H == 1024)
     launch_ex(kb_resid_norm_rows<8>, dim3(grid), dim3(kNormThreads), 0, s, h, parts, np, stride, embed, tokens, d.V, w,
               (int)rows, d.eps, b->w_xh, b->w_xl, b->errw);
   else if (d.H == 512)

@@ -113,7 +113,7 @@ void bench_rows_matvec(qd_engine* e, const char* base, long long row_stride, int
 // leaving their K/V rows at positions 0..n-1 of the engine's cache; no LM head.
 // prompt_pass_fits says whether this engine and length take it (f16 KV, option
 // on, kPromptPassMin <= n <= kPromptPassMax, a shape the batched path supports).
-constexpr int kPromptPassMin = 4, kPromptPassMax = 256;
+constexpr int kPromptPassMin = 5, kPromptPassMax = 256;
 bool prompt_pass_fits(qd_engine* e, int n);
 void prompt_pass(qd_engine* e, int n);
 void prompt_pass_check(qd_engine* e);  // raises the pass's device status (synchronises)

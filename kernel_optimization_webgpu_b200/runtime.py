@@ -61,7 +61,7 @@ class Engine:
         # kernel per fused stage.
         opt.persistent = int(persistent)
         opt.timeline = int(timeline)
-        # True: a prompt's first 4..256 tokens take one batched pass (f16 KV cache);
+        # True: a prompt's first 5..256 tokens take one batched pass (f16 KV cache);
         # False: every prompt token goes through the decode kernel.
         opt.prompt_pass = int(prompt_pass)
         h = C.c_void_p()

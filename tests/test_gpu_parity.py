@@ -399,14 +399,14 @@ def test_engine_rope_row_stride_option(tiny_runtime, tiny_model, persistent):
 
 @pytest.mark.parametrize("persistent", [1, 0])
 def test_prompt_pass_matches_token_by_token_and_oracle(tiny_runtime, tiny_model, persistent):
-    """Prompts of 4..258 tokens with the batched prompt pass on and off: identical
+    """Prompts of 5..258 tokens with the batched prompt pass on and off: identical
     greedy ids, and every step's logits within 1e-4 of the oracle either way. The
-    pass covers a prompt's first 4..256 tokens (the last one always goes through the
-    decode kernel): 4 tokens (3 < 4: no pass), 5 (the shortest pass), 257 (the
+    pass covers a prompt's first 5..256 tokens (the last one always goes through the
+    decode kernel): 5 tokens (4 < 5: no pass), 6 (the shortest pass), 257 (the
     longest) and 258 (too long: token by token); one engine takes every length in
     turn (graphs cached per length, nine lengths evict the oldest)."""
     rng = np.random.Generator(np.random.PCG64(11))
-    lengths = [4, 5, 9, 33, 64, 65, 129, 257, 258, 9, 5]
+    lengths = [5, 6, 9, 33, 64, 65, 129, 257, 258, 9, 6]
     prompts = {n: rng.integers(0, tiny_model.vocab, size=n).tolist() for n in set(lengths)}
     with R.Engine(tiny_runtime, max_seq=320, persistent=persistent) as on, \
             R.Engine(tiny_runtime, max_seq=320, persistent=persistent, prompt_pass=False) as off:
@@ -416,7 +416,7 @@ def test_prompt_pass_matches_token_by_token_and_oracle(tiny_runtime, tiny_model,
             assert got_ids == ref_ids, n
             for g, r in zip(got_logits, ref_logits):
                 assert rel(g, r) < TOL, n
-            if n in (5, 257):
+            if n in (6, 257):
                 want_ids, want_logits, margins = _oracle_step_logits(tiny_model, prompts[n], 4, max_seq=320,
                                                                      kv_f16=True)
                 _check_steps(got_ids, got_logits, want_ids, want_logits, margins)
