@@ -203,7 +203,7 @@ void enqueue_layers(qd_batch* b, cudaStream_t s) {
       launch_ex(kb_resid_norm, dim3(B), dim3(kNormThreads), 0, s, b->h, (const float*)b->parts, b->sd, sB * d.H, (const __half*)nullptr,
              (const int*)nullptr, d.V, L.n_in, d.H, d.eps, b->xh, b->xl, b->errw);
     gemm_q4(L.qkv, d.H, d.R, b->xh, b->xl, B, b->sq, b->ktq, b->parts, s, b->errw);
-    launch(kb_rope_cache, dim3(rope_grid), s, (const float*)b->parts, b->sq, sB * d.R, B, d.NH, d.NKV, L.n_q, L.n_k,
+    launch(kb_rope_cache<true>, dim3(rope_grid), s, (const float*)b->parts, b->sq, sB * d.R, B, d.NH, d.NKV, L.n_q, L.n_k,
            d.eps, (const float*)e->cos_t, (const float*)e->sin_t, e->opt.rope_row_stride, (const int*)b->pos, 1, 0LL,
            b->max_seq, kc_of(b, l), vc_of(b, l), b->q, b->errw);
     launch_attn(b, l, s);  // attention + split combine
@@ -459,7 +459,7 @@ void fill_context(qd_batch* b, int ctx, uint32_t seed) {
       gemm_q4(L.qkv + (size_t)d.QS * rec_bytes(d.H), d.H, 2 * d.KVS, b->w_xh, b->w_xl, R, 1, d.H / kTcK, b->w_y, s,
               b->errw);
       const int grid = rope_grid_for((long long)R * 2 * d.NKV, 8192);
-      launch(kb_rope_cache, dim3(grid), s, (const float*)b->w_y, 1, 0LL, R, 0, d.NKV, L.n_q, L.n_k, d.eps,
+      launch(kb_rope_cache<false>, dim3(grid), s, (const float*)b->w_y, 1, 0LL, R, 0, d.NKV, L.n_q, L.n_k, d.eps,
              (const float*)e->cos_t, (const float*)e->sin_t, e->opt.rope_row_stride, (const int*)nullptr, ctx, r0,
              b->max_seq, kc_of(b, l), vc_of(b, l), (float*)nullptr, b->errw);
     }
@@ -544,7 +544,7 @@ void prefill(qd_batch* b, const int32_t* ids, int n, int32_t* first_ids) {
     else
       rows_norm(b, b->w_h, b->w_y, nullptr, nullptr, L.n_in, T, s);
     gemm_q4(L.qkv, d.H, d.R, b->w_xh, b->w_xl, (int)T, 1, d.H / kTcK, b->w_y, s, b->errw);
-    launch(kb_rope_cache, dim3(rope_grid), s, (const float*)b->w_y, 1, 0LL, (int)T, d.NH, d.NKV, L.n_q, L.n_k, d.eps,
+    launch(kb_rope_cache<false>, dim3(rope_grid), s, (const float*)b->w_y, 1, 0LL, (int)T, d.NH, d.NKV, L.n_q, L.n_k, d.eps,
            (const float*)e->cos_t, (const float*)e->sin_t, e->opt.rope_row_stride, (const int*)nullptr, n, 0LL,
            b->max_seq, kc_of(b, l), vc_of(b, l), b->w_q, b->errw);
     const long long k_row0 = (long long)l * layer_rows, v_row0 = (long long)(d.L + l) * layer_rows;
@@ -628,7 +628,7 @@ void enqueue_prompt(qd_batch* b, const int* ids, int T, const PromptPlan& pl, cu
     else
       rows_norm(b, b->w_h, b->pp, nullptr, nullptr, L.n_in, T, s, pl.sd, sT * d.H);
     gemm_q4(L.qkv, d.H, d.R, b->w_xh, b->w_xl, T, pl.sq, pl.ktq, b->pp, s, b->errw);
-    launch(kb_rope_cache, dim3(rope_grid), s, (const float*)b->pp, pl.sq, sT * d.R, T, d.NH, d.NKV, L.n_q, L.n_k,
+    launch(kb_rope_cache<true>, dim3(rope_grid), s, (const float*)b->pp, pl.sq, sT * d.R, T, d.NH, d.NKV, L.n_q, L.n_k,
            d.eps, (const float*)e->cos_t, (const float*)e->sin_t, e->opt.rope_row_stride, (const int*)nullptr, T,
            0LL, b->max_seq, kc_of(b, l), vc_of(b, l), b->w_q, b->errw);
     if (l == d.L - 1) break;

@@ -267,7 +267,8 @@ static __global__ void __launch_bounds__(kNormThreads) kb_resid_norm_rows(float*
 // its tasks before the first reduction, so that kRopeTasks * 512 bytes of
 // partials per warp are in flight at once.
 constexpr int kRopeTasks = 4;
-static __global__ void __launch_bounds__(256, 3) kb_rope_cache(const float* parts, int nparts, long long part_stride, int R,
+template <bool kSplit>
+static __global__ void __launch_bounds__(256, kSplit ? 2 : 3) kb_rope_cache(const float* parts, int nparts, long long part_stride, int R,
                                                      int q_heads, int NKV, const float* norm_q, const float* norm_k,
                                                      float eps, const float* cos_t, const float* sin_t, int row_stride,
                                                      const int* pos, int rows_per_seq, long long row0, int max_seq,
@@ -288,18 +289,49 @@ static __global__ void __launch_bounds__(256, 3) kb_rope_cache(const float* part
       const int r = task / tasks, t = task - r * tasks;
       x[i] = __ldg(reinterpret_cast<const float4*>(parts + (long long)r * ld + (long long)t * kHeadDim) + lane);
     }
-    for (int s = 1; s < nparts; ++s) {  // split-K partials (decode only: at most a few)
+    // split-K partials, added in split order. kSplit (decode, short prompts: up to 16
+    // splits): four splits' loads in flight at once (split indices clamped, the extra
+    // loads unused; 126 registers, two CTAs per SM). Otherwise (one split, the
+    // prefill's wide launches: three CTAs per SM) one split after another.
+    if constexpr (!kSplit) {
+      for (int s = 1; s < nparts; ++s) {
 #pragma unroll
-      for (int i = 0; i < kRopeTasks; ++i) {
-        const int task = min(t0 + i, nt - 1);
-        const int r = task / tasks, t = task - r * tasks;
-        const float4 y = __ldg(reinterpret_cast<const float4*>(parts + (long long)s * part_stride + (long long)r * ld +
-                                                               (long long)t * kHeadDim) + lane);
-        x[i].x += y.x;
-        x[i].y += y.y;
-        x[i].z += y.z;
-        x[i].w += y.w;
+        for (int i = 0; i < kRopeTasks; ++i) {
+          const int task = min(t0 + i, nt - 1);
+          const int r = task / tasks, t = task - r * tasks;
+          const float4 y = __ldg(reinterpret_cast<const float4*>(parts + (long long)s * part_stride +
+                                                                 (long long)r * ld + (long long)t * kHeadDim) + lane);
+          x[i].x += y.x;
+          x[i].y += y.y;
+          x[i].z += y.z;
+          x[i].w += y.w;
+        }
       }
+    } else {
+     for (int s0 = 1; s0 < nparts; s0 += 4) {
+      float4 y[4][kRopeTasks];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const long long so = (long long)min(s0 + u, nparts - 1) * part_stride;
+#pragma unroll
+        for (int i = 0; i < kRopeTasks; ++i) {
+          const int task = min(t0 + i, nt - 1);
+          const int r = task / tasks, t = task - r * tasks;
+          y[u][i] = __ldg(reinterpret_cast<const float4*>(parts + so + (long long)r * ld + (long long)t * kHeadDim) + lane);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        if (s0 + u < nparts) {
+#pragma unroll
+          for (int i = 0; i < kRopeTasks; ++i) {
+            x[i].x += y[u][i].x;
+            x[i].y += y[u][i].y;
+            x[i].z += y[u][i].z;
+            x[i].w += y[u][i].w;
+          }
+        }
+     }
     }
 #pragma unroll
     for (int i = 0; i < kRopeTasks; ++i) {
