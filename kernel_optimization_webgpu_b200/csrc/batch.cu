@@ -586,7 +586,8 @@ void prefill(qd_batch* b, const int32_t* ids, int n, int32_t* first_ids) {
 // The engine's prompt tokens 0..T-1 as T rows of one sequence: per layer the input
 // norm, the QKV GEMM, head norm + RoPE + K/V append, causal prompt attention, the O
 // GEMM, the post-attention norm, gate/up, silu(gate) * up and the down GEMM, with
-// split-K planned for about one CTA per SM (T is small: few row tiles per GEMM). The
+// split-K planned for about two CTAs per SM (T is small: few row tiles per GEMM; at 7
+// rows two per SM measured 1.587 against 1.610 ms from prompt to first id). The
 // last layer stops after its K/V append (nothing after it feeds the cache), and the
 // K/V rows are then copied into the engine's cache layout.
 struct PromptPlan {
@@ -599,7 +600,7 @@ PromptPlan prompt_plan(qd_batch* b, int T) {
   const int col_tiles = T <= 128 ? 1 : (T + 255) / 256;
   auto plan = [&](int n_rows, int K, int* kt) {
     const int tiles = (n_rows + kTcM - 1) / kTcM * col_tiles;
-    return gemm_plan_splits(K, std::max(1, std::min(kMaxParts, b->e->sms / std::max(1, tiles))), kt);
+    return gemm_plan_splits(K, std::max(1, std::min(kMaxParts, 2 * b->e->sms / std::max(1, tiles))), kt);
   };
   PromptPlan p{};
   p.sq = plan(d.R, d.H, &p.ktq);
@@ -612,7 +613,11 @@ PromptPlan prompt_plan(qd_batch* b, int T) {
   return p;
 }
 
-void enqueue_prompt(qd_batch* b, const int* ids, int T, const PromptPlan& pl, cudaStream_t s) {
+// With first_id set, every layer runs to its end, and the final norm, the LM head on
+// the last row and the argmax merge follow: the id goes to first_id[0] (the engine's
+// token slot after the prompt) and out0[0] (its first output slot).
+void enqueue_prompt(qd_batch* b, const int* ids, int T, const PromptPlan& pl, cudaStream_t s, int* first_id = nullptr,
+                    int* out0 = nullptr) {
   qd_engine* e = b->e;
   const Dims d = dims(e);
   const long long sT = T;
@@ -631,7 +636,7 @@ void enqueue_prompt(qd_batch* b, const int* ids, int T, const PromptPlan& pl, cu
     launch(kb_rope_cache<true>, dim3(rope_grid), s, (const float*)b->pp, pl.sq, sT * d.R, T, d.NH, d.NKV, L.n_q, L.n_k,
            d.eps, (const float*)e->cos_t, (const float*)e->sin_t, e->opt.rope_row_stride, (const int*)nullptr, T,
            0LL, b->max_seq, kc_of(b, l), vc_of(b, l), b->w_q, b->errw);
-    if (l == d.L - 1) break;
+    if (l == d.L - 1 && !first_id) break;
     const long long k_row0 = (long long)l * layer_rows, v_row0 = (long long)(d.L + l) * layer_rows;
     const dim3 agrid(d.NKV, qtiles, 1);
     if (d.G == 1) {
@@ -648,6 +653,14 @@ void enqueue_prompt(qd_batch* b, const int* ids, int T, const PromptPlan& pl, cu
     gemm_q4(L.gu, d.H, 2 * d.I, b->w_xh, b->w_xl, T, pl.sg, pl.ktg, b->pp, s, b->errw);
     launch(kb_silu_split, dim3(silu_grid), s, (const float*)b->pp, pl.sg, sT * 2 * d.I, T, d.I, b->w_ah, b->w_al);
     gemm_q4(L.d, d.I, d.H, b->w_ah, b->w_al, T, pl.sd, pl.ktd, b->pp, s, b->errw);
+  }
+  if (first_id) {
+    rows_norm(b, b->w_h, b->pp, nullptr, nullptr, e->final_norm, T, s, pl.sd, sT * d.H);
+    lm_head(b, b->w_xh + (size_t)(T - 1) * d.H, b->w_xl + (size_t)(T - 1) * d.H, d.H, 1, nullptr, s);
+    QD_CK(cudaMemsetAsync(b->step, 0, 4, s));
+    BatchState st{first_id, b->pos, out0, b->step, 1};
+    launch(kb_argmax_merge, dim3(1), s, (const float*)b->lm_pv, (const uint32_t*)b->lm_pi, b->lm_tiles, 1, st,
+           (uint32_t*)nullptr);
   }
   const long long ekv_layer = (long long)e->opt.max_seq * d.KVS * 2;  // bytes of one layer's K (f16)
   const long long copies = (long long)d.L * 2 * T * d.NKV * 16;
@@ -704,13 +717,14 @@ bool prompt_pass_fits(qd_engine* e, int n) {
   return true;
 }
 
-void prompt_pass(qd_engine* e, int n) {
+void prompt_pass(qd_engine* e, int n, bool with_head) {
   qd_batch* b = e->pbatch;
   if (!b || n > b->max_seq) throw QdError{QD_E_INVALID, "prompt pass: no batch for this length"};
   const PromptPlan pl = prompt_plan(b, n);
+  const int key = 2 * n + (with_head ? 1 : 0);
   cudaGraphExec_t x = nullptr;
   for (auto& g : b->g_prompt)
-    if (g.first == n) x = g.second;
+    if (g.first == key) x = g.second;
   if (!x) {
     // Buffers first (a graph holds their addresses): wide rows for the longest prompt,
     // partials for this plan.
@@ -729,7 +743,8 @@ void prompt_pass(qd_engine* e, int n) {
     cudaGraph_t g = nullptr;
     QD_CK(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal));
     try {
-      enqueue_prompt(b, e->tokens, n, pl, e->stream);
+      if (with_head) enqueue_prompt(b, e->tokens, n, pl, e->stream, e->tokens + n, e->out_host_dev);
+      else enqueue_prompt(b, e->tokens, n, pl, e->stream);
     } catch (...) {
       cudaStreamEndCapture(e->stream, &g);
       if (g) cudaGraphDestroy(g);
@@ -743,7 +758,7 @@ void prompt_pass(qd_engine* e, int n) {
       cudaGraphExecDestroy(b->g_prompt.front().second);
       b->g_prompt.erase(b->g_prompt.begin());
     }
-    b->g_prompt.emplace_back(n, x);
+    b->g_prompt.emplace_back(key, x);
   }
   QD_CK(cudaGraphLaunch(x, e->stream));
 }

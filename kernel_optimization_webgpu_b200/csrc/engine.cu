@@ -787,9 +787,9 @@ int fail(qd_engine* e, const QdError& err) {
   return err.code;
 }
 
-void set_state(qd_engine* e, int pos, int max_new) {
+void set_state(qd_engine* e, int pos, int max_new, int step = 0) {
   e->pinned_state->pos = pos;
-  e->pinned_state->step = 0;
+  e->pinned_state->step = step;
   e->pinned_state->max_new = max_new;
   e->pinned_state->err = 0;
   // pos, step, max_new, err only: epoch and abort belong to the device
@@ -1017,13 +1017,27 @@ int generate(qd_engine* e, const int32_t* input_ids, int n_prompt, int max_new_t
     std::memcpy(e->pinned_ids, input_ids, (size_t)n_prompt * 4);
     QD_CK(cudaMemcpyAsync(e->tokens, e->pinned_ids, (size_t)n_prompt * 4, cudaMemcpyHostToDevice, e->stream));
     const int n_layers_only = max_new_tokens > 0 ? n_prompt - 1 : n_prompt;
-    const int first = run_prompt(e, n_layers_only);
-    set_state(e, first, max_new_tokens);
+    // A greedy generation of two or more ids whose whole prompt fits the batched pass
+    // takes its first id from the pass as well (final norm + LM head on the last
+    // prompt row); the decode kernel then starts at the first generated token. With
+    // one id the decode kernel computes it, so that qd_engine_logits has the final
+    // hidden state it recomputes logits from.
+    int first = 0, step0 = 0;
+    if (!sample && max_new_tokens >= 2 && prompt_pass_fits(e, n_prompt)) {
+      prompt_pass(e, n_prompt, true);
+      e->pbatch_used = true;
+      first = n_prompt;
+      step0 = 1;
+      QD_CK(cudaEventRecord(e->ev[0], e->stream));  // out_host[0] is written
+    } else {
+      first = run_prompt(e, n_layers_only);
+    }
+    set_state(e, first, max_new_tokens, step0);
     for (int i = first; i < n_layers_only; ++i) run_token(e, kHeadNone);
     double first_ms = 0.0;
     int produced = 0;
     bool stop = false;
-    for (int step = 0; step < max_new_tokens && !stop; ++step) {
+    for (int step = step0; step < max_new_tokens && !stop; ++step) {
       run_token(e, sample ? kHeadFull : kHeadArgmax);  // the sampler reads the logits
       if (sample) enqueue_engine_sample(e, *sampling);
       QD_CK(cudaEventRecord(e->ev[step & 1], e->stream));

@@ -114,8 +114,10 @@ void bench_rows_matvec(qd_engine* e, const char* base, long long row_stride, int
 // prompt_pass_fits says whether this engine and length take it (f16 KV, option
 // on, kPromptPassMin <= n <= kPromptPassMax, a shape the batched path supports).
 constexpr int kPromptPassMin = 5, kPromptPassMax = 256;
+// With with_head, the pass also takes the last prompt token through the final norm
+// and the LM head: the first generated id lands in e->tokens[n] and out_host[0].
 bool prompt_pass_fits(qd_engine* e, int n);
-void prompt_pass(qd_engine* e, int n);
+void prompt_pass(qd_engine* e, int n, bool with_head = false);
 void prompt_pass_check(qd_engine* e);  // raises the pass's device status (synchronises)
 void prompt_pass_free(qd_engine* e);
 
