@@ -59,9 +59,12 @@ typedef struct qd_options {
   int timeline;          /* 1: record per-CTA stage timestamps of each persistent launch */
   int prompt_pass;       /* 1 (default): with an f16 KV cache, a prompt's first 5..256 tokens
                             take one batched pass through the layers (tensor-core GEMMs over
-                            all of them, causal attention among them) before decoding;
-                            0: every prompt token goes through the decode kernel, one at a
-                            time, as runCustomQwenGreedyPrompt feeds them */
+                            all of them, causal attention among them) before decoding; a
+                            greedy generation of two or more ids whose whole prompt is
+                            5..256 tokens also takes its first id from that pass (LM head on
+                            the last prompt row); 0: every prompt token goes through the
+                            decode kernel, one at a time, as runCustomQwenGreedyPrompt
+                            feeds them */
 } qd_options;
 
 typedef struct qd_profile {
