@@ -400,13 +400,16 @@ def test_engine_rope_row_stride_option(tiny_runtime, tiny_model, persistent):
 @pytest.mark.parametrize("persistent", [1, 0])
 def test_prompt_pass_matches_token_by_token_and_oracle(tiny_runtime, tiny_model, persistent):
     """Prompts of 5..258 tokens with the batched prompt pass on and off: identical
-    greedy ids, and every step's logits within 1e-4 of the oracle either way. The
-    pass covers a prompt's first 5..256 tokens (the last one always goes through the
-    decode kernel): 5 tokens (4 < 5: no pass), 6 (the shortest pass), 257 (the
-    longest) and 258 (too long: token by token); one engine takes every length in
-    turn (graphs cached per length, nine lengths evict the oldest)."""
+    greedy ids, and every step's logits within 1e-4 of the oracle either way. Through
+    the stepping calls the pass covers a prompt's first 5..256 tokens (the last one
+    goes through the decode kernel): 5 tokens (4 < 5: no pass), 6 (the shortest pass),
+    257 (the longest) and 258 (too long: token by token). qd_generate_greedy with two
+    or more ids also takes a whole prompt of 5..256 tokens and the first id from the
+    pass (5 and 256 are its edges; 257 falls back to the 256-token pass). One engine
+    takes every length in turn (graphs cached per length, nine lengths evict the
+    oldest)."""
     rng = np.random.Generator(np.random.PCG64(11))
-    lengths = [5, 6, 9, 33, 64, 65, 129, 257, 258, 9, 6]
+    lengths = [5, 6, 9, 33, 64, 65, 129, 256, 257, 258, 9, 6]
     prompts = {n: rng.integers(0, tiny_model.vocab, size=n).tolist() for n in set(lengths)}
     with R.Engine(tiny_runtime, max_seq=320, persistent=persistent) as on, \
             R.Engine(tiny_runtime, max_seq=320, persistent=persistent, prompt_pass=False) as off:
@@ -422,6 +425,10 @@ def test_prompt_pass_matches_token_by_token_and_oracle(tiny_runtime, tiny_model,
                 _check_steps(got_ids, got_logits, want_ids, want_logits, margins)
             ids, _ = on.generate_greedy(prompts[n], 4)
             assert ids == ref_ids, n
+            if n in (5, 256):  # two ids (the first from the pass), and one (no head in the pass)
+                assert on.generate_greedy(prompts[n], 2)[0] == ref_ids[:2], n
+                assert on.generate_greedy(prompts[n], 1)[0] == ref_ids[:1], n
+                assert rel(on.logits(), ref_logits[0]) < TOL, n
 
 
 # ---- the argmax-only LM head (int8 coarse pass + exact recompute of candidates) ------
