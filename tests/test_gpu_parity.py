@@ -395,6 +395,20 @@ def test_engine_rope_row_stride_option(tiny_runtime, tiny_model, persistent):
     assert any(rel(a, b) > 1e-3 for a, b in zip(want_logits, default_logits))
 
 
+def test_prompt_pass_rope_row_stride(tiny_runtime, tiny_model):
+    """The batched prompt pass reads the RoPE table with the engine's row stride too:
+    a 12-token prompt at rope_row_stride = 64, pass on and off, against the oracle."""
+    prompt = [11, 4000, 7, 123, 9, 77, 3000, 5, 19, 2048, 1, 400]
+    want_ids, want_logits, margins = _oracle_step_logits(tiny_model, prompt, 6, max_seq=64, kv_f16=True,
+                                                         rope_row_stride=64)
+    for pp in (True, False):
+        with R.Engine(tiny_runtime, max_seq=64, rope_row_stride=64, prompt_pass=pp) as eng:
+            got_ids, got_logits = _engine_step_logits(eng, prompt, 6)
+            ids, _ = eng.generate_greedy(prompt, 6)
+        _check_steps(got_ids, got_logits, want_ids, want_logits, margins)
+        assert ids == want_ids, pp
+
+
 # ---- the batched prompt pass --------------------------------------------------------
 
 @pytest.mark.parametrize("persistent", [1, 0])
