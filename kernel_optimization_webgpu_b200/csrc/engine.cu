@@ -33,7 +33,10 @@ struct StagePlan {
 // Register budget at 2 CTAs per SM (128 per thread): a lane holds KC * 32
 // activations and KC * NR * NW uint4 of weights plus their scales. Combos over
 // the budget are not instantiated (except the single-row one, which every
-// shape needs); rows beyond one wave of warps go to more CTAs instead.
+// shape needs); rows beyond one wave of warps go to more CTAs instead. Rows per
+// warp grow only while the grid still covers every SM (the 1024 -> 3072 gate
+// matvec: 4 rows per warp on 96 CTAs took 3.56 us per isolated launch, 2 rows on
+// 192 CTAs 2.69 us).
 constexpr bool stage_ok(int kc, int nr, int nw) {
   return kc * 32 + kc * nr * nw * 5 < 112 || (nr == 1 && nw == 1);
 }
@@ -45,7 +48,7 @@ StagePlan plan_stage(int rows, int nb, int sms, int nw = 1) {
   const int want = (rows + sms * kWarps - 1) / (sms * kWarps);
   p.nr = 1;
   for (int nr : {2, 4, 8})
-    if (p.nr < want && stage_ok(p.kc, nr, nw)) p.nr = nr;
+    if (p.nr < want && stage_ok(p.kc, nr, nw) && (rows + kWarps * nr - 1) / (kWarps * nr) >= sms) p.nr = nr;
   p.grid = (rows + kWarps * p.nr - 1) / (kWarps * p.nr);
   return p;
 }
