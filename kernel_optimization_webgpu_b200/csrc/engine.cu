@@ -34,9 +34,10 @@ struct StagePlan {
 // activations and KC * NR * NW uint4 of weights plus their scales. Combos over
 // the budget are not instantiated (except the single-row one, which every
 // shape needs); rows beyond one wave of warps go to more CTAs instead. Rows per
-// warp grow only while the grid still covers every SM (the 1024 -> 3072 gate
-// matvec: 4 rows per warp on 96 CTAs took 3.56 us per isolated launch, 2 rows on
-// 192 CTAs 2.69 us).
+// warp grow only while the grid still gives every SM two CTAs (the small
+// instances use 50-60 registers, so four fit per SM): the 1024 -> 3072 gate matvec
+// took 3.56 us per isolated launch at 4 rows per warp on 96 CTAs, 2.69 us at 2 rows
+// on 192 CTAs and 2.47 us at 1 row on 384 CTAs.
 constexpr bool stage_ok(int kc, int nr, int nw) {
   return kc * 32 + kc * nr * nw * 5 < 112 || (nr == 1 && nw == 1);
 }
@@ -48,7 +49,7 @@ StagePlan plan_stage(int rows, int nb, int sms, int nw = 1) {
   const int want = (rows + sms * kWarps - 1) / (sms * kWarps);
   p.nr = 1;
   for (int nr : {2, 4, 8})
-    if (p.nr < want && stage_ok(p.kc, nr, nw) && (rows + kWarps * nr - 1) / (kWarps * nr) >= sms) p.nr = nr;
+    if (p.nr < want && stage_ok(p.kc, nr, nw) && (rows + kWarps * nr - 1) / (kWarps * nr) >= 2 * sms) p.nr = nr;
   p.grid = (rows + kWarps * p.nr - 1) / (kWarps * p.nr);
   return p;
 }
